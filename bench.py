@@ -1,0 +1,299 @@
+"""Benchmark: int8 MoE decode tokens/s on B200 (one process per GPU).
+
+Workload (the batched decode MoE layer): 64
+concurrent sequences per GPU through one MoE FFN layer (hidden 1280, 64
+routed experts of intermediate 896, top-6, + 2 fused shared experts of 896),
+int8 per-row weights, routing drawn with a Zipf(1.1) expert skew.  A step is
+one such layer over one batch of 64 tokens.  Weights come from a ring of
+layers (each > L2) so consecutive steps stream weights from HBM.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints ONE JSON line (rank 0).  ``value`` = tokens/s over all ranks with
+inputs resident in HBM; ``e2e`` = the same through the host-buffer C-ABI call
+(h2d of x/routing, d2h of y inside the timed region); ``roofline`` = the
+expert kernels' algorithmic bytes per step / step time vs measured HBM peak;
+``cpu_baseline`` = the reference's x86 tier restated (oracle/cpu_baseline.c)
+on this host's cores over a bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+HIDDEN, INTER, NEXP, TOPK, SHARED = 1280, 896, 64, 6, 1792
+TOKENS = 64
+L2_BYTES = 126 * 2**20
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def expert_bytes(inter=INTER, hidden=HIDDEN):
+    w = 3 * inter * hidden
+    s = (2 * inter + hidden) * 4
+    return w + s
+
+
+def step_bytes(idx_step, experts_local, tokens=TOKENS):
+    """Algorithmic HBM bytes of one forward step: every routed expert hit
+    (weights + scales, read once), the shared expert, x in, y out, routing."""
+    hit = np.unique(idx_step)
+    hit = hit[np.isin(hit, experts_local)]
+    b = len(hit) * expert_bytes()
+    b += expert_bytes(SHARED)
+    b += tokens * HIDDEN * 4 * 2 + tokens * TOPK * 8
+    return b
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, dev):
+        self.dev = dev
+        self.p = None
+        self.path = Path("/tmp") / f"focr_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if not self.p:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        self.p.wait()
+        self.f.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        self.path.unlink(missing_ok=True)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_init():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    return ws, rank, local
+
+
+def cpu_baseline(seconds=12.0, seed=7):
+    """Restated reference CPU tier on the host cores over a bounded sample:
+    batches of 64 tokens of the same workload until `seconds` elapse."""
+    from franken_ocr_b200 import synth
+    from oracle import oracle as O
+    from oracle.oracle import MoeOracle
+
+    threads = os.cpu_count() or 1
+    W = synth.moe_layer(seed, shared_inter=SHARED)
+    orc = MoeOracle(W)
+    toks = 0
+    t0 = time.perf_counter()
+    i = 0
+    while True:
+        x = synth.hidden_states(seed, TOKENS, idx=1000 + i)
+        idx, w = synth.zipf_routing(seed, TOKENS, idx=1000 + i)
+        orc.cpu_forward(x, idx, w, threads)
+        toks += TOKENS
+        i += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": toks / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{toks} tokens ({i} batches of 64) of the config-2 layer, "
+                      f"{O.cpu_tier()} restatement + threaded decode_mlp_i8 driver, "
+                      f"{threads} threads, {dt:.1f} s"}
+
+
+def run_reference(args, ws, rank):
+    if rank != 0:
+        return
+    from franken_ocr_b200 import synth
+    from oracle import oracle as O
+    from oracle.oracle import MoeOracle
+
+    threads = os.cpu_count() or 1
+    W = synth.moe_layer(7, shared_inter=SHARED)
+    orc = MoeOracle(W)
+    batches = [(synth.hidden_states(7, TOKENS, idx=i), *synth.zipf_routing(7, TOKENS, idx=i))
+               for i in range(args.steps + args.warmup)]
+    for i in range(args.warmup):
+        orc.cpu_forward(*batches[i], threads)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        orc.cpu_forward(*batches[args.warmup + i], threads)
+    dt = time.perf_counter() - t0
+    v = args.steps * TOKENS / dt
+    print(json.dumps({
+        "impl": "reference", "metric": "int8 MoE decode tokens/s (config 2: M=64 batched decode layer)",
+        "value": v, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8 (i32 accumulate, f32 dequant)", "data": "synthetic",
+        "config": {"workload": "config2_moe_layer_m64_zipf_shared", "tokens_per_step": TOKENS,
+                   "hidden": HIDDEN, "inter": INTER, "experts": NEXP, "topk": TOPK,
+                   "shared_inter": SHARED},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} steps x 64 tokens, {O.cpu_tier()} restatement"},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_ours(args, ws, rank, local):
+    import torch
+
+    from franken_ocr_b200 import synth
+    from franken_ocr_b200.moe import MoeLayer
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        raise SystemExit("multi-GPU expert-parallel bench not built yet")
+    hbm_peak, peak_kind = peaks()
+    # ring of layers so that consecutive steps stream from HBM
+    R = 2
+    layers = [MoeLayer(synth.moe_layer(100 + r, shared_inter=SHARED), max_tokens=TOKENS)
+              for r in range(R)]
+    n = args.steps + args.warmup
+    xs = [synth.hidden_states(7, TOKENS, idx=i) for i in range(n)]
+    rts = [synth.zipf_routing(7, TOKENS, idx=i) for i in range(n)]
+    xd = [torch.from_numpy(x).to(dev) for x in xs]
+    idd = [torch.from_numpy(r[0]).to(dev) for r in rts]
+    wd = [torch.from_numpy(r[1]).to(dev) for r in rts]
+    y = torch.empty((TOKENS, HIDDEN), dtype=torch.float32, device=dev)
+    experts_local = np.arange(NEXP)
+
+    def step(i):
+        layers[i % R].forward(xd[i], idd[i], wd[i], y)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.3)
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(st)
+    for i in range(args.warmup, n):
+        step(i)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    ms_step = ms / args.steps
+    value = args.steps * TOKENS * ws / (ms / 1e3)
+    bytes_per_step = float(np.mean([step_bytes(rts[i][0], experts_local) for i in range(args.warmup, n)]))
+    achieved = bytes_per_step / (ms_step / 1e3) / 1e9
+
+    # e2e: same steps through the host-buffer C-ABI call (pinned host memory)
+    xh = [torch.from_numpy(x).pin_memory().numpy() for x in xs]
+    ih = [torch.from_numpy(r[0]).pin_memory().numpy() for r in rts]
+    wh = [torch.from_numpy(r[1]).pin_memory().numpy() for r in rts]
+    yh = torch.empty((TOKENS, HIDDEN), dtype=torch.float32).pin_memory().numpy()
+    for i in range(args.warmup):
+        layers[i % R].forward(xh[i], ih[i], wh[i], yh)
+    ds = torch.cuda.default_stream()
+    torch.cuda.synchronize()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(ds)
+    for i in range(args.warmup, n):
+        layers[i % R].forward(xh[i], ih[i], wh[i], yh)
+    e3.record(ds)
+    torch.cuda.synchronize()
+    e2e_ms = e2.elapsed_time(e3)
+    h2d = TOKENS * HIDDEN * 4 + TOKENS * TOPK * 8
+    d2h = TOKENS * HIDDEN * 4
+
+    cpu = cpu_baseline() if rank == 0 and not args.no_cpu else None
+    launches_per_step = 8
+    line = {
+        "metric": "int8 MoE decode tokens/s (config 2: M=64 batched decode layer)",
+        "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8 (i32 accumulate, f32 dequant)",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) hidden, Zipf(1.1) routing)",
+        "config": {"workload": "config2_moe_layer_m64_zipf_shared", "tokens_per_step": TOKENS,
+                   "hidden": HIDDEN, "inter": INTER, "experts": NEXP, "topk": TOPK,
+                   "shared_inter": SHARED, "parallelism": "single GPU" if ws == 1 else f"ep{ws}",
+                   "l2": f"ring of {R} layers of {expert_bytes() * NEXP / 1e6:.0f} MB each (> L2)"},
+        "roofline": {"bound": "hbm", "kernel": "moe_forward step (all expert kernels)",
+                     "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": achieved / hbm_peak, "peak_kind": peak_kind, "traffic": None,
+                     "algorithmic_bytes_per_step": bytes_per_step},
+        "e2e": {"value": args.steps * TOKENS * ws / (e2e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clk,
+    }
+    if cpu:
+        line["cpu_baseline"] = cpu
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    args = ap.parse_args()
+    ws, rank, local = dist_init()
+    if args.impl == "reference":
+        run_reference(args, ws, rank)
+    else:
+        run_ours(args, ws, rank, local)
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

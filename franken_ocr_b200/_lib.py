@@ -1,0 +1,93 @@
+"""ctypes binding of ``libfocr_cuda.so`` (the C ABI in ``include/focr_cuda.h``).
+
+The library is the product: there is no CPU fallback.  If the shared object is
+missing, importing this module raises immediately.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "libfocr_cuda.so"
+
+FOCR_OK = 0
+FOCR_E_SHAPE = -1
+FOCR_E_ARG = -2
+FOCR_E_CUDA = -3
+FOCR_E_ALLOC = -4
+FOCR_E_ROUTE = -5
+FOCR_E_TIMEOUT = -6
+FOCR_E_UNSUPPORTED = -7
+MEM_HOST = 0
+MEM_DEVICE = 1
+
+# Every symbol declared in include/focr_cuda.h.
+EXPORTS = [
+    "focr_last_error", "focr_tier_string", "focr_igemm_s8s8", "focr_igemm_u8s8",
+    "focr_igemm_s4s8_packed", "focr_quantize_rows_i8", "focr_gemv_i8",
+    "focr_moe_create", "focr_moe_destroy", "focr_moe_route", "focr_moe_forward",
+    "focr_moe_decode", "focr_lmhead_create", "focr_lmhead_destroy", "focr_lmhead_top1",
+    "focr_top1_combine", "focr_selftest",
+]
+
+
+class FocrError(RuntimeError):
+    """A non-zero status from the C ABI; ``.code`` is the FOCR_E_* value."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(msg)
+        self.code = code
+
+
+if not LIB_PATH.exists():
+    raise ImportError(
+        f"{LIB_PATH} is missing: build it with `python franken_ocr_b200/build.py` "
+        "(the CUDA library is required; there is no CPU fallback)")
+
+lib = C.CDLL(str(LIB_PATH))
+
+vp = C.c_void_p
+sz = C.c_size_t
+i32 = C.c_int
+
+
+class MoeConfig(C.Structure):
+    _fields_ = [
+        ("hidden", C.c_uint32), ("inter", C.c_uint32), ("n_experts", C.c_uint32),
+        ("topk", C.c_uint32), ("shared_inter", C.c_uint32), ("norm_topk_prob", C.c_int32),
+        ("routed_scaling_factor", C.c_float), ("group", C.c_uint32),
+        ("expert_begin", C.c_uint32), ("expert_count", C.c_uint32),
+        ("max_tokens", C.c_uint32),
+    ]
+
+
+class MoeWeights(C.Structure):
+    _fields_ = [(n, vp) for n in (
+        "router", "gate_w", "gate_s", "up_w", "up_s", "down_w", "down_s",
+        "gate_p", "gate_gs", "up_p", "up_gs", "down_p", "down_gs",
+        "sh_gate_w", "sh_gate_s", "sh_up_w", "sh_up_s", "sh_down_w", "sh_down_s")]
+
+
+lib.focr_last_error.restype = C.c_char_p
+lib.focr_tier_string.restype = C.c_char_p
+for _name in ("focr_igemm_s8s8", "focr_igemm_u8s8"):
+    getattr(lib, _name).argtypes = [vp, sz, vp, sz, sz, sz, sz, vp, sz, i32, vp]
+lib.focr_igemm_s4s8_packed.argtypes = [vp, sz, vp, sz, vp, sz, sz, sz, sz, sz, vp, sz, i32, vp]
+lib.focr_quantize_rows_i8.argtypes = [vp, sz, sz, i32, vp, vp, i32, vp]
+lib.focr_gemv_i8.argtypes = [vp, sz, sz, vp, vp, sz, vp, i32, vp]
+lib.focr_moe_create.argtypes = [C.POINTER(MoeConfig), C.POINTER(MoeWeights), C.POINTER(vp)]
+lib.focr_moe_destroy.argtypes = [vp]
+lib.focr_moe_route.argtypes = [vp, vp, sz, vp, vp, i32, vp]
+lib.focr_moe_forward.argtypes = [vp, vp, sz, vp, vp, vp, i32, vp]
+lib.focr_moe_decode.argtypes = [vp, vp, sz, vp, vp, vp, i32, vp]
+lib.focr_lmhead_create.argtypes = [vp, vp, sz, sz, sz, sz, C.POINTER(vp)]
+lib.focr_lmhead_destroy.argtypes = [vp]
+lib.focr_lmhead_top1.argtypes = [vp, vp, sz, vp, vp, vp, i32, vp]
+lib.focr_top1_combine.argtypes = [vp, vp, sz, sz, vp]
+lib.focr_selftest.argtypes = [C.c_char_p, sz, C.POINTER(i32)]
+
+
+def check(rc: int) -> None:
+    if rc != FOCR_OK:
+        raise FocrError(rc, lib.focr_last_error().decode(errors="replace"))

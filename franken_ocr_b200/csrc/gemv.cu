@@ -1,0 +1,221 @@
+// Decode-shaped GEMV kernels + launchers (see gemv.cuh).
+#include "gemv.cuh"
+
+namespace focr {
+
+__global__ void quantize_rows_kernel(const float *__restrict__ x, int K, int te,
+                                     int8_t *__restrict__ xq, float *__restrict__ scales) {
+    __shared__ float red[32];
+    __shared__ float s_inv;
+    const float *row = x + (size_t)blockIdx.x * K;
+    int8_t *q = xq + (size_t)blockIdx.x * K;
+    float m = 0.0f;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) m = fmaxf(m, fabsf(row[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float a = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) a = fmaxf(a, red[w]);
+        const float sc = a > 0.0f ? __fdiv_rn(a, 127.0f) : 1.0f;
+        scales[blockIdx.x] = sc;
+        s_inv = __fdiv_rn(1.0f, sc);
+    }
+    __syncthreads();
+    const float inv = s_inv;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) q[i] = (int8_t)quant_i8(row[i], inv, te != 0);
+}
+
+__global__ void __launch_bounds__(GEMV_THREADS)
+gemv_s4_kernel(const int8_t *__restrict__ A, const uint8_t *__restrict__ Bp,
+               const float *__restrict__ scales, int group, int M, int K, int N,
+               float *__restrict__ out, const float *__restrict__ dequant_a) {
+    extern __shared__ int4 sAraw[];
+    int8_t *sA = reinterpret_cast<int8_t *>(sAraw);
+    for (int i = threadIdx.x; i < M * K; i += blockDim.x) sA[i] = A[i];
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const int warp = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int nwarps = gridDim.x * (blockDim.x >> 5);
+    const int G = K / group;
+    const int words_per_group = group / 8;  // 8 nibbles per 32-bit word
+    const int Kb = K / 2;
+    for (int n = warp; n < N; n += nwarps) {
+        const uint32_t *row = reinterpret_cast<const uint32_t *>(Bp + (size_t)n * Kb);
+        const float *srow = scales + (size_t)n * G;
+        float accf[8];
+#pragma unroll
+        for (int m = 0; m < 8; m++) accf[m] = 0.0f;
+        for (int g0 = 0; g0 < G; g0 += 32) {
+            const int g = g0 + lane;
+            int dot[8];
+#pragma unroll
+            for (int m = 0; m < 8; m++) dot[m] = 0;
+            float s = 0.0f;
+            if (g < G) {
+                s = srow[g];
+                for (int wi = 0; wi < words_per_group; wi++) {
+                    const uint32_t w = __ldg(row + g * words_per_group + wi);
+                    int lo, hi;
+                    unpack8_s4(w, lo, hi);
+                    const int kbase = g * group + wi * 8;
+#pragma unroll
+                    for (int m = 0; m < 8; m++) {
+                        if (m < M) {
+                            const int a0 = *reinterpret_cast<const int *>(sA + m * K + kbase);
+                            const int a1 = *reinterpret_cast<const int *>(sA + m * K + kbase + 4);
+                            dot[m] = dp4a_ss(a0, lo, dot[m]);
+                            dot[m] = dp4a_ss(a1, hi, dot[m]);
+                        }
+                    }
+                }
+            }
+            const int cnt = min(32, G - g0);
+#pragma unroll
+            for (int m = 0; m < 8; m++) {
+                if (m < M) {
+                    const float t = __fmul_rn(s, (float)dot[m]);
+                    float a = accf[m];
+                    for (int l = 0; l < cnt; l++) a = __fadd_rn(a, __shfl_sync(0xffffffffu, t, l));
+                    accf[m] = a;
+                }
+            }
+        }
+        if (lane == 0) {
+#pragma unroll
+            for (int m = 0; m < 8; m++)
+                if (m < M)
+                    out[(size_t)m * N + n] =
+                        dequant_a ? __fmul_rn(accf[m], dequant_a[m]) : accf[m];
+        }
+    }
+}
+
+static int gemv_grid(size_t rows, int rows_per_block) {
+    size_t blocks = (rows + rows_per_block - 1) / rows_per_block;
+    size_t cap = (size_t)num_sms() * 8;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    return (int)blocks;
+}
+
+template <int MT, bool AU8, int EPI>
+static void launch_rows(const int8_t *A, const int8_t *B, int M, int K, int N, int32_t *out,
+                        float *y, const float *as, const float *ws, bool fast, cudaStream_t st) {
+    const int warps = GEMV_THREADS / 32;
+    if (fast) {
+        size_t smem = (size_t)M * K;
+        gemv16_kernel<MT, AU8, EPI><<<gemv_grid(N, warps * 2), GEMV_THREADS, smem, st>>>(
+            A, B, M, K, N, out, y, as, ws);
+    } else {
+        size_t smem = ((size_t)M * K + 15) / 16 * 16;
+        gemv_any_kernel<MT, AU8, EPI><<<gemv_grid(N, warps), GEMV_THREADS, smem, st>>>(
+            A, B, M, K, N, out, y, as, ws);
+    }
+}
+
+template <bool AU8, int EPI>
+static int launch_chunk(const int8_t *A, const int8_t *B, int M, int K, int N, int32_t *out,
+                        float *y, const float *as, const float *ws, cudaStream_t st) {
+    const bool fast = (K % 16 == 0) && ((uintptr_t)A % 16 == 0) && ((uintptr_t)B % 16 == 0);
+    size_t smem = (size_t)M * K;
+    static bool attr_done[2][2][4] = {};
+    if (smem > 48 * 1024) {
+        // opt-in to large dynamic shared memory once per instantiation
+        int mi = M <= 1 ? 0 : M <= 2 ? 1 : M <= 4 ? 2 : 3;
+        if (!attr_done[fast][EPI][mi]) {
+#define FOCR_SET_ATTR(MT)                                                                   \
+    do {                                                                                    \
+        cudaFuncSetAttribute(gemv16_kernel<MT, AU8, EPI>,                                   \
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);      \
+        cudaFuncSetAttribute(gemv_any_kernel<MT, AU8, EPI>,                                 \
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);      \
+    } while (0)
+            if (mi == 0) FOCR_SET_ATTR(1);
+            else if (mi == 1) FOCR_SET_ATTR(2);
+            else if (mi == 2) FOCR_SET_ATTR(4);
+            else FOCR_SET_ATTR(8);
+#undef FOCR_SET_ATTR
+            attr_done[fast][EPI][mi] = true;
+        }
+        if (smem > 200 * 1024) return fail(FOCR_E_UNSUPPORTED, "gemv: M*K too large for shared memory");
+    }
+    if (M <= 1) launch_rows<1, AU8, EPI>(A, B, M, K, N, out, y, as, ws, fast, st);
+    else if (M <= 2) launch_rows<2, AU8, EPI>(A, B, M, K, N, out, y, as, ws, fast, st);
+    else if (M <= 4) launch_rows<4, AU8, EPI>(A, B, M, K, N, out, y, as, ws, fast, st);
+    else launch_rows<8, AU8, EPI>(A, B, M, K, N, out, y, as, ws, fast, st);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    return FOCR_OK;
+}
+
+int launch_tc_igemm(const void *A, bool au8, const int8_t *B, size_t M, size_t K, size_t N,
+                    int32_t *out, cudaStream_t st);
+bool tc_igemm_eligible(const void *A, const int8_t *B, size_t M, size_t K, size_t N,
+                       const int32_t *out);
+
+int launch_igemm(const void *A, bool au8, const int8_t *B, size_t M, size_t K, size_t N,
+                 int32_t *out, cudaStream_t st) {
+    if (M == 0 || N == 0) return FOCR_OK;
+    if (K == 0) return FOCR_OK;  // every dot is empty: out += 0
+    if (tc_igemm_eligible(A, B, M, K, N, out)) return launch_tc_igemm(A, au8, B, M, K, N, out, st);
+    if (K > (size_t)INT32_MAX || N > (size_t)INT32_MAX)
+        return fail(FOCR_E_UNSUPPORTED, "igemm: dimension exceeds int32 range");
+    for (size_t m0 = 0; m0 < M; m0 += 8) {
+        const int mc = (int)((M - m0) < 8 ? (M - m0) : 8);
+        const int8_t *Ac = reinterpret_cast<const int8_t *>(A) + m0 * K;
+        int32_t *oc = out + m0 * N;
+        int rc = au8 ? launch_chunk<true, EPI_ADD_I32>(Ac, B, mc, (int)K, (int)N, oc, nullptr,
+                                                       nullptr, nullptr, st)
+                     : launch_chunk<false, EPI_ADD_I32>(Ac, B, mc, (int)K, (int)N, oc, nullptr,
+                                                        nullptr, nullptr, st);
+        if (rc) return rc;
+    }
+    return FOCR_OK;
+}
+
+int launch_gemv_dequant(const int8_t *xq, const float *a_scale, const int8_t *B,
+                        const float *w_scale, size_t M, size_t K, size_t N, float *y,
+                        cudaStream_t st) {
+    if (M == 0 || N == 0) return FOCR_OK;
+    for (size_t m0 = 0; m0 < M; m0 += 8) {
+        const int mc = (int)((M - m0) < 8 ? (M - m0) : 8);
+        int rc = launch_chunk<false, EPI_DEQUANT_F32>(xq + m0 * K, B, mc, (int)K, (int)N,
+                                                      nullptr, y + m0 * N, a_scale + m0,
+                                                      w_scale, st);
+        if (rc) return rc;
+    }
+    return FOCR_OK;
+}
+
+int launch_quantize_rows(const float *x, size_t M, size_t K, bool te, int8_t *xq,
+                         float *scales, cudaStream_t st) {
+    if (M == 0) return FOCR_OK;
+    quantize_rows_kernel<<<(unsigned)M, 256, 0, st>>>(x, (int)K, te ? 1 : 0, xq, scales);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    return FOCR_OK;
+}
+
+int launch_gemv_s4(const int8_t *A, const uint8_t *Bp, const float *scales, size_t group,
+                   size_t M, size_t K, size_t N, float *out, const float *dequant_a,
+                   cudaStream_t st) {
+    if (M == 0 || N == 0) return FOCR_OK;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(gemv_s4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             200 * 1024);
+        attr = true;
+    }
+    for (size_t m0 = 0; m0 < M; m0 += 8) {
+        const int mc = (int)((M - m0) < 8 ? (M - m0) : 8);
+        size_t smem = ((size_t)mc * K + 15) / 16 * 16;
+        if (smem > 200 * 1024) return fail(FOCR_E_UNSUPPORTED, "gemv_s4: M*K too large");
+        gemv_s4_kernel<<<gemv_grid(N, GEMV_THREADS / 32), GEMV_THREADS, smem, st>>>(
+            A + m0 * K, Bp, scales, (int)group, mc, (int)K, (int)N, out + m0 * N,
+            dequant_a ? dequant_a + m0 : nullptr);
+        FOCR_CUDA_TRY(cudaGetLastError());
+    }
+    return FOCR_OK;
+}
+
+}  // namespace focr

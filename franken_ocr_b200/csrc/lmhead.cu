@@ -1,0 +1,166 @@
+// Vocab-sharded int8 lm-head: gemv_i8 over a contiguous shard of the
+// [vocab, hidden] head (decoder.rs:2275-2296; tiles :1851-1927) followed by a
+// first-maximum top-1 (sampler.rs:168-186 argmax_row).  Every logit is an
+// independent dot, so any contiguous tiling is byte-identical to the
+// monolithic head; the cross-shard combine keeps the lowest index on ties.
+#include <cmath>
+
+#include "gemv.cuh"
+
+struct focr_lmhead {
+    int8_t *w = nullptr;
+    float *scales = nullptr;
+    size_t rows = 0, hidden = 0, row_begin = 0, max_tokens = 0;
+    float *x = nullptr;        // [T][hidden] staging
+    int8_t *xq = nullptr;      // [T][hidden]
+    float *xs = nullptr;       // [T]
+    float *logits = nullptr;   // [T][rows]
+    float *bv = nullptr;       // [T]
+    int32_t *bi = nullptr;     // [T]
+};
+
+namespace focr {
+
+// First maximum of one row (NaN skipped); -1 / NaN when the row is all-NaN.
+__global__ void argmax_rows_kernel(const float *__restrict__ logits, int n, int offset,
+                                   float *__restrict__ best_v, int32_t *__restrict__ best_i) {
+    const float *row = logits + (size_t)blockIdx.x * n;
+    int bi = -1;
+    float bv = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = row[i];
+        if (v != v) continue;
+        if (bi >= 0 && v <= bv) continue;
+        bi = i;
+        bv = v;
+    }
+    __shared__ float sv[32];
+    __shared__ int si[32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) {
+            bi = oi;
+            bv = ov;
+        }
+    }
+    if ((threadIdx.x & 31) == 0) {
+        sv[threadIdx.x >> 5] = bv;
+        si[threadIdx.x >> 5] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int b = -1;
+        float v = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) {
+            const int oi = si[w];
+            const float ov = sv[w];
+            if (oi >= 0 && (b < 0 || ov > v || (ov == v && oi < b))) {
+                b = oi;
+                v = ov;
+            }
+        }
+        best_i[blockIdx.x] = b < 0 ? -1 : b + offset;
+        best_v[blockIdx.x] = b < 0 ? NAN : v;
+    }
+}
+
+}  // namespace focr
+
+using namespace focr;
+
+extern "C" {
+
+int focr_lmhead_destroy(focr_lmhead *h) {
+    if (!h) return FOCR_OK;
+    void *ptrs[] = {h->w, h->scales, h->x, h->xq, h->xs, h->logits, h->bv, h->bi};
+    for (void *p : ptrs)
+        if (p) cudaFree(p);
+    delete h;
+    return FOCR_OK;
+}
+
+int focr_lmhead_create(const int8_t *w, const float *scales, size_t rows, size_t hidden,
+                       size_t row_begin, size_t max_tokens, focr_lmhead **out) {
+    if (!w || !scales || !out) return fail(FOCR_E_ARG, "lmhead_create: null argument");
+    if (!rows || !hidden || !max_tokens) return fail(FOCR_E_ARG, "lmhead_create: empty shape");
+    if (rows > (size_t)INT32_MAX || row_begin + rows > (size_t)INT32_MAX)
+        return fail(FOCR_E_UNSUPPORTED, "lmhead_create: vocab exceeds int32");
+    focr_lmhead *h = new focr_lmhead();
+    h->rows = rows;
+    h->hidden = hidden;
+    h->row_begin = row_begin;
+    h->max_tokens = max_tokens;
+    cudaError_t e = cudaSuccess;
+#define A(p, n)                                       \
+    if (e == cudaSuccess) e = cudaMalloc((void **)&p, (n));
+    A(h->w, rows * hidden);
+    A(h->scales, rows * 4);
+    A(h->x, max_tokens * hidden * 4);
+    A(h->xq, max_tokens * hidden);
+    A(h->xs, max_tokens * 4);
+    A(h->logits, max_tokens * rows * 4);
+    A(h->bv, max_tokens * 4);
+    A(h->bi, max_tokens * 4);
+#undef A
+    if (e == cudaSuccess) e = cudaMemcpy(h->w, w, rows * hidden, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(h->scales, scales, rows * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        focr_lmhead_destroy(h);
+        return cuda_fail(e, "lmhead_create");
+    }
+    *out = h;
+    return FOCR_OK;
+}
+
+int focr_lmhead_top1(focr_lmhead *h, const float *x, size_t m, float *best_val,
+                     int32_t *best_idx, float *logits, int mem, void *stream) {
+    if (!h) return fail(FOCR_E_ARG, "lmhead_top1: null handle");
+    if (m == 0) return FOCR_OK;
+    if (m > h->max_tokens) return fail(FOCR_E_SHAPE, "lmhead_top1: m > max_tokens");
+    cudaStream_t st = (cudaStream_t)stream;
+    const float *dx = x;
+    if (mem == FOCR_MEM_HOST) {
+        FOCR_CUDA_TRY(cudaMemcpyAsync(h->x, x, m * h->hidden * 4, cudaMemcpyHostToDevice, st));
+        dx = h->x;
+    }
+    float *dlog = (mem == FOCR_MEM_DEVICE && logits) ? logits : h->logits;
+    int rc = launch_quantize_rows(dx, m, h->hidden, false, h->xq, h->xs, st);
+    if (!rc) rc = launch_gemv_dequant(h->xq, h->xs, h->w, h->scales, m, h->hidden, h->rows, dlog, st);
+    if (rc) return rc;
+    float *dbv = mem == FOCR_MEM_DEVICE ? best_val : h->bv;
+    int32_t *dbi = mem == FOCR_MEM_DEVICE ? best_idx : h->bi;
+    argmax_rows_kernel<<<(unsigned)m, 1024, 0, st>>>(dlog, (int)h->rows, (int)h->row_begin, dbv, dbi);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    if (mem == FOCR_MEM_HOST) {
+        FOCR_CUDA_TRY(cudaMemcpyAsync(best_val, h->bv, m * 4, cudaMemcpyDeviceToHost, st));
+        FOCR_CUDA_TRY(cudaMemcpyAsync(best_idx, h->bi, m * 4, cudaMemcpyDeviceToHost, st));
+        if (logits)
+            FOCR_CUDA_TRY(cudaMemcpyAsync(logits, h->logits, m * h->rows * 4,
+                                          cudaMemcpyDeviceToHost, st));
+        FOCR_CUDA_TRY(cudaStreamSynchronize(st));
+    }
+    return FOCR_OK;
+}
+
+int focr_top1_combine(const float *vals, const int32_t *idx, size_t shards, size_t m,
+                      uint32_t *token) {
+    if (!vals || !idx || !token) return fail(FOCR_E_ARG, "top1_combine: null pointer");
+    for (size_t r = 0; r < m; r++) {
+        int32_t b = -1;
+        float bv = 0.0f;
+        for (size_t s = 0; s < shards; s++) {
+            const int32_t i = idx[s * m + r];
+            const float v = vals[s * m + r];
+            if (i < 0 || std::isnan(v)) continue;
+            if (b >= 0 && v <= bv) continue;
+            b = i;
+            bv = v;
+        }
+        token[r] = b < 0 ? 0u : (uint32_t)b;
+    }
+    return FOCR_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,627 @@
+// MoE decode layer: router (moe.rs:181-266), expert SwiGLU FFN and combine
+// (decoder.rs:2199-2268), batched per-stream semantics (decoder.rs:2812-2933).
+//
+// General path (any m): route -> quantise tokens -> bucket (token, slot)
+// pairs by expert -> gate+up GEMV with SwiGLU over every pair of an expert
+// while its weight rows are in registers (each weight row is read from HBM
+// once per call, whatever the number of tokens routed to it) -> per-pair
+// activation requantisation -> down GEMV (weight row read once) writing the
+// weighted partial p_j -> slot-ordered combine + shared expert.
+#include <cstring>
+
+#include "gemv.cuh"
+#include "moe.cuh"
+
+namespace focr {
+
+constexpr int MOE_THREADS = 256;
+constexpr int MOE_MAX_CH = 4;  // 16-byte chunks per lane: K <= 32*16*4 = 2048
+
+struct MoeDev {
+    int H, I, S, E, topk, T;
+    int expert_begin;
+    const int8_t *gate_w, *up_w, *down_w;
+    const float *gate_s, *up_s, *down_s;
+    const int8_t *sh_gate_w, *sh_up_w, *sh_down_w;
+    const float *sh_gate_s, *sh_up_s, *sh_down_s;
+    const int32_t *offsets, *pair_tok, *pair_slot;
+    const int8_t *xq;
+    const float *xs;
+    float *act, *sh_act;
+    const int8_t *aq, *sh_aq;
+    const float *as2, *sh_as;
+    const float *w;   // routing weights [T][topk]
+    float *part, *sh_y;
+};
+
+// ---------------------------------------------------------------------------
+// Router
+// ---------------------------------------------------------------------------
+
+// One warp per (token, expert): the lane-striped dot order defined in the
+// oracle (oracle_router_logits): lane l adds the 4-element chunks c with
+// c % 32 == l in increasing k, then an xor butterfly 16, 8, 4, 2, 1.
+__global__ void router_logits_kernel(const float *__restrict__ x, const float *__restrict__ G,
+                                     int H, int E, float *__restrict__ logits) {
+    const int t = blockIdx.y;
+    const int lane = threadIdx.x & 31;
+    const int e = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (e >= E) return;
+    const float *xr = x + (size_t)t * H;
+    const float *g = G + (size_t)e * H;
+    float s = 0.0f;
+    if ((H & 3) == 0) {
+        const float4 *x4 = reinterpret_cast<const float4 *>(xr);
+        const float4 *g4 = reinterpret_cast<const float4 *>(g);
+        for (int c = lane; c < (H >> 2); c += 32) {
+            const float4 a = x4[c], b = __ldg(g4 + c);
+            s = __fadd_rn(s, __fmul_rn(a.x, b.x));
+            s = __fadd_rn(s, __fmul_rn(a.y, b.y));
+            s = __fadd_rn(s, __fmul_rn(a.z, b.z));
+            s = __fadd_rn(s, __fmul_rn(a.w, b.w));
+        }
+    } else {
+        for (int c = lane; 4 * c < H; c += 32)
+            for (int k = 4 * c; k < 4 * c + 4 && k < H; k++) s = __fadd_rn(s, __fmul_rn(xr[k], g[k]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+    if (lane == 0) logits[(size_t)t * E + e] = s;
+}
+
+// Softmax + greedy top-k + optional renorm + scaling for one token (one
+// warp).  Tie/NaN rules of next_router_expert (moe.rs:245-266): the first
+// maximum among not-taken experts wins, NaN scores are skipped.
+__device__ void topk_warp(const float *__restrict__ l, int E, int topk, int norm, float scaling,
+                          float *ev /* smem [E] */, unsigned *taken /* smem [(E+31)/32] */,
+                          int32_t *idx_out, float *w_out, int *bad) {
+    const int lane = threadIdx.x & 31;
+    float m = -INFINITY;
+    for (int e = lane; e < E; e += 32) m = fmaxf(m, l[e]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    for (int e = lane; e < E; e += 32) ev[e] = dexpf(__fsub_rn(l[e], m));
+    for (int i = lane; i < (E + 31) / 32; i += 32) taken[i] = 0u;
+    __syncwarp();
+    float sum = 0.0f;
+    if (lane == 0)
+        for (int e = 0; e < E; e++) sum = __fadd_rn(sum, ev[e]);
+    sum = __shfl_sync(0xffffffffu, sum, 0);
+    for (int e = lane; e < E; e += 32) ev[e] = __fdiv_rn(ev[e], sum);
+    __syncwarp();
+    float wsel[8];
+    int isel[8];
+    int fail_any = 0;
+    for (int s = 0; s < topk; s++) {
+        int be = -1;
+        float bv = 0.0f;
+        for (int e = lane; e < E; e += 32) {
+            const float v = ev[e];
+            if ((taken[e >> 5] >> (e & 31)) & 1u) continue;
+            if (v != v) continue;
+            if (be >= 0 && v <= bv) continue;
+            be = e;
+            bv = v;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const bool take = oe >= 0 && (be < 0 || ov > bv || (ov == bv && oe < be));
+            if (take) {
+                be = oe;
+                bv = ov;
+            }
+        }
+        if (be < 0) {
+            fail_any = 1;
+            isel[s] = -1;
+            wsel[s] = 0.0f;
+            continue;
+        }
+        if (lane == 0) taken[be >> 5] |= 1u << (be & 31);
+        __syncwarp();
+        isel[s] = be;
+        wsel[s] = bv;
+    }
+    if (lane == 0) {
+        if (norm && !fail_any) {
+            float d = 0.0f;
+            for (int s = 0; s < topk; s++) d = __fadd_rn(d, wsel[s]);
+            d = __fadd_rn(d, 1e-20f);
+            for (int s = 0; s < topk; s++) wsel[s] = __fdiv_rn(wsel[s], d);
+        }
+        for (int s = 0; s < topk; s++) {
+            idx_out[s] = isel[s];
+            w_out[s] = __fmul_rn(wsel[s], scaling);
+        }
+        *bad = fail_any;
+    }
+}
+
+__global__ void topk_kernel(const float *__restrict__ logits, int E, int topk, int norm,
+                            float scaling, int32_t *__restrict__ idx, float *__restrict__ w,
+                            int32_t *err) {
+    __shared__ float ev[1024];
+    __shared__ unsigned taken[32];
+    const int t = blockIdx.x;
+    int bad = 0;
+    topk_warp(logits + (size_t)t * E, E, topk, norm, scaling, ev, taken, idx + (size_t)t * topk,
+              w + (size_t)t * topk, &bad);
+    if (threadIdx.x == 0 && bad) atomicOr(err, 1);
+}
+
+// ---------------------------------------------------------------------------
+// Expert FFN (general path)
+// ---------------------------------------------------------------------------
+
+// Bucket the (token, slot) pairs by local expert.  Single block.
+__global__ void bucket_kernel(const int32_t *__restrict__ idx, int T, int topk, int E,
+                              int expert_begin, int32_t *__restrict__ offsets,
+                              int32_t *__restrict__ pair_tok, int32_t *__restrict__ pair_slot) {
+    __shared__ int cnt[1025];
+    __shared__ int cur[1025];
+    for (int e = threadIdx.x; e <= E; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    const int P = T * topk;
+    for (int p = threadIdx.x; p < P; p += blockDim.x) {
+        const int e = idx[p] - expert_begin;
+        if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int run = 0;
+        for (int e = 0; e < E; e++) {
+            cur[e] = run;
+            offsets[e] = run;
+            run += cnt[e];
+        }
+        offsets[E] = run;
+    }
+    __syncthreads();
+    for (int p = threadIdx.x; p < P; p += blockDim.x) {
+        const int e = idx[p] - expert_begin;
+        if (e >= 0 && e < E) {
+            const int pos = atomicAdd(&cur[e], 1);
+            pair_tok[pos] = p / topk;
+            pair_slot[pos] = p % topk;
+        }
+    }
+}
+
+// Load one weight row's 16-byte chunks owned by this lane into registers.
+__device__ __forceinline__ void load_row(const int8_t *row, int K16, int lane, int4 (&r)[MOE_MAX_CH]) {
+#pragma unroll
+    for (int u = 0; u < MOE_MAX_CH; u++) {
+        const int c = lane + 32 * u;
+        r[u] = c < K16 ? ld_stream16(reinterpret_cast<const int4 *>(row) + c) : make_int4(0, 0, 0, 0);
+    }
+}
+
+__device__ __forceinline__ int dot_row(const int8_t *a, int K16, int lane, const int4 (&r)[MOE_MAX_CH]) {
+    int acc = 0;
+#pragma unroll
+    for (int u = 0; u < MOE_MAX_CH; u++) {
+        const int c = lane + 32 * u;
+        if (c < K16) acc = dot16<false>(reinterpret_cast<const int4 *>(a)[c], r[u], acc);
+    }
+    return acc;
+}
+
+// Gate + up + SwiGLU.  One warp per weight row pair (gate row i, up row i)
+// of a local expert (or of the shared expert), applied to every pair routed
+// to that expert: act = silu(g) * u with g, u dequantised per
+// decoder.rs:1621-1640.
+__global__ void __launch_bounds__(MOE_THREADS) expert_gateup_kernel(MoeDev d) {
+    const int lane = threadIdx.x & 31;
+    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int nw = gridDim.x * (blockDim.x >> 5);
+    const int H16 = d.H >> 4;
+    const long routed_rows = (long)d.E * d.I;
+    const long total = routed_rows + (d.S ? d.S : 0);
+    for (long r = gw; r < total; r += nw) {
+        const int8_t *grow, *urow;
+        float gsc, usc;
+        int p0, p1, I;
+        float *act;
+        bool shared = r >= routed_rows;
+        int i;
+        if (!shared) {
+            const int e = (int)(r / d.I);
+            i = (int)(r % d.I);
+            p0 = d.offsets[e];
+            p1 = d.offsets[e + 1];
+            if (p0 == p1) continue;
+            grow = d.gate_w + ((size_t)e * d.I + i) * d.H;
+            urow = d.up_w + ((size_t)e * d.I + i) * d.H;
+            gsc = d.gate_s[(size_t)e * d.I + i];
+            usc = d.up_s[(size_t)e * d.I + i];
+            I = d.I;
+            act = d.act;
+        } else {
+            i = (int)(r - routed_rows);
+            p0 = 0;
+            p1 = d.T;
+            grow = d.sh_gate_w + (size_t)i * d.H;
+            urow = d.sh_up_w + (size_t)i * d.H;
+            gsc = d.sh_gate_s[i];
+            usc = d.sh_up_s[i];
+            I = d.S;
+            act = d.sh_act;
+        }
+        int4 gr[MOE_MAX_CH], ur[MOE_MAX_CH];
+        load_row(grow, H16, lane, gr);
+        load_row(urow, H16, lane, ur);
+        for (int p = p0; p < p1; p++) {
+            const int tok = shared ? p : d.pair_tok[p];
+            const int8_t *xr = d.xq + (size_t)tok * d.H;
+            int ag = dot_row(xr, H16, lane, gr);
+            int au = dot_row(xr, H16, lane, ur);
+            ag = warp_sum_i32(ag);
+            au = warp_sum_i32(au);
+            if (lane == 0) {
+                const float as = d.xs[tok];
+                const float g = __fmul_rn(__fmul_rn((float)ag, as), gsc);
+                const float u = __fmul_rn(__fmul_rn((float)au, as), usc);
+                act[(size_t)p * I + i] = __fmul_rn(silu_f(g), u);
+            }
+        }
+    }
+}
+
+// Requantise activation rows (pairs, then shared tokens).  One block per row;
+// rows >= the live pair count are skipped.
+__global__ void act_quant_kernel(const float *__restrict__ act, int I, const int32_t *__restrict__ count,
+                                 int8_t *__restrict__ aq, float *__restrict__ as) {
+    if (count && (int)blockIdx.x >= *count) return;
+    __shared__ float red[32];
+    __shared__ float s_inv;
+    const float *row = act + (size_t)blockIdx.x * I;
+    int8_t *q = aq + (size_t)blockIdx.x * I;
+    float m = 0.0f;
+    for (int i = threadIdx.x; i < I; i += blockDim.x) m = fmaxf(m, fabsf(row[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float a = 0.0f;
+        for (int wi = 0; wi < (int)(blockDim.x >> 5); wi++) a = fmaxf(a, red[wi]);
+        const float sc = a > 0.0f ? __fdiv_rn(a, 127.0f) : 1.0f;
+        as[blockIdx.x] = sc;
+        s_inv = __fdiv_rn(1.0f, sc);
+    }
+    __syncthreads();
+    const float inv = s_inv;
+    for (int i = threadIdx.x; i < I; i += blockDim.x) q[i] = (int8_t)quant_i8(row[i], inv, false);
+}
+
+// Down GEMV: one warp per down row c of a local expert (K = I) or of the
+// shared expert (K = S); writes p = y * w for routed pairs and y for shared.
+__global__ void __launch_bounds__(MOE_THREADS) expert_down_kernel(MoeDev d) {
+    const int lane = threadIdx.x & 31;
+    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int nw = gridDim.x * (blockDim.x >> 5);
+    const long routed_rows = (long)d.E * d.H;
+    const long total = routed_rows + (d.S ? d.H : 0);
+    for (long r = gw; r < total; r += nw) {
+        const bool shared = r >= routed_rows;
+        int c, p0, p1, K;
+        const int8_t *drow;
+        float dsc;
+        if (!shared) {
+            const int e = (int)(r / d.H);
+            c = (int)(r % d.H);
+            p0 = d.offsets[e];
+            p1 = d.offsets[e + 1];
+            if (p0 == p1) continue;
+            K = d.I;
+            drow = d.down_w + ((size_t)e * d.H + c) * d.I;
+            dsc = d.down_s[(size_t)e * d.H + c];
+        } else {
+            c = (int)(r - routed_rows);
+            p0 = 0;
+            p1 = d.T;
+            K = d.S;
+            drow = d.sh_down_w + (size_t)c * d.S;
+            dsc = d.sh_down_s[c];
+        }
+        const int K16 = K >> 4;
+        int4 wr[MOE_MAX_CH];
+        load_row(drow, K16, lane, wr);
+        for (int p = p0; p < p1; p++) {
+            const int8_t *ar = shared ? d.sh_aq + (size_t)p * K : d.aq + (size_t)p * K;
+            int acc = warp_sum_i32(dot_row(ar, K16, lane, wr));
+            if (lane == 0) {
+                if (shared) {
+                    d.sh_y[(size_t)p * d.H + c] = __fmul_rn(__fmul_rn((float)acc, d.sh_as[p]), dsc);
+                } else {
+                    const int tok = d.pair_tok[p], slot = d.pair_slot[p];
+                    const float yv = __fmul_rn(__fmul_rn((float)acc, d.as2[p]), dsc);
+                    d.part[((size_t)tok * d.topk + slot) * d.H + c] =
+                        __fmul_rn(yv, d.w[(size_t)tok * d.topk + slot]);
+                }
+            }
+        }
+    }
+}
+
+// out = (((0 + p_0) + p_1) + ... + p_{k-1}) + s   (decoder.rs:2253-2261)
+__global__ void combine_kernel(const float *__restrict__ part, const float *__restrict__ sh_y,
+                               int H, int topk, float *__restrict__ y) {
+    const int t = blockIdx.y;
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= H) return;
+    float o = 0.0f;
+    for (int j = 0; j < topk; j++) o = __fadd_rn(o, part[((size_t)t * topk + j) * H + c]);
+    if (sh_y) o = __fadd_rn(o, sh_y[(size_t)t * H + c]);
+    y[(size_t)t * H + c] = o;
+}
+
+__global__ void check_idx_kernel(const int32_t *idx, int P, int lo, int hi, int32_t *err) {
+    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < P; p += gridDim.x * blockDim.x)
+        if (idx[p] < lo || idx[p] >= hi) atomicOr(err, 2);
+}
+
+// ---------------------------------------------------------------------------
+// Host orchestration
+// ---------------------------------------------------------------------------
+
+static MoeDev make_dev(focr_moe_layer *L, int T, const float *w, float *part) {
+    MoeDev d;
+    d.H = L->cfg.hidden;
+    d.I = L->cfg.inter;
+    d.S = L->cfg.shared_inter;
+    d.E = L->E;
+    d.topk = L->cfg.topk;
+    d.T = T;
+    d.expert_begin = L->cfg.expert_begin;
+    d.gate_w = L->gate_w; d.up_w = L->up_w; d.down_w = L->down_w;
+    d.gate_s = L->gate_s; d.up_s = L->up_s; d.down_s = L->down_s;
+    d.sh_gate_w = L->sh_gate_w; d.sh_up_w = L->sh_up_w; d.sh_down_w = L->sh_down_w;
+    d.sh_gate_s = L->sh_gate_s; d.sh_up_s = L->sh_up_s; d.sh_down_s = L->sh_down_s;
+    d.offsets = L->offsets; d.pair_tok = L->pair_tok; d.pair_slot = L->pair_slot;
+    d.xq = L->xq; d.xs = L->xs;
+    d.act = L->act; d.sh_act = L->sh_act;
+    d.aq = L->aq; d.sh_aq = L->sh_aq;
+    d.as2 = L->as2; d.sh_as = L->sh_as;
+    d.w = w;
+    d.part = part; d.sh_y = L->sh_y;
+    return d;
+}
+
+static int moe_grid() { return num_sms() * 8; }
+
+int moe_route_dev(focr_moe_layer *L, const float *x, int m, int32_t *idx, float *w,
+                  cudaStream_t st) {
+    const int E = L->cfg.n_experts, H = L->cfg.hidden;
+    dim3 g1((E + 7) / 8, m);
+    router_logits_kernel<<<g1, 256, 0, st>>>(x, L->router, H, E, L->logits);
+    topk_kernel<<<m, 32, 0, st>>>(L->logits, E, L->cfg.topk, L->cfg.norm_topk_prob,
+                                  L->cfg.routed_scaling_factor, idx, w, L->err);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    return FOCR_OK;
+}
+
+int moe_forward_dev(focr_moe_layer *L, const float *x, int m, const int32_t *idx,
+                    const float *w, float *y, cudaStream_t st) {
+    const int H = L->cfg.hidden, K = L->cfg.topk;
+    check_idx_kernel<<<1, 256, 0, st>>>(idx, m * K, (int)L->cfg.expert_begin,
+                                        (int)(L->cfg.expert_begin + L->E), L->err);
+    int rc = launch_quantize_rows(x, m, H, false, L->xq, L->xs, st);
+    if (rc) return rc;
+    bucket_kernel<<<1, 1024, 0, st>>>(idx, m, K, L->E, L->cfg.expert_begin, L->offsets,
+                                      L->pair_tok, L->pair_slot);
+    MoeDev d = make_dev(L, m, w, L->part);
+    expert_gateup_kernel<<<moe_grid(), MOE_THREADS, 0, st>>>(d);
+    act_quant_kernel<<<m * K, 256, 0, st>>>(L->act, L->cfg.inter, L->offsets + L->E, L->aq, L->as2);
+    if (L->cfg.shared_inter)
+        act_quant_kernel<<<m, 256, 0, st>>>(L->sh_act, L->cfg.shared_inter, nullptr, L->sh_aq, L->sh_as);
+    expert_down_kernel<<<moe_grid(), MOE_THREADS, 0, st>>>(d);
+    dim3 gc((H + 255) / 256, m);
+    combine_kernel<<<gc, 256, 0, st>>>(L->part, L->cfg.shared_inter ? L->sh_y : nullptr, H, K, y);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    return FOCR_OK;
+}
+
+}  // namespace focr
+
+using namespace focr;
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+
+template <typename T>
+static int dev_upload(T **dst, const T *src, size_t count) {
+    if (!count) return FOCR_OK;
+    if (!src) return fail(FOCR_E_ARG, "moe_create: missing weight array");
+    FOCR_CUDA_TRY(cudaMalloc((void **)dst, count * sizeof(T)));
+    FOCR_CUDA_TRY(cudaMemcpy(*dst, src, count * sizeof(T), cudaMemcpyHostToDevice));
+    return FOCR_OK;
+}
+
+template <typename T>
+static int dev_alloc(T **dst, size_t count) {
+    FOCR_CUDA_TRY(cudaMalloc((void **)dst, (count ? count : 1) * sizeof(T)));
+    FOCR_CUDA_TRY(cudaMemset(*dst, 0, (count ? count : 1) * sizeof(T)));
+    return FOCR_OK;
+}
+
+#define TRY(x)                  \
+    do {                        \
+        int _rc = (x);          \
+        if (_rc) {              \
+            focr_moe_destroy(L); \
+            return _rc;         \
+        }                       \
+    } while (0)
+
+extern "C" {
+
+int focr_moe_destroy(focr_moe_layer *L) {
+    if (!L) return FOCR_OK;
+    void *ptrs[] = {L->router, L->gate_w, L->up_w, L->down_w, L->gate_s, L->up_s, L->down_s,
+                    L->gate_p, L->up_p, L->down_p, L->gate_gs, L->up_gs, L->down_gs,
+                    L->sh_gate_w, L->sh_up_w, L->sh_down_w, L->sh_gate_s, L->sh_up_s,
+                    L->sh_down_s, L->x, L->y, L->idx, L->w, L->logits, L->xq, L->xs,
+                    L->counts, L->offsets, L->pair_tok, L->pair_slot, L->act, L->amax, L->aq,
+                    L->as2, L->part, L->sh_act, L->sh_amax, L->sh_as, L->sh_y, L->sh_aq, L->err,
+                    L->sync};
+    for (void *p : ptrs)
+        if (p) cudaFree(p);
+    delete L;
+    return FOCR_OK;
+}
+
+int focr_moe_create(const focr_moe_config *cfg, const focr_moe_weights *wt,
+                    focr_moe_layer **out) {
+    if (!cfg || !wt || !out) return fail(FOCR_E_ARG, "moe_create: null argument");
+    const focr_moe_config c = *cfg;
+    if (c.hidden == 0 || c.hidden % 16 || c.hidden > 2048)
+        return fail(FOCR_E_UNSUPPORTED, "moe_create: hidden must be a multiple of 16 and <= 2048");
+    if (c.inter == 0 || c.inter % 16 || c.inter > 2048)
+        return fail(FOCR_E_UNSUPPORTED, "moe_create: inter must be a multiple of 16 and <= 2048");
+    if (c.shared_inter % 16 || c.shared_inter > 2048)
+        return fail(FOCR_E_UNSUPPORTED, "moe_create: shared_inter must be a multiple of 16 and <= 2048");
+    if (c.topk == 0 || c.topk > 8) return fail(FOCR_E_UNSUPPORTED, "moe_create: topk must be 1..8");
+    if (c.n_experts < c.topk) return fail(FOCR_E_ARG, "moe::route: n_routed_experts < top_k");
+    if (c.n_experts > 1024) return fail(FOCR_E_UNSUPPORTED, "moe_create: n_experts > 1024");
+    if (c.expert_count == 0 || c.expert_begin + c.expert_count > c.n_experts)
+        return fail(FOCR_E_ARG, "moe_create: bad expert_begin/expert_count");
+    if (c.max_tokens == 0 || c.max_tokens > 65536)
+        return fail(FOCR_E_ARG, "moe_create: max_tokens must be 1..65536");
+    if (c.group != 0) return fail(FOCR_E_UNSUPPORTED, "moe_create: int4 experts not built yet");
+    focr_moe_layer *L = new focr_moe_layer();
+    L->cfg = c;
+    L->E = c.expert_count;
+    cudaGetDevice(&L->device);
+    const size_t H = c.hidden, I = c.inter, S = c.shared_inter, E = c.expert_count;
+    const size_t T = c.max_tokens, K = c.topk, P = T * K;
+    TRY(dev_upload(&L->router, wt->router, (size_t)c.n_experts * H));
+    TRY(dev_upload(&L->gate_w, wt->gate_w, E * I * H));
+    TRY(dev_upload(&L->up_w, wt->up_w, E * I * H));
+    TRY(dev_upload(&L->down_w, wt->down_w, E * H * I));
+    TRY(dev_upload(&L->gate_s, wt->gate_s, E * I));
+    TRY(dev_upload(&L->up_s, wt->up_s, E * I));
+    TRY(dev_upload(&L->down_s, wt->down_s, E * H));
+    if (S) {
+        TRY(dev_upload(&L->sh_gate_w, wt->sh_gate_w, S * H));
+        TRY(dev_upload(&L->sh_up_w, wt->sh_up_w, S * H));
+        TRY(dev_upload(&L->sh_down_w, wt->sh_down_w, H * S));
+        TRY(dev_upload(&L->sh_gate_s, wt->sh_gate_s, S));
+        TRY(dev_upload(&L->sh_up_s, wt->sh_up_s, S));
+        TRY(dev_upload(&L->sh_down_s, wt->sh_down_s, H));
+        TRY(dev_alloc(&L->sh_act, T * S));
+        TRY(dev_alloc(&L->sh_aq, T * S));
+        TRY(dev_alloc(&L->sh_as, T));
+        TRY(dev_alloc(&L->sh_amax, T));
+        TRY(dev_alloc(&L->sh_y, T * H));
+    }
+    TRY(dev_alloc(&L->x, T * H));
+    TRY(dev_alloc(&L->y, T * H));
+    TRY(dev_alloc(&L->idx, P));
+    TRY(dev_alloc(&L->w, P));
+    TRY(dev_alloc(&L->logits, T * c.n_experts));
+    TRY(dev_alloc(&L->xq, T * H));
+    TRY(dev_alloc(&L->xs, T));
+    TRY(dev_alloc(&L->counts, E + 1));
+    TRY(dev_alloc(&L->offsets, E + 2));
+    TRY(dev_alloc(&L->pair_tok, P));
+    TRY(dev_alloc(&L->pair_slot, P));
+    TRY(dev_alloc(&L->act, P * I));
+    TRY(dev_alloc(&L->amax, P));
+    TRY(dev_alloc(&L->aq, P * I));
+    TRY(dev_alloc(&L->as2, P));
+    TRY(dev_alloc(&L->part, T * K * H));
+    TRY(dev_alloc(&L->err, 4));
+    TRY(dev_alloc(&L->sync, 64));
+    L->fused_ok = moe_fused_eligible(L) ? 1 : 0;
+    *out = L;
+    return FOCR_OK;
+}
+
+// Reads and clears the device status word (synchronises the stream).
+static int read_status(focr_moe_layer *L, cudaStream_t st) {
+    int32_t e = 0;
+    FOCR_CUDA_TRY(cudaMemcpyAsync(&e, L->err, 4, cudaMemcpyDeviceToHost, st));
+    FOCR_CUDA_TRY(cudaStreamSynchronize(st));
+    if (e) {
+        cudaMemsetAsync(L->err, 0, 4, st);
+        cudaStreamSynchronize(st);
+        if (e & 1) return fail(FOCR_E_ROUTE, "moe::route: no finite router score");
+        if (e & 2) return fail(FOCR_E_ARG, "moe_forward: routed expert index not resident on this device");
+        if (e & 4) return fail(FOCR_E_TIMEOUT, "moe_decode: device-side barrier wait expired");
+    }
+    return FOCR_OK;
+}
+
+int focr_moe_route(focr_moe_layer *L, const float *x, size_t m, int32_t *idx, float *w, int mem,
+                   void *stream) {
+    if (!L) return fail(FOCR_E_ARG, "moe_route: null layer");
+    if (m == 0) return FOCR_OK;
+    if (m > L->cfg.max_tokens) return fail(FOCR_E_SHAPE, "moe_route: m > max_tokens");
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t H = L->cfg.hidden, K = L->cfg.topk;
+    if (mem == FOCR_MEM_DEVICE) return moe_route_dev(L, x, (int)m, idx, w, st);
+    FOCR_CUDA_TRY(cudaMemcpyAsync(L->x, x, m * H * 4, cudaMemcpyHostToDevice, st));
+    int rc = moe_route_dev(L, L->x, (int)m, L->idx, L->w, st);
+    if (rc) return rc;
+    FOCR_CUDA_TRY(cudaMemcpyAsync(idx, L->idx, m * K * 4, cudaMemcpyDeviceToHost, st));
+    FOCR_CUDA_TRY(cudaMemcpyAsync(w, L->w, m * K * 4, cudaMemcpyDeviceToHost, st));
+    return read_status(L, st);
+}
+
+int focr_moe_forward(focr_moe_layer *L, const float *x, size_t m, const int32_t *idx,
+                     const float *w, float *y, int mem, void *stream) {
+    if (!L) return fail(FOCR_E_ARG, "moe_forward: null layer");
+    if (m == 0) return FOCR_OK;
+    if (m > L->cfg.max_tokens) return fail(FOCR_E_SHAPE, "moe_forward: m > max_tokens");
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t H = L->cfg.hidden, K = L->cfg.topk;
+    if (mem == FOCR_MEM_DEVICE) return moe_forward_dev(L, x, (int)m, idx, w, y, st);
+    FOCR_CUDA_TRY(cudaMemcpyAsync(L->x, x, m * H * 4, cudaMemcpyHostToDevice, st));
+    FOCR_CUDA_TRY(cudaMemcpyAsync(L->idx, idx, m * K * 4, cudaMemcpyHostToDevice, st));
+    FOCR_CUDA_TRY(cudaMemcpyAsync(L->w, w, m * K * 4, cudaMemcpyHostToDevice, st));
+    int rc = moe_forward_dev(L, L->x, (int)m, L->idx, L->w, L->y, st);
+    if (rc) return rc;
+    FOCR_CUDA_TRY(cudaMemcpyAsync(y, L->y, m * H * 4, cudaMemcpyDeviceToHost, st));
+    return read_status(L, st);
+}
+
+int focr_moe_decode(focr_moe_layer *L, const float *x, size_t m, float *y, int32_t *idx,
+                    float *w, int mem, void *stream) {
+    if (!L) return fail(FOCR_E_ARG, "moe_decode: null layer");
+    if (m == 0) return FOCR_OK;
+    if (m > L->cfg.max_tokens) return fail(FOCR_E_SHAPE, "moe_decode: m > max_tokens");
+    if (L->E != L->cfg.n_experts)
+        return fail(FOCR_E_ARG, "moe_decode: layer holds a subset of experts; use route + forward");
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t H = L->cfg.hidden, K = L->cfg.topk;
+    const float *dx = x;
+    float *dy = y;
+    if (mem == FOCR_MEM_HOST) {
+        FOCR_CUDA_TRY(cudaMemcpyAsync(L->x, x, m * H * 4, cudaMemcpyHostToDevice, st));
+        dx = L->x;
+        dy = L->y;
+    }
+    int32_t *di = (mem == FOCR_MEM_DEVICE && idx) ? idx : L->idx;
+    float *dw = (mem == FOCR_MEM_DEVICE && w) ? w : L->w;
+    int rc;
+    if (m == 1 && L->fused_ok) {
+        rc = moe_decode_fused_m1(L, dx, dy, di, dw, st);
+    } else {
+        rc = moe_route_dev(L, dx, (int)m, di, dw, st);
+        if (!rc) rc = moe_forward_dev(L, dx, (int)m, di, dw, dy, st);
+    }
+    if (rc) return rc;
+    if (mem == FOCR_MEM_HOST) {
+        FOCR_CUDA_TRY(cudaMemcpyAsync(y, L->y, m * H * 4, cudaMemcpyDeviceToHost, st));
+        if (idx) FOCR_CUDA_TRY(cudaMemcpyAsync(idx, L->idx, m * K * 4, cudaMemcpyDeviceToHost, st));
+        if (w) FOCR_CUDA_TRY(cudaMemcpyAsync(w, L->w, m * K * 4, cudaMemcpyDeviceToHost, st));
+        return read_status(L, st);
+    }
+    return FOCR_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,51 @@
+// MoE decode layer internals (device weights + scratch of one handle).
+#pragma once
+
+#include "common.cuh"
+
+struct focr_moe_layer {
+    focr_moe_config cfg;
+    int device;
+    uint32_t E;   // local expert count
+    // ---- weights (device) ----
+    float *router = nullptr;                       // [n_experts][H]
+    int8_t *gate_w = nullptr, *up_w = nullptr, *down_w = nullptr;
+    float *gate_s = nullptr, *up_s = nullptr, *down_s = nullptr;
+    uint8_t *gate_p = nullptr, *up_p = nullptr, *down_p = nullptr;
+    float *gate_gs = nullptr, *up_gs = nullptr, *down_gs = nullptr;
+    int8_t *sh_gate_w = nullptr, *sh_up_w = nullptr, *sh_down_w = nullptr;
+    float *sh_gate_s = nullptr, *sh_up_s = nullptr, *sh_down_s = nullptr;
+    // ---- scratch (sized by cfg.max_tokens = T) ----
+    float *x = nullptr, *y = nullptr;              // [T][H] host-call staging
+    int32_t *idx = nullptr;                        // [T][topk]
+    float *w = nullptr;                            // [T][topk]
+    float *logits = nullptr;                       // [T][n_experts]
+    int8_t *xq = nullptr;                          // [T][H]
+    float *xs = nullptr;                           // [T]
+    int32_t *counts = nullptr;                     // [E+1] pairs per local expert
+    int32_t *offsets = nullptr;                    // [E+2]
+    int32_t *pair_tok = nullptr, *pair_slot = nullptr;  // [P]
+    float *act = nullptr;                          // [P][I]
+    float *amax = nullptr;                         // [P]   (pairs), then [T] shared
+    int8_t *aq = nullptr;                          // [P][I]
+    float *as2 = nullptr;                          // [P]
+    float *part = nullptr;                         // [T][topk][H]
+    float *sh_act = nullptr, *sh_amax = nullptr, *sh_as = nullptr, *sh_y = nullptr;
+    int8_t *sh_aq = nullptr;
+    int32_t *err = nullptr;                        // device status word
+    // fused M=1 path
+    unsigned int *sync = nullptr;                  // grid-barrier counters
+    int fused_ok = 0;
+};
+
+namespace focr {
+
+int moe_route_dev(focr_moe_layer *L, const float *x, int m, int32_t *idx, float *w,
+                  cudaStream_t st);
+int moe_forward_dev(focr_moe_layer *L, const float *x, int m, const int32_t *idx,
+                    const float *w, float *y, cudaStream_t st);
+int moe_decode_fused_m1(focr_moe_layer *L, const float *x, float *y, int32_t *idx, float *w,
+                        cudaStream_t st);
+bool moe_fused_eligible(const focr_moe_layer *L);
+
+}  // namespace focr

@@ -1,0 +1,184 @@
+/*
+ * focr_cuda.h -- C ABI of the B200 (sm_100a) int8 decode tier.
+ *
+ * Drop-in replacement for franken_ocr's CPU int8 kernel tier (src/simd) and
+ * the int8 MoE decode engine built on it (src/native_engine/decoder.rs int8
+ * engine + src/native_engine/moe.rs router).  Plain pointers and sizes only;
+ * a Rust FFI crate (or ctypes/cgo/JNI) binds these directly.
+ *
+ * Conventions
+ *   - Return 0 (FOCR_OK) on success, a negative FOCR_E_* code otherwise.
+ *     focr_last_error() returns a thread-local message; for shape errors it is
+ *     the reference's own panic text (e.g. "igemm_s8s8: a.len 2 != m*k 1").
+ *   - mem = FOCR_MEM_HOST: every array argument is host memory; the call
+ *     copies in, runs, copies out and synchronises `stream` before returning.
+ *     mem = FOCR_MEM_DEVICE: every array argument is device memory on the
+ *     current device; the call only enqueues work on `stream` (a
+ *     cudaStream_t, NULL = legacy default stream) and returns.
+ *   - Kernel-level entry points are stateless and re-entrant.  A layer handle
+ *     (focr_moe_layer, focr_lmhead) owns device scratch sized at create time;
+ *     calls on one handle must not overlap (use one handle per stream).
+ *   - Device-side waits are bounded; an expired wait returns FOCR_E_TIMEOUT
+ *     and leaves the CUDA context usable.
+ */
+#ifndef FOCR_CUDA_H
+#define FOCR_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FOCR_OK 0
+#define FOCR_E_SHAPE (-1)       /* length/shape contract violated (reference: panic) */
+#define FOCR_E_ARG (-2)         /* invalid argument (null pointer, bad group, ...)  */
+#define FOCR_E_CUDA (-3)        /* CUDA runtime error                               */
+#define FOCR_E_ALLOC (-4)       /* device allocation failed                         */
+#define FOCR_E_ROUTE (-5)       /* no finite router score (moe.rs:245-266)          */
+#define FOCR_E_TIMEOUT (-6)     /* a bounded device-side wait expired               */
+#define FOCR_E_UNSUPPORTED (-7) /* no sm_100 device / configuration not supported   */
+
+#define FOCR_MEM_HOST 0
+#define FOCR_MEM_DEVICE 1
+
+/* Thread-local text of the last error raised on this thread ("" if none). */
+const char *focr_last_error(void);
+
+/* Dispatched tier string, the value `focr robot backends` reports as
+ * `selected`.  Replaces simd::tier_string() (src/simd/dispatch.rs:128-136). */
+const char *focr_tier_string(void);
+
+/* C[M,N] += A[M,K] (i8, row-major) . B[N,K] (i8, output-channel-major) into
+ * i32 `out` (row-major [M,N]).  Lengths are checked like the reference:
+ * a_len == m*k, b_len == n*k, out_len == m*n.
+ * Replaces simd::igemm_s8s8 (src/simd/dispatch.rs:246; oracle
+ * src/simd/scalar.rs:78-127). */
+int focr_igemm_s8s8(const int8_t *a, size_t a_len, const int8_t *b, size_t b_len,
+                    size_t m, size_t k, size_t n, int32_t *out, size_t out_len,
+                    int mem, void *stream);
+
+/* Same with unsigned activations.  Replaces simd::igemm_u8s8
+ * (src/simd/dispatch.rs:276; oracle src/simd/scalar.rs:129-175). */
+int focr_igemm_u8s8(const uint8_t *a, size_t a_len, const int8_t *b, size_t b_len,
+                    size_t m, size_t k, size_t n, int32_t *out, size_t out_len,
+                    int mem, void *stream);
+
+/* out[M,N] = sum_g scales[n,g] * f32(sum_{k in g} a[m,k]*q4[n,k]), groups in
+ * increasing g; out OVERWRITTEN.  b_packed is [N, K/2] (low nibble = even k),
+ * scales [N, K/group], group in {16, 32}.  Replaces
+ * simd::int4::igemm_s4s8_packed (src/simd/int4.rs:437; oracle :304-343). */
+int focr_igemm_s4s8_packed(const int8_t *a, size_t a_len, const uint8_t *b_packed,
+                           size_t b_len, const float *scales, size_t scales_len,
+                           size_t group, size_t m, size_t k, size_t n, float *out,
+                           size_t out_len, int mem, void *stream);
+
+/* Per-row dynamic symmetric int8 quantisation: scale[r] = max|x[r,:]|/127
+ * (1.0 if 0), xq = clamp(round(x * (1/scale)), +-127).  ties_even = 0 rounds
+ * half away from zero (decoder.rs:1588-1597 quantize_row_i8), 1 rounds ties
+ * to even (decoder.rs:1647-1656 quantize_row_i8_te). */
+int focr_quantize_rows_i8(const float *x, size_t m, size_t k, int ties_even,
+                          int8_t *xq, float *scales, int mem, void *stream);
+
+/* y[M,N] = ((f32)(Q(x[m]) . w[n]) * a_scale[m]) * w_scale[n] with Q the
+ * half-away row quantiser -- decoder.rs:1607 gemv_i8 / :2703-2747
+ * gemv_i8_batched (per-row a_scale). */
+int focr_gemv_i8(const float *x, size_t m, size_t k, const int8_t *w,
+                 const float *w_scale, size_t n, float *y, int mem, void *stream);
+
+/* ---- MoE layer (native_engine/moe.rs + decoder.rs:2199-2268) ----------- */
+
+typedef struct focr_moe_config {
+    uint32_t hidden;          /* 1280 */
+    uint32_t inter;           /* routed expert intermediate (896) */
+    uint32_t n_experts;       /* routed experts in the model (64) */
+    uint32_t topk;            /* experts per token (6), <= 8 */
+    uint32_t shared_inter;    /* fused shared-expert intermediate (1792), 0 = none */
+    int32_t norm_topk_prob;   /* moe.rs:71-73 (pinned model: 0) */
+    float routed_scaling_factor; /* moe.rs:66 (1.0) */
+    uint32_t group;           /* 0: int8 per-row experts; 16/32: int4 group experts */
+    uint32_t expert_begin;    /* experts [expert_begin, expert_begin+expert_count) */
+    uint32_t expert_count;    /*   are resident on this device (expert parallel) */
+    uint32_t max_tokens;      /* largest m passed to any call on this handle */
+} focr_moe_config;
+
+/* Host-side weights.  int8 experts (group == 0): gate_w/up_w [E][inter][hidden],
+ * gate_s/up_s [E][inter], down_w [E][hidden][inter], down_s [E][hidden] --
+ * the QInt8 layout (tensor.rs:149-180), E = expert_count, local expert 0 is
+ * global expert expert_begin.  int4 experts (group 16/32): *_p packed
+ * [E][rows][cols/2] and *_gs [E][rows][cols/group] (QInt4, tensor.rs:190-206).
+ * router [n_experts][hidden] f32.  Shared expert arrays may be NULL when
+ * shared_inter == 0 (always int8). */
+typedef struct focr_moe_weights {
+    const float *router;
+    const int8_t *gate_w; const float *gate_s;
+    const int8_t *up_w;   const float *up_s;
+    const int8_t *down_w; const float *down_s;
+    const uint8_t *gate_p; const float *gate_gs;
+    const uint8_t *up_p;   const float *up_gs;
+    const uint8_t *down_p; const float *down_gs;
+    const int8_t *sh_gate_w; const float *sh_gate_s;
+    const int8_t *sh_up_w;   const float *sh_up_s;
+    const int8_t *sh_down_w; const float *sh_down_s;
+} focr_moe_weights;
+
+typedef struct focr_moe_layer focr_moe_layer;
+
+/* Upload a layer's weights once (the device twin of
+ * DecoderWeightCacheI8::build, decoder.rs:2018) onto the current device. */
+int focr_moe_create(const focr_moe_config *cfg, const focr_moe_weights *w,
+                    focr_moe_layer **out);
+int focr_moe_destroy(focr_moe_layer *layer);
+
+/* Router: softmax over n_experts, greedy top-k, optional renormalisation,
+ * routed scaling (moe.rs:181-266).  idx [m][topk] i32, w [m][topk] f32. */
+int focr_moe_route(focr_moe_layer *layer, const float *x, size_t m, int32_t *idx,
+                   float *w, int mem, void *stream);
+
+/* Expert FFN + combine for given routing: y[t] = (((0 + p_0) + ...) + p_{k-1})
+ * + shared(x[t]) with p_j = expert_{idx[t][j]}(x[t]) * w[t][j] -- the per
+ * stream result of decode_mlp_i8 (decoder.rs:2199-2268, batched semantics
+ * :2812-2933).  All idx must be resident (expert_begin..+expert_count). */
+int focr_moe_forward(focr_moe_layer *layer, const float *x, size_t m,
+                     const int32_t *idx, const float *w, float *y, int mem,
+                     void *stream);
+
+/* Route + forward in one call (decode_mlp_i8).  idx/w outputs may be NULL. */
+int focr_moe_decode(focr_moe_layer *layer, const float *x, size_t m, float *y,
+                    int32_t *idx, float *w, int mem, void *stream);
+
+/* ---- lm-head (decoder.rs:2275-2296, 1851-1927; sampler.rs:168-186) ---- */
+
+typedef struct focr_lmhead focr_lmhead;
+
+/* Upload a vocab shard: rows [row_begin, row_begin+rows) of the [vocab,
+ * hidden] int8 head with per-row scales. */
+int focr_lmhead_create(const int8_t *w, const float *scales, size_t rows,
+                       size_t hidden, size_t row_begin, size_t max_tokens,
+                       focr_lmhead **out);
+int focr_lmhead_destroy(focr_lmhead *h);
+
+/* For each of m (already RMS-normed) rows: logits = gemv_i8(x, shard); top-1
+ * over the shard with argmax_row semantics (first max, NaN skipped).  Writes
+ * best_val[m], best_idx[m] (GLOBAL vocab index; -1 if the shard is all-NaN)
+ * and, if logits != NULL, the shard logits [m][rows]. */
+int focr_lmhead_top1(focr_lmhead *h, const float *x, size_t m, float *best_val,
+                     int32_t *best_idx, float *logits, int mem, void *stream);
+
+/* Combine per-shard top-1 pairs [shards][m] (ascending shard = ascending
+ * vocab) into the argmax_row token per row (all-NaN -> 0).  Host arrays. */
+int focr_top1_combine(const float *vals, const int32_t *idx, size_t shards,
+                      size_t m, uint32_t *token);
+
+/* ---- runtime self-test (dispatch.rs:340-431, `focr robot selftest`) --- */
+
+/* Runs the reference's selftest battery (12 shapes x {s8s8, u8s8}) on the
+ * GPU tier against a host scalar check.  Writes a JSON report into buf
+ * (truncated to buflen) and *all_ok.  Returns FOCR_OK if it ran. */
+int focr_selftest(char *buf, size_t buflen, int *all_ok);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

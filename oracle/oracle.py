@@ -1,0 +1,247 @@
+"""ctypes wrapper of the CPU oracle (``oracle/_build/libfocr_oracle.so``).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, ``__graft_entry__.smoke()`` and
+the CPU-baseline legs of bench.py -- never by the product package.  The C
+sources (focr_oracle.c, cpu_baseline.c) restate the reference's Rust with
+file:line citations; ``make -C oracle`` builds the library.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "_build" / "libfocr_oracle.so"
+
+
+def build() -> Path:
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    return LIB_PATH
+
+
+if not LIB_PATH.exists():
+    build()
+lib = C.CDLL(str(LIB_PATH))
+vp, sz = C.c_void_p, C.c_size_t
+
+
+class MoeLayerC(C.Structure):
+    _fields_ = [
+        ("hidden", sz), ("inter", sz), ("n_experts", sz), ("topk", sz), ("shared_inter", sz),
+        ("norm_topk_prob", C.c_int), ("routed_scaling_factor", C.c_float),
+        ("router", vp), ("gate_w", vp), ("gate_s", vp), ("up_w", vp), ("up_s", vp),
+        ("down_w", vp), ("down_s", vp),
+        ("sh_gate_w", vp), ("sh_gate_s", vp), ("sh_up_w", vp), ("sh_up_s", vp),
+        ("sh_down_w", vp), ("sh_down_s", vp),
+        ("group", sz), ("gate_p", vp), ("gate_gs", vp), ("up_p", vp), ("up_gs", vp),
+        ("down_p", vp), ("down_gs", vp),
+    ]
+
+
+lib.oracle_sign_extend_nibble.restype = C.c_int8
+lib.oracle_sign_extend_nibble.argtypes = [C.c_uint8]
+lib.oracle_quantize_row_i8.restype = C.c_float
+lib.oracle_quantize_row_i8_te.restype = C.c_float
+lib.oracle_silu.restype = C.c_float
+lib.oracle_silu.argtypes = [C.c_float]
+lib.oracle_argmax_row.restype = C.c_uint32
+lib.oracle_cpu_tier.restype = C.c_char_p
+for _f in ("oracle_igemm_s8s8", "oracle_igemm_u8s8", "oracle_cpu_igemm_s8s8"):
+    getattr(lib, _f).argtypes = [vp, vp, sz, sz, sz, vp]
+lib.oracle_cpu_igemm_s8s8_mt.argtypes = [vp, vp, sz, sz, sz, vp, C.c_int]
+lib.oracle_unpack_to_i8.argtypes = [vp, sz, sz, vp]
+lib.oracle_igemm_s4s8_packed.argtypes = [vp, vp, vp, sz, sz, sz, sz, vp]
+lib.oracle_quantize_row_i8.argtypes = [vp, sz, vp]
+lib.oracle_quantize_row_i8_te.argtypes = [vp, sz, vp]
+lib.oracle_quantize_int8_weights.argtypes = [vp, sz, sz, vp, vp]
+lib.oracle_pack_int4.argtypes = [vp, sz, sz, sz, vp, vp]
+lib.oracle_gemv_i8_prequant.argtypes = [vp, C.c_float, vp, vp, sz, sz, vp]
+lib.oracle_gemv_i8.argtypes = [vp, vp, vp, sz, sz, vp]
+lib.oracle_expert_i8.argtypes = [vp, sz, sz, vp, vp, vp, vp, vp, vp, vp]
+lib.oracle_router_logits.argtypes = [vp, sz, vp, sz, vp]
+lib.oracle_route.argtypes = [vp, sz, sz, vp, sz, sz, C.c_int, C.c_float, vp, vp]
+lib.oracle_moe_decode.argtypes = [C.POINTER(MoeLayerC), vp, sz, vp, vp, vp]
+lib.oracle_moe_decode_routed.argtypes = [C.POINTER(MoeLayerC), vp, sz, vp, vp, vp]
+lib.oracle_cpu_moe_decode.argtypes = [C.POINTER(MoeLayerC), vp, sz, vp, vp, vp, C.c_int]
+lib.oracle_vocab_tile_ranges.argtypes = [sz, sz, vp, vp]
+lib.oracle_argmax_row.argtypes = [vp, sz]
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data
+
+
+def _c(a, dt):
+    return np.ascontiguousarray(a, dtype=dt)
+
+
+def igemm_s8s8(a, b, m, k, n, out):
+    lib.oracle_igemm_s8s8(_p(a), _p(b), m, k, n, _p(out))
+
+
+def igemm_u8s8(a, b, m, k, n, out):
+    lib.oracle_igemm_u8s8(_p(a), _p(b), m, k, n, _p(out))
+
+
+def cpu_igemm_s8s8(a, b, m, k, n, out, threads=1):
+    if threads == 1:
+        lib.oracle_cpu_igemm_s8s8(_p(a), _p(b), m, k, n, _p(out))
+    else:
+        lib.oracle_cpu_igemm_s8s8_mt(_p(a), _p(b), m, k, n, _p(out), threads)
+
+
+def cpu_tier() -> str:
+    return lib.oracle_cpu_tier().decode()
+
+
+def sign_extend_nibble(n: int) -> int:
+    return int(lib.oracle_sign_extend_nibble(n))
+
+
+def unpack_to_i8(packed, n, k):
+    out = np.empty(n * k, np.int8)
+    lib.oracle_unpack_to_i8(_p(_c(packed, np.uint8)), n, k, _p(out))
+    return out
+
+
+def igemm_s4s8_packed(a, b_packed, scales, group, m, k, n):
+    out = np.empty(m * n, np.float32)
+    lib.oracle_igemm_s4s8_packed(_p(_c(a, np.int8)), _p(_c(b_packed, np.uint8)),
+                                 _p(_c(scales, np.float32)), group, m, k, n, _p(out))
+    return out
+
+
+def quantize_row_i8(x, ties_even=False):
+    x = _c(x, np.float32)
+    q = np.empty(x.size, np.int8)
+    f = lib.oracle_quantize_row_i8_te if ties_even else lib.oracle_quantize_row_i8
+    s = f(_p(x), x.size, _p(q))
+    return q, np.float32(s)
+
+
+def quantize_int8_weights(w):
+    w = _c(w, np.float32)
+    n, k = w.shape
+    q = np.empty((n, k), np.int8)
+    s = np.empty(n, np.float32)
+    lib.oracle_quantize_int8_weights(_p(w), n, k, _p(q), _p(s))
+    return q, s
+
+
+def pack_int4(w, group):
+    w = _c(w, np.float32)
+    n, k = w.shape
+    p = np.empty((n, k // 2), np.uint8)
+    s = np.empty((n, k // group), np.float32)
+    lib.oracle_pack_int4(_p(w), n, k, group, _p(p), _p(s))
+    return p, s
+
+
+def silu(x: float) -> float:
+    return float(lib.oracle_silu(x))
+
+
+def gemv_i8(x, w, ws):
+    x, w, ws = _c(x, np.float32), _c(w, np.int8), _c(ws, np.float32)
+    n, k = w.shape
+    y = np.empty(n, np.float32)
+    lib.oracle_gemv_i8(_p(x), _p(w), _p(ws), n, k, _p(y))
+    return y
+
+
+def expert_i8(x, gw, gs, uw, us, dw, ds):
+    H = x.size
+    I = gw.shape[0]
+    y = np.empty(H, np.float32)
+    lib.oracle_expert_i8(_p(_c(x, np.float32)), H, I, _p(_c(gw, np.int8)), _p(_c(gs, np.float32)),
+                         _p(_c(uw, np.int8)), _p(_c(us, np.float32)), _p(_c(dw, np.int8)),
+                         _p(_c(ds, np.float32)), _p(y))
+    return y
+
+
+def router_logits(x, gate):
+    x, gate = _c(x, np.float32), _c(gate, np.float32)
+    E, H = gate.shape
+    out = np.empty(E, np.float32)
+    lib.oracle_router_logits(_p(x), H, _p(gate), E, _p(out))
+    return out
+
+
+def route(x, gate, topk=6, norm_topk_prob=False, scaling=1.0):
+    """Returns (rc, idx [n,topk], w [n,topk]); rc < 0 mirrors the reference's
+    'no finite router score' error."""
+    x, gate = _c(x, np.float32), _c(gate, np.float32)
+    n, H = x.shape
+    E = gate.shape[0]
+    idx = np.zeros((n, topk), np.int32)
+    w = np.zeros((n, topk), np.float32)
+    rc = lib.oracle_route(_p(x), n, H, _p(gate), E, topk, int(norm_topk_prob), float(scaling),
+                          _p(idx), _p(w))
+    return rc, idx, w
+
+
+class MoeOracle:
+    """Oracle view of a synth.MoeWeightsHost (all experts must be present)."""
+
+    def __init__(self, W, norm_topk_prob=True, scaling=1.0):
+        self.W = W
+        self._keep = []
+        L = MoeLayerC()
+        L.hidden, L.inter, L.n_experts, L.topk = W.hidden, W.inter, W.n_experts, W.topk
+        L.shared_inter = W.shared_inter
+        L.norm_topk_prob = int(norm_topk_prob)
+        L.routed_scaling_factor = scaling
+        L.group = W.group
+        self._set(L, "router", W.router)
+        for name, arr in W.arrays.items():
+            self._set(L, name, arr)
+        self.L = L
+
+    def _set(self, L, name, arr):
+        arr = np.ascontiguousarray(arr)
+        self._keep.append(arr)
+        setattr(L, name, arr.ctypes.data)
+
+    def decode(self, x):
+        x = _c(x, np.float32)
+        m = x.shape[0]
+        y = np.empty((m, self.W.hidden), np.float32)
+        idx = np.empty((m, self.W.topk), np.int32)
+        w = np.empty((m, self.W.topk), np.float32)
+        rc = lib.oracle_moe_decode(C.byref(self.L), _p(x), m, _p(y), _p(idx), _p(w))
+        return rc, y, idx, w
+
+    def forward(self, x, idx, w):
+        x = _c(x, np.float32)
+        m = x.shape[0]
+        y = np.empty((m, self.W.hidden), np.float32)
+        rc = lib.oracle_moe_decode_routed(C.byref(self.L), _p(x), m, _p(_c(idx, np.int32)),
+                                          _p(_c(w, np.float32)), _p(y))
+        assert rc == 0, rc
+        return y
+
+    def cpu_forward(self, x, idx, w, threads):
+        """The timed CPU baseline (restated AVX-512-VNNI tier + threaded driver)."""
+        x = _c(x, np.float32)
+        m = x.shape[0]
+        y = np.empty((m, self.W.hidden), np.float32)
+        rc = lib.oracle_cpu_moe_decode(C.byref(self.L), _p(x), m, _p(_c(idx, np.int32)),
+                                       _p(_c(w, np.float32)), _p(y), threads)
+        assert rc == 0, rc
+        return y
+
+
+def vocab_tile_ranges(n, tiles):
+    t = max(1, min(tiles, max(n, 1)))
+    s = np.empty(t, np.uint64)
+    e = np.empty(t, np.uint64)
+    lib.oracle_vocab_tile_ranges(n, tiles, _p(s), _p(e))
+    return list(zip(s.tolist(), e.tolist()))
+
+
+def argmax_row(v):
+    v = _c(v, np.float32)
+    return int(lib.oracle_argmax_row(_p(v), v.size))
