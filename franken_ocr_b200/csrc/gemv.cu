@@ -158,7 +158,7 @@ int launch_igemm(const void *A, bool au8, const int8_t *B, size_t M, size_t K, s
                  int32_t *out, cudaStream_t st) {
     if (M == 0 || N == 0) return FOCR_OK;
     if (K == 0) return FOCR_OK;  // every dot is empty: out += 0
-    if (tc_igemm_eligible(A, B, M, K, N, out)) return launch_tc_igemm(A, au8, B, M, K, N, out, st);
+    if (!au8 && tc_igemm_eligible(A, B, M, K, N, out)) return launch_tc_igemm(A, au8, B, M, K, N, out, st);
     if (K > (size_t)INT32_MAX || N > (size_t)INT32_MAX)
         return fail(FOCR_E_UNSUPPORTED, "igemm: dimension exceeds int32 range");
     for (size_t m0 = 0; m0 < M; m0 += 8) {

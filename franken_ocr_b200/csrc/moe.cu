@@ -7,6 +7,7 @@
 // once per call, whatever the number of tokens routed to it) -> per-pair
 // activation requantisation -> down GEMV (weight row read once) writing the
 // weighted partial p_j -> slot-ordered combine + shared expert.
+#include <cstdlib>
 #include <cstring>
 
 #include "gemv.cuh"
@@ -392,6 +393,14 @@ static MoeDev make_dev(focr_moe_layer *L, int T, const float *w, float *part) {
 
 static int moe_grid() { return num_sms() * 8; }
 
+void launch_act_quant(focr_moe_layer *L, int m, cudaStream_t st) {
+    act_quant_kernel<<<m * L->cfg.topk, 256, 0, st>>>(L->act, L->cfg.inter, L->offsets + L->E,
+                                                      L->aq, L->as2);
+    if (L->cfg.shared_inter)
+        act_quant_kernel<<<m, 256, 0, st>>>(L->sh_act, L->cfg.shared_inter, nullptr, L->sh_aq,
+                                            L->sh_as);
+}
+
 int moe_route_dev(focr_moe_layer *L, const float *x, int m, int32_t *idx, float *w,
                   cudaStream_t st) {
     const int E = L->cfg.n_experts, H = L->cfg.hidden;
@@ -412,12 +421,15 @@ int moe_forward_dev(focr_moe_layer *L, const float *x, int m, const int32_t *idx
     if (rc) return rc;
     bucket_kernel<<<1, 1024, 0, st>>>(idx, m, K, L->E, L->cfg.expert_begin, L->offsets,
                                       L->pair_tok, L->pair_slot);
-    MoeDev d = make_dev(L, m, w, L->part);
-    expert_gateup_kernel<<<moe_grid(), MOE_THREADS, 0, st>>>(d);
-    act_quant_kernel<<<m * K, 256, 0, st>>>(L->act, L->cfg.inter, L->offsets + L->E, L->aq, L->as2);
-    if (L->cfg.shared_inter)
-        act_quant_kernel<<<m, 256, 0, st>>>(L->sh_act, L->cfg.shared_inter, nullptr, L->sh_aq, L->sh_as);
-    expert_down_kernel<<<moe_grid(), MOE_THREADS, 0, st>>>(d);
+    if (L->tc_state) {
+        rc = moe_tc_experts(L, m, w, st);
+        if (rc) return rc;
+    } else {
+        MoeDev d = make_dev(L, m, w, L->part);
+        expert_gateup_kernel<<<moe_grid(), MOE_THREADS, 0, st>>>(d);
+        launch_act_quant(L, m, st);
+        expert_down_kernel<<<moe_grid(), MOE_THREADS, 0, st>>>(d);
+    }
     dim3 gc((H + 255) / 256, m);
     combine_kernel<<<gc, 256, 0, st>>>(L->part, L->cfg.shared_inter ? L->sh_y : nullptr, H, K, y);
     FOCR_CUDA_TRY(cudaGetLastError());
@@ -461,13 +473,14 @@ extern "C" {
 
 int focr_moe_destroy(focr_moe_layer *L) {
     if (!L) return FOCR_OK;
+    if (L->tc_state) moe_tc_free(L);
     void *ptrs[] = {L->router, L->gate_w, L->up_w, L->down_w, L->gate_s, L->up_s, L->down_s,
                     L->gate_p, L->up_p, L->down_p, L->gate_gs, L->up_gs, L->down_gs,
                     L->sh_gate_w, L->sh_up_w, L->sh_down_w, L->sh_gate_s, L->sh_up_s,
                     L->sh_down_s, L->x, L->y, L->idx, L->w, L->logits, L->xq, L->xs,
                     L->counts, L->offsets, L->pair_tok, L->pair_slot, L->act, L->amax, L->aq,
                     L->as2, L->part, L->sh_act, L->sh_amax, L->sh_as, L->sh_y, L->sh_aq, L->err,
-                    L->sync};
+                    L->sync, L->xq_sorted, L->xs_sorted};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     delete L;
@@ -513,7 +526,7 @@ int focr_moe_create(const focr_moe_config *cfg, const focr_moe_weights *wt,
         TRY(dev_upload(&L->sh_up_s, wt->sh_up_s, S));
         TRY(dev_upload(&L->sh_down_s, wt->sh_down_s, H));
         TRY(dev_alloc(&L->sh_act, T * S));
-        TRY(dev_alloc(&L->sh_aq, T * S));
+        TRY(dev_alloc(&L->sh_aq, (T < 128 ? 128 : T) * S));
         TRY(dev_alloc(&L->sh_as, T));
         TRY(dev_alloc(&L->sh_amax, T));
         TRY(dev_alloc(&L->sh_y, T * H));
@@ -523,7 +536,7 @@ int focr_moe_create(const focr_moe_config *cfg, const focr_moe_weights *wt,
     TRY(dev_alloc(&L->idx, P));
     TRY(dev_alloc(&L->w, P));
     TRY(dev_alloc(&L->logits, T * c.n_experts));
-    TRY(dev_alloc(&L->xq, T * H));
+    TRY(dev_alloc(&L->xq, (T < 128 ? 128 : T) * H));
     TRY(dev_alloc(&L->xs, T));
     TRY(dev_alloc(&L->counts, E + 1));
     TRY(dev_alloc(&L->offsets, E + 2));
@@ -531,11 +544,18 @@ int focr_moe_create(const focr_moe_config *cfg, const focr_moe_weights *wt,
     TRY(dev_alloc(&L->pair_slot, P));
     TRY(dev_alloc(&L->act, P * I));
     TRY(dev_alloc(&L->amax, P));
-    TRY(dev_alloc(&L->aq, P * I));
+    TRY(dev_alloc(&L->aq, (P < 128 ? 128 : P) * I));
     TRY(dev_alloc(&L->as2, P));
     TRY(dev_alloc(&L->part, T * K * H));
     TRY(dev_alloc(&L->err, 4));
     TRY(dev_alloc(&L->sync, 64));
+    TRY(dev_alloc(&L->xq_sorted, (P < 128 ? 128 : P) * H));
+    TRY(dev_alloc(&L->xs_sorted, P));
+    // Tensor-core expert path: every TMA box (128 rows x 128 bytes) fits inside
+    // its tensor when hidden/inter/shared_inter are multiples of 128 (all model
+    // shapes are); other shapes use the GEMV-grouped kernels.
+    if (!getenv("FOCR_DISABLE_TC") && H % 128 == 0 && I % 128 == 0 && S % 128 == 0)
+        TRY(moe_tc_setup(L));
     L->fused_ok = moe_fused_eligible(L) ? 1 : 0;
     *out = L;
     return FOCR_OK;

@@ -32,6 +32,9 @@ struct focr_moe_layer {
     float *part = nullptr;                         // [T][topk][H]
     float *sh_act = nullptr, *sh_amax = nullptr, *sh_as = nullptr, *sh_y = nullptr;
     int8_t *sh_aq = nullptr;
+    int8_t *xq_sorted = nullptr;                   // [P][H] token rows in pair order
+    float *xs_sorted = nullptr;                    // [P]
+    void *tc_state = nullptr;                      // tensor-core path (tensor maps)
     int32_t *err = nullptr;                        // device status word
     // fused M=1 path
     unsigned int *sync = nullptr;                  // grid-barrier counters
@@ -47,5 +50,9 @@ int moe_forward_dev(focr_moe_layer *L, const float *x, int m, const int32_t *idx
 int moe_decode_fused_m1(focr_moe_layer *L, const float *x, float *y, int32_t *idx, float *w,
                         cudaStream_t st);
 bool moe_fused_eligible(const focr_moe_layer *L);
+int moe_tc_setup(focr_moe_layer *L);
+void moe_tc_free(focr_moe_layer *L);
+int moe_tc_experts(focr_moe_layer *L, int m, const float *w, cudaStream_t st);
+void launch_act_quant(focr_moe_layer *L, int m, cudaStream_t st);
 
 }  // namespace focr

@@ -1,15 +1,132 @@
-// tcgen05 int8 GEMM for M >= 64 (placeholder: the GEMV family serves all M).
-#include "common.cuh"
+// tcgen05 int8 GEMM for igemm_s8s8 at M >= 64 (simd/dispatch.rs:246
+// contract: out[M,N] += A[M,K] . B[N,K]^T in int32).
+//
+// Tile 128 (rows of A, MMA M) x BN (rows of B, MMA N) x 128 bytes of K per
+// stage; the epilogue adds the TMEM accumulator onto `out`.  BN is chosen per
+// call so the grid covers the 148 SMs; CTAs are ordered with the A tile
+// fastest so the CTAs that share one B (weight) tile run together and re-read
+// it from L2.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "tc_kernel.cuh"
 
 namespace focr {
 
-bool tc_igemm_eligible(const void *, const int8_t *, size_t, size_t, size_t, const int32_t *) {
-    return false;
+int make_tmap_i8(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
+                 uint32_t box_rows) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void *fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    if (!encode) return fail(FOCR_E_CUDA, "cuTensorMapEncodeTiled unavailable");
+    if (cols % 16 || (uintptr_t)base % 16 || rows == 0)
+        return fail(FOCR_E_ARG, "tensor map: base/cols must be 16-byte aligned");
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols};
+    cuuint32_t box[2] = {128, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(FOCR_E_CUDA, "cuTensorMapEncodeTiled failed");
+    return FOCR_OK;
 }
 
-int launch_tc_igemm(const void *, bool, const int8_t *, size_t, size_t, size_t, int32_t *,
-                    cudaStream_t) {
-    return fail(FOCR_E_UNSUPPORTED, "tcgen05 igemm not available");
+template <int BN_, int STAGES_>
+struct RawIgemm {
+    static constexpr int NA = 1, BN = BN_, STAGES = STAGES_;
+    CUtensorMap ta, tb;
+    int M, N, K, mtiles;
+    int32_t *out;
+    int *err;
+
+    __device__ bool job(int j, TcJob &jb) const {
+        if (j > 0) return false;
+        const int mt = blockIdx.x % mtiles, nt = blockIdx.x / mtiles;
+        jb.a[0] = &ta;
+        jb.a[1] = nullptr;
+        jb.b = &tb;
+        jb.a_row = mt * 128;
+        jb.b_row = nt * BN;
+        jb.kblocks = (K + tc::BK - 1) / tc::BK;
+        const int nv = min(BN, N - nt * BN);
+        jb.n_mma = (nv + 15) & ~15;
+        jb.t0 = nv;
+        return true;
+    }
+
+    __device__ void epilogue(const TcJob &jb, uint32_t tmem, int q, int lane) const {
+        const int row = jb.a_row + 32 * q + lane;
+        const int nv = jb.t0;
+        int32_t *orow = out + (size_t)row * N + jb.b_row;
+        for (int c0 = 0; c0 < nv; c0 += 16) {
+            int v[16];
+            tc::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + c0, v);
+            tc::tmem_ld_wait();
+            if (row < M) {
+#pragma unroll
+                for (int c = 0; c < 16; c++)
+                    if (c0 + c < nv) orow[c0 + c] += v[c];
+            }
+        }
+    }
+};
+
+bool tc_igemm_eligible(const void *A, const int8_t *B, size_t M, size_t K, size_t N,
+                       const int32_t *out) {
+    (void)out;
+    if (getenv("FOCR_DISABLE_TC")) return false;
+    // every TMA box (128 rows of A, >= 64 rows of B, 128 bytes of K) fits inside its tensor
+    return M >= 128 && N >= 64 && K >= 128 && K % 16 == 0 && (uintptr_t)A % 16 == 0 &&
+           (uintptr_t)B % 16 == 0 && M <= (size_t)INT32_MAX / 2 && N <= (size_t)INT32_MAX / 2 &&
+           K <= (size_t)INT32_MAX / 2;
+}
+
+template <int BN, int S>
+static int run_raw(const void *A, const int8_t *B, size_t M, size_t K, size_t N, int32_t *out,
+                   int *err, cudaStream_t st) {
+    RawIgemm<BN, S> p;
+    int rc = make_tmap_i8(&p.ta, A, M, K, 128);
+    if (!rc) rc = make_tmap_i8(&p.tb, B, N, K, BN);
+    if (rc) return rc;
+    p.M = (int)M;
+    p.N = (int)N;
+    p.K = (int)K;
+    p.mtiles = (int)((M + 127) / 128);
+    p.out = out;
+    p.err = err;
+    const long grid = (long)p.mtiles * (long)((N + BN - 1) / BN);
+    if (grid > INT32_MAX) return fail(FOCR_E_UNSUPPORTED, "igemm: grid too large");
+    return launch_tc(p, (int)grid, st);
+}
+
+static int *tc_status_word() {
+    static int *w = nullptr;
+    if (!w) cudaMalloc(&w, sizeof(int) * 64);
+    return w;
+}
+
+int launch_tc_igemm(const void *A, bool au8, const int8_t *B, size_t M, size_t K, size_t N,
+                    int32_t *out, cudaStream_t st) {
+    if (au8) return fail(FOCR_E_UNSUPPORTED, "tc igemm: u8 activations use the GEMV tier");
+    int *err = tc_status_word();
+    const size_t mt = (M + 127) / 128;
+    const int sms = num_sms();
+    // widest tile that still gives every SM a CTA
+    if (N >= 256 && mt * ((N + 255) / 256) >= (size_t)sms)
+        return run_raw<256, 4>(A, B, M, K, N, out, err, st);
+    if (N >= 128 && mt * ((N + 127) / 128) >= (size_t)sms)
+        return run_raw<128, 6>(A, B, M, K, N, out, err, st);
+    return run_raw<64, 8>(A, B, M, K, N, out, err, st);
 }
 
 }  // namespace focr

@@ -173,3 +173,37 @@ def test_lmhead_shards_and_argmax(cuda, oracle):
     tok = top1_combine(np.stack(vals), np.stack(idxs))
     assert tok.tolist() == fi.astype(np.uint32).tolist()
     full.close()
+
+
+def test_forward_gemv_grouped_path(cuda, oracle, layer2, monkeypatch):
+    """The dp4a GEMV-grouped expert kernels (used when the tensor-core path is
+    disabled or the shapes are not multiples of 128) at m = 64."""
+    from franken_ocr_b200 import synth
+    from franken_ocr_b200.moe import MoeLayer
+    from oracle.oracle import MoeOracle
+
+    monkeypatch.setenv("FOCR_DISABLE_TC", "1")
+    m = 64
+    L = MoeLayer(layer2, max_tokens=m)
+    x = synth.hidden_states(22, m)
+    idx, w = synth.zipf_routing(22, m)
+    y = L.forward(x, idx, w)
+    assert_close_rel(y, MoeOracle(layer2).forward(x, idx, w), "gemv-grouped forward m=64")
+    L.close()
+
+
+@pytest.mark.parametrize("m", [2, 17, 128, 300])
+def test_forward_tc_token_counts(cuda, oracle, m):
+    """Tensor-core expert path across token counts, incl. experts with more
+    than 128 tokens (several N jobs per CTA) and uniform routing."""
+    from franken_ocr_b200 import synth
+    from franken_ocr_b200.moe import MoeLayer
+    from oracle.oracle import MoeOracle
+
+    W = synth.moe_layer(77, n_experts=8, shared_inter=256, inter=256)
+    L = MoeLayer(W, max_tokens=m)
+    x = synth.hidden_states(m, m)
+    idx, w = synth.zipf_routing(m, m, n_experts=8)
+    y = L.forward(x, idx, w)
+    assert_close_rel(y, MoeOracle(W).forward(x, idx, w), f"tc forward m={m}")
+    L.close()
