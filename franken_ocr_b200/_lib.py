@@ -25,7 +25,7 @@ MEM_DEVICE = 1
 # Every symbol declared in include/focr_cuda.h.
 EXPORTS = [
     "focr_last_error", "focr_tier_string", "focr_igemm_s8s8", "focr_igemm_u8s8",
-    "focr_igemm_s4s8_packed", "focr_quantize_rows_i8", "focr_gemv_i8",
+    "focr_igemm_s4s8_packed", "focr_quantize_rows_i8", "focr_gemv_i8", "focr_gemv_i8_noalloc",
     "focr_moe_create", "focr_moe_destroy", "focr_moe_route", "focr_moe_forward",
     "focr_moe_decode", "focr_lmhead_create", "focr_lmhead_destroy", "focr_lmhead_top1",
     "focr_top1_combine", "focr_selftest",
@@ -76,6 +76,7 @@ for _name in ("focr_igemm_s8s8", "focr_igemm_u8s8"):
 lib.focr_igemm_s4s8_packed.argtypes = [vp, sz, vp, sz, vp, sz, sz, sz, sz, sz, vp, sz, i32, vp]
 lib.focr_quantize_rows_i8.argtypes = [vp, sz, sz, i32, vp, vp, i32, vp]
 lib.focr_gemv_i8.argtypes = [vp, sz, sz, vp, vp, sz, vp, i32, vp]
+lib.focr_gemv_i8_noalloc.argtypes = [vp, sz, sz, vp, vp, sz, vp, vp]
 lib.focr_moe_create.argtypes = [C.POINTER(MoeConfig), C.POINTER(MoeWeights), C.POINTER(vp)]
 lib.focr_moe_destroy.argtypes = [vp]
 lib.focr_moe_route.argtypes = [vp, vp, sz, vp, vp, i32, vp]

@@ -87,6 +87,19 @@ int focr_quantize_rows_i8(const float *x, size_t m, size_t k, int ties_even,
 int focr_gemv_i8(const float *x, size_t m, size_t k, const int8_t *w,
                  const float *w_scale, size_t n, float *y, int mem, void *stream);
 
+/* focr_gemv_i8 without any allocation.  No counterpart in the reference: it
+ * exists for callers that cannot allocate device memory (an embedder whose
+ * GPU memory belongs to its own pool allocator, or code where an allocation
+ * would block or is not allowed).  Same result as focr_gemv_i8; all pointers
+ * are device memory on the current device, work is enqueued on `stream`.
+ * Scratch is a fixed ~260 KB array inside the library (held by every GPU that
+ * loads it until exit), so m*k <= 262144 and m <= 1024, otherwise
+ * FOCR_E_SHAPE.  The first call on a device looks up that array's device
+ * address (cudaGetSymbolAddress); make it before any stream capture.  Calls
+ * share the array: calls that overlap on the GPU race. */
+int focr_gemv_i8_noalloc(const float *x, size_t m, size_t k, const int8_t *w,
+                         const float *w_scale, size_t n, float *y, void *stream);
+
 /* ---- MoE layer (native_engine/moe.rs + decoder.rs:2199-2268) ----------- */
 
 typedef struct focr_moe_config {
