@@ -46,6 +46,33 @@ struct DevBuf {
     }
 };
 
+// ---- programmatic dependent launch ----------------------------------------
+// Kernels of one forward are launched with programmatic stream serialisation:
+// a kernel may be scheduled while its predecessor drains, runs its prologue
+// (barrier init, TMEM allocation), and calls pdl_wait() -- which returns once
+// the predecessor grid has completed and its memory is visible -- before it
+// touches any global memory.  pdl_trigger() lets the successor be scheduled.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // ---- device numerics -----------------------------------------------------
 
 // expf with the result rounded from CUDA's double-precision exp (relative

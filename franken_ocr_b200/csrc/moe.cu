@@ -350,6 +350,8 @@ __global__ void __launch_bounds__(MOE_THREADS) expert_down_kernel(MoeDev d) {
 // out = (((0 + p_0) + p_1) + ... + p_{k-1}) + s   (decoder.rs:2253-2261)
 __global__ void combine_kernel(const float *__restrict__ part, const float *__restrict__ sh_y,
                                int H, int topk, float *__restrict__ y) {
+    pdl_wait();
+    pdl_trigger();
     const int t = blockIdx.y;
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= H) return;
@@ -415,24 +417,25 @@ int moe_route_dev(focr_moe_layer *L, const float *x, int m, int32_t *idx, float 
 int moe_forward_dev(focr_moe_layer *L, const float *x, int m, const int32_t *idx,
                     const float *w, float *y, cudaStream_t st) {
     const int H = L->cfg.hidden, K = L->cfg.topk;
-    check_idx_kernel<<<1, 256, 0, st>>>(idx, m * K, (int)L->cfg.expert_begin,
-                                        (int)(L->cfg.expert_begin + L->E), L->err);
-    int rc = launch_quantize_rows(x, m, H, false, L->xq, L->xs, st);
-    if (rc) return rc;
-    bucket_kernel<<<1, 1024, 0, st>>>(idx, m, K, L->E, L->cfg.expert_begin, L->offsets,
-                                      L->pair_tok, L->pair_slot);
+    int rc;
     if (L->tc_state) {
-        rc = moe_tc_experts(L, m, w, st);
+        rc = moe_tc_experts(L, x, m, idx, w, st);
         if (rc) return rc;
     } else {
+        check_idx_kernel<<<1, 256, 0, st>>>(idx, m * K, (int)L->cfg.expert_begin,
+                                            (int)(L->cfg.expert_begin + L->E), L->err);
+        rc = launch_quantize_rows(x, m, H, false, L->xq, L->xs, st);
+        if (rc) return rc;
+        bucket_kernel<<<1, 1024, 0, st>>>(idx, m, K, L->E, L->cfg.expert_begin, L->offsets,
+                                          L->pair_tok, L->pair_slot);
         MoeDev d = make_dev(L, m, w, L->part);
         expert_gateup_kernel<<<moe_grid(), MOE_THREADS, 0, st>>>(d);
         launch_act_quant(L, m, st);
         expert_down_kernel<<<moe_grid(), MOE_THREADS, 0, st>>>(d);
     }
     dim3 gc((H + 255) / 256, m);
-    combine_kernel<<<gc, 256, 0, st>>>(L->part, L->cfg.shared_inter ? L->sh_y : nullptr, H, K, y);
-    FOCR_CUDA_TRY(cudaGetLastError());
+    FOCR_CUDA_TRY(launch_pdl(combine_kernel, gc, dim3(256), 0, st, (const float *)L->part,
+                             (const float *)(L->cfg.shared_inter ? L->sh_y : nullptr), H, K, y));
     return FOCR_OK;
 }
 

@@ -52,7 +52,8 @@ int moe_decode_fused_m1(focr_moe_layer *L, const float *x, float *y, int32_t *id
 bool moe_fused_eligible(const focr_moe_layer *L);
 int moe_tc_setup(focr_moe_layer *L);
 void moe_tc_free(focr_moe_layer *L);
-int moe_tc_experts(focr_moe_layer *L, int m, const float *w, cudaStream_t st);
+int moe_tc_experts(focr_moe_layer *L, const float *x, int m, const int32_t *idx, const float *w,
+                   cudaStream_t st);
 void launch_act_quant(focr_moe_layer *L, int m, cudaStream_t st);
 
 }  // namespace focr

@@ -44,17 +44,27 @@ int make_tmap_i8(CUtensorMap *map, const void *base, uint64_t rows, uint64_t col
 template <int BN_, int STAGES_>
 struct RawIgemm {
     static constexpr int NA = 1, BN = BN_, STAGES = STAGES_;
+    struct Iter {
+        long tile;
+    };
     CUtensorMap ta, tb;
     int M, N, K, mtiles;
+    long ntiles;
     int32_t *out;
     int *err;
 
-    __device__ bool job(int j, TcJob &jb) const {
-        if (j > 0) return false;
-        const int mt = blockIdx.x % mtiles, nt = blockIdx.x / mtiles;
+    __device__ void iter_init(Iter &it) const { it.tile = blockIdx.x; }
+
+    // Persistent: CTA c takes tiles c, c + grid, ...; the A (activation) tile
+    // index runs fastest so concurrently running CTAs share one B tile in L2.
+    __device__ bool iter_next(Iter &it, TcJob &jb) const {
+        if (it.tile >= ntiles) return false;
+        const int mt = (int)(it.tile % mtiles), nt = (int)(it.tile / mtiles);
+        it.tile += gridDim.x;
         jb.a[0] = &ta;
         jb.a[1] = nullptr;
         jb.b = &tb;
+        jb.b_box = BN;
         jb.a_row = mt * 128;
         jb.b_row = nt * BN;
         jb.kblocks = (K + tc::BK - 1) / tc::BK;
@@ -104,9 +114,9 @@ static int run_raw(const void *A, const int8_t *B, size_t M, size_t K, size_t N,
     p.mtiles = (int)((M + 127) / 128);
     p.out = out;
     p.err = err;
-    const long grid = (long)p.mtiles * (long)((N + BN - 1) / BN);
-    if (grid > INT32_MAX) return fail(FOCR_E_UNSUPPORTED, "igemm: grid too large");
-    return launch_tc(p, (int)grid, st);
+    p.ntiles = (long)p.mtiles * (long)((N + BN - 1) / BN);
+    const long sms = num_sms();
+    return launch_tc(p, (int)(p.ntiles < sms ? p.ntiles : sms), st);
 }
 
 static int *tc_status_word() {
