@@ -28,7 +28,7 @@ EXPORTS = [
     "focr_igemm_s4s8_packed", "focr_quantize_rows_i8", "focr_gemv_i8", "focr_gemv_i8_noalloc",
     "focr_moe_create", "focr_moe_destroy", "focr_moe_route", "focr_moe_forward",
     "focr_moe_decode", "focr_lmhead_create", "focr_lmhead_destroy", "focr_lmhead_top1",
-    "focr_top1_combine", "focr_selftest",
+    "focr_top1_combine", "focr_selftest", "focr_trace_set",
 ]
 
 
@@ -87,6 +87,7 @@ lib.focr_lmhead_destroy.argtypes = [vp]
 lib.focr_lmhead_top1.argtypes = [vp, vp, sz, vp, vp, vp, i32, vp]
 lib.focr_top1_combine.argtypes = [vp, vp, sz, sz, vp]
 lib.focr_selftest.argtypes = [C.c_char_p, sz, C.POINTER(i32)]
+lib.focr_trace_set.argtypes = [vp, vp, sz]
 
 
 def check(rc: int) -> None:

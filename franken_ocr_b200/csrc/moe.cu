@@ -483,7 +483,8 @@ int focr_moe_destroy(focr_moe_layer *L) {
                     L->sh_down_s, L->x, L->y, L->idx, L->w, L->logits, L->xq, L->xs,
                     L->counts, L->offsets, L->pair_tok, L->pair_slot, L->act, L->amax, L->aq,
                     L->as2, L->part, L->sh_act, L->sh_amax, L->sh_as, L->sh_y, L->sh_aq, L->err,
-                    L->sync, L->xq_sorted, L->xs_sorted};
+                    L->sync, L->sched, L->xq_sorted, L->xs_sorted, L->gate_t, L->up_t, L->down_t,
+                    L->sh_gate_t, L->sh_up_t, L->sh_down_t};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     delete L;
@@ -552,6 +553,7 @@ int focr_moe_create(const focr_moe_config *cfg, const focr_moe_weights *wt,
     TRY(dev_alloc(&L->part, T * K * H));
     TRY(dev_alloc(&L->err, 4));
     TRY(dev_alloc(&L->sync, 64));
+    TRY(dev_alloc(&L->sched, 2));
     TRY(dev_alloc(&L->xq_sorted, (P < 128 ? 128 : P) * H));
     TRY(dev_alloc(&L->xs_sorted, P));
     // Tensor-core expert path: every TMA box (128 rows x 128 bytes) fits inside

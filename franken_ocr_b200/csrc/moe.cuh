@@ -15,6 +15,10 @@ struct focr_moe_layer {
     float *gate_gs = nullptr, *up_gs = nullptr, *down_gs = nullptr;
     int8_t *sh_gate_w = nullptr, *sh_up_w = nullptr, *sh_down_w = nullptr;
     float *sh_gate_s = nullptr, *sh_up_s = nullptr, *sh_down_s = nullptr;
+    // TMA-tiled copies for the tensor-core path: each (128-row block,
+    // 128-byte K block) of a weight matrix is one contiguous 16 KB chunk
+    int8_t *gate_t = nullptr, *up_t = nullptr, *down_t = nullptr;
+    int8_t *sh_gate_t = nullptr, *sh_up_t = nullptr, *sh_down_t = nullptr;
     // ---- scratch (sized by cfg.max_tokens = T) ----
     float *x = nullptr, *y = nullptr;              // [T][H] host-call staging
     int32_t *idx = nullptr;                        // [T][topk]
@@ -38,6 +42,7 @@ struct focr_moe_layer {
     int32_t *err = nullptr;                        // device status word
     // fused M=1 path
     unsigned int *sync = nullptr;                  // grid-barrier counters
+    int *sched = nullptr;                          // [2] tile-claim counters (gate+up, down)
     int fused_ok = 0;
 };
 

@@ -23,152 +23,295 @@ constexpr int NBOX = 3;
 __device__ __forceinline__ int box_index(int nv) { return nv <= 32 ? 0 : nv <= 64 ? 1 : 2; }
 __host__ __device__ constexpr int box_rows(int i) { return i == 0 ? 32 : i == 1 ? 64 : 128; }
 
-struct TileIter {
-    int tile, chunk;
+// ---------------------------------------------------------------------------
+// Dynamic tile scheduling shared by the two MoE GEMMs.
+//
+// The producer thread claims tiles from a global atomic counter (zeroed by
+// the prep kernel) in the problem's tile order -- heaviest first -- and
+// publishes each job (tile, token chunk) in a shared-memory ring guarded by
+// mbarriers; the MMA thread and the epilogue warps follow the ring.  The
+// epilogue warps free a ring slot when they ask for their next job, so the
+// producer never runs more than RING jobs ahead of the epilogue.  A tile
+// costs the same weight bytes wherever it runs, but epilogue work grows with
+// its token count, so claiming on demand keeps the SMs' finish times close.
+// ---------------------------------------------------------------------------
+
+constexpr int RING = 8;
+
+struct SchedSmem {
+    int32_t offsets[1025];   // expert pair offsets, staged from global
+    int32_t active[1025];    // active experts (heaviest first), [E] = count
+    int2 ring[RING];         // (tile, chunk); tile < 0 ends the sequence
+    uint64_t ready[RING];    // producer -> MMA + epilogue (count 1)
+    uint64_t freed[RING];    // epilogue -> producer (count 4)
+};
+constexpr int MOE_JOB_SMEM = (int)sizeof(SchedSmem);
+
+struct DynIter {
+    SchedSmem *sm;
+    int j;          // jobs handed out so far by this role's iterator
+    int tile, chunk, nchunks;
+    int role;       // 0 producer, 1 MMA, 2 epilogue
 };
 
+template <class P>
+__device__ void sched_stage(const P &p, void *js) {
+    SchedSmem *sm = static_cast<SchedSmem *>(js);
+    for (int i = threadIdx.x; i <= p.E; i += blockDim.x) {
+        sm->offsets[i] = p.offsets[i];
+        sm->active[i] = p.active[i];
+    }
+    if (threadIdx.x == 0) {
+        for (int r = 0; r < RING; r++) {
+            tc::mbar_init(&sm->ready[r], 1);
+            tc::mbar_init(&sm->freed[r], 4);
+        }
+        tc::fence_barrier_init();
+    }
+}
+
+template <class P>
+__device__ void sched_init(DynIter &it, void *js) {
+    it.sm = static_cast<SchedSmem *>(js);
+    it.j = 0;
+    it.tile = -1;
+    it.chunk = it.nchunks = 0;
+    it.role = threadIdx.x == 0 ? 0 : (threadIdx.x >> 5) == 1 ? 1 : 2;
+}
+
+template <class P>
+__device__ bool sched_next(const P &p, DynIter &it, TcJob &jb) {
+    SchedSmem *sm = it.sm;
+    const int slot = it.j % RING;
+    int tile, chunk;
+    if (it.role == 0) {
+        if (it.chunk >= it.nchunks) {   // claim the next tile
+            const int ntiles = p.num_tiles(sm);
+            it.tile = atomicAdd(p.sched, 1);
+            it.chunk = 0;
+            it.nchunks = it.tile < ntiles ? p.num_chunks(it.tile, sm) : 0;
+            if (it.tile >= ntiles) it.tile = -1;
+        }
+        tile = it.tile;
+        chunk = it.chunk++;
+        if (it.j >= RING && !tc::mbar_wait(&sm->freed[slot], ((it.j / RING) - 1) & 1, p.err))
+            tile = -1;
+        sm->ring[slot] = make_int2(tile, chunk);
+        tc::mbar_arrive(&sm->ready[slot]);
+    } else {
+        if (it.role == 2 && it.j > 0 && (threadIdx.x & 31) == 0)
+            tc::mbar_arrive(&sm->freed[(it.j - 1) % RING]);
+        if (!tc::mbar_wait(&sm->ready[slot], (it.j / RING) & 1, p.err)) return false;
+        const int2 r = sm->ring[slot];
+        tile = r.x;
+        chunk = r.y;
+    }
+    it.j++;
+    if (tile < 0) return false;
+    p.make_job(tile, chunk, sm, jb);
+    return true;
+}
+
+// Gate+up: the weights are stored TMA-tiled with gate and up interleaved --
+// every 128-row MMA block holds 64 gate rows followed by the same 64 up rows
+// (tile_gate_up_kernel) -- so one MMA yields g and u for 64 intermediate rows
+// and a tile is 64 intermediate rows x all of K (half the work of a
+// 128-gate + 128-up tile, which keeps the persistent CTAs balanced).
 struct MoeGateUp {
-    static constexpr int NA = 2, BN = 128, STAGES = 4;
-    using Iter = TileIter;
-    CUtensorMap tg, tu, tsg, tsu;
+    static constexpr int NA = 1, BN = 128, STAGES = 6;
+    static constexpr int EPI_SMEM = 2 * 64 * 17 * 4;   // both halves of one 16-column chunk
+    static constexpr int NBUF = 4;                      // TMEM accumulator buffers
+    static constexpr int JOB_SMEM = MOE_JOB_SMEM;
+    static constexpr uint32_t KERNEL_ID = 2;
+    TraceBuf trace;
+    CUtensorMap tgu, tsgu;
     CUtensorMap tx[NBOX], txt[NBOX];
-    int H, I, S, E, T, itiles, stiles;
+    int H, I, S, E, T, itiles, stiles;   // itiles = I / 64, stiles = S / 64
     const int32_t *offsets;
-    const int32_t *active;   // [E] local ids of experts with >= 1 pair, ascending; [E] = count
+    const int32_t *active;   // [E] local ids of experts with >= 1 pair, most pairs first; [E] = count
+    int *sched;              // tile-claim counter (zeroed by the prep kernel)
     const float *gate_s, *up_s, *sh_gate_s, *sh_up_s, *xs_sorted, *xs;
     float *act, *sh_act;
     int *err;
 
-    __device__ void iter_init(Iter &it) const {
-        it.tile = blockIdx.x;
-        it.chunk = 0;
+    __device__ void prefetch() const {
+        tc::prefetch_tmap(&tgu);
+        if (S) tc::prefetch_tmap(&tsgu);
+        for (int b = 0; b < NBOX; b++) tc::prefetch_tmap(&tx[b]);
     }
 
-    __device__ bool iter_next(Iter &it, TcJob &jb) const {
-        const int na = active[E];
-        const int ntiles = na * itiles + (S ? stiles : 0);
-        while (it.tile < ntiles) {
-            const int t = it.tile;
-            const bool routed = t < na * itiles;
-            const int e = routed ? active[t / itiles] : -1;
-            const int rt = routed ? t % itiles : t - na * itiles;
-            const int p0 = routed ? offsets[e] : 0;
-            const int cnt = routed ? offsets[e + 1] - p0 : T;
-            if (it.chunk * BN >= cnt) {
-                it.tile += gridDim.x;
-                it.chunk = 0;
-                continue;
-            }
-            const int nv = min(BN, cnt - it.chunk * BN);
-            const int bi = box_index(nv);
-            jb.a[0] = routed ? &tg : &tsg;
-            jb.a[1] = routed ? &tu : &tsu;
-            jb.b = routed ? &tx[bi] : &txt[bi];
-            jb.b_box = box_rows(bi);
-            jb.a_row = routed ? e * I + rt * 128 : rt * 128;
-            jb.b_row = p0 + it.chunk * BN;
-            jb.kblocks = (H + tc::BK - 1) / tc::BK;
-            jb.n_mma = (nv + 15) & ~15;
-            jb.t0 = e;
-            jb.t1 = rt;
-            jb.t2 = jb.b_row;
-            jb.t3 = nv;
-            it.chunk++;
-            return true;
+    using Iter = DynIter;
+    __device__ void load_job_state(void *js) const { sched_stage(*this, js); }
+    __device__ void iter_init(Iter &it, void *js) const { sched_init<MoeGateUp>(it, js); }
+    __device__ bool iter_next(Iter &it, TcJob &jb) const { return sched_next(*this, it, jb); }
+
+    // tiles: the shared expert's first (64 tokens each), then the active
+    // experts' in the prep kernel's order (most pairs first)
+    __device__ int num_tiles(const SchedSmem *sm) const {
+        return sm->active[E] * itiles + (S ? stiles : 0);
+    }
+    __device__ void tile_info(int t, const SchedSmem *sm, int &e, int &rt, int &p0,
+                              int &cnt) const {
+        const int sh = S ? stiles : 0;
+        if (t < sh) {
+            e = -1; rt = t; p0 = 0; cnt = T;
+        } else {
+            e = sm->active[(t - sh) / itiles];
+            rt = (t - sh) % itiles;
+            p0 = sm->offsets[e];
+            cnt = sm->offsets[e + 1] - p0;
         }
-        return false;
+    }
+    __device__ int num_chunks(int t, const SchedSmem *sm) const {
+        int e, rt, p0, cnt;
+        tile_info(t, sm, e, rt, p0, cnt);
+        return (cnt + BN - 1) / BN;
+    }
+    __device__ void make_job(int t, int chunk, const SchedSmem *sm, TcJob &jb) const {
+        int e, rt, p0, cnt;
+        tile_info(t, sm, e, rt, p0, cnt);
+        const bool routed = e >= 0;
+        const int nv = min(BN, cnt - chunk * BN);
+        const int bi = box_index(nv);
+        jb.a[0] = routed ? &tgu : &tsgu;
+        jb.a[1] = nullptr;
+        jb.a_kbt = (H + tc::BK - 1) / tc::BK;
+        jb.b = routed ? &tx[bi] : &txt[bi];
+        jb.b_box = box_rows(bi);
+        // 128-row block index of (expert, 64-row tile) in the interleaved array
+        jb.a_row = (routed ? e * itiles + rt : rt) * 128;
+        jb.b_row = p0 + chunk * BN;
+        jb.kblocks = (H + tc::BK - 1) / tc::BK;
+        jb.n_mma = (nv + 15) & ~15;
+        jb.t0 = e;
+        jb.t1 = rt;
+        jb.t2 = jb.b_row;
+        jb.t3 = nv;
     }
 
-    __device__ void epilogue(const TcJob &jb, uint32_t tmem, int q, int lane) const {
+    // Quarters 0,1 hold the gate rows, quarters 2,3 the matching up rows.
+    // Per 16-column chunk all four warps stage their accumulators in shared
+    // memory (named barrier 1 over the 4 epilogue warps); then thread t
+    // finishes row t % 64 for columns t / 64 + 2k (k < 8): 8 independent
+    // SwiGLU evaluations per thread, all loads before any store.
+    __device__ void epilogue(const TcJob &jb, uint32_t tmem, int q, int lane, void *smem) const {
+        int *acc = static_cast<int *>(smem);   // [2 halves][64 rows][17] (padded)
         const bool routed = jb.t0 >= 0;
         const int rows = routed ? I : S;
-        const int i = jb.t1 * 128 + 32 * q + lane;
-        const bool valid = i < rows;
-        float gsc = 0.0f, usc = 0.0f;
-        if (valid) {
-            gsc = routed ? gate_s[(size_t)jb.t0 * I + i] : sh_gate_s[i];
-            usc = routed ? up_s[(size_t)jb.t0 * I + i] : sh_up_s[i];
-        }
+        const int tid = 32 * q + lane;          // 0..127
+        const int half = q >> 1, r_in = 32 * (q & 1) + lane;
+        const int row = tid & 63, col0 = tid >> 6;
+        const int i = jb.t1 * 64 + row;
+        const float gsc = routed ? gate_s[(size_t)jb.t0 * I + i] : sh_gate_s[i];
+        const float usc = routed ? up_s[(size_t)jb.t0 * I + i] : sh_up_s[i];
         float *out = routed ? act : sh_act;
         const float *scl = routed ? xs_sorted : xs;
         const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
         for (int c0 = 0; c0 < jb.t3; c0 += 16) {
-            int vg[16], vu[16];
-            tc::tmem_ld16(lane_base + c0, vg);
-            tc::tmem_ld16(lane_base + BN + c0, vu);
+            int v[16];
+            tc::tmem_ld16(lane_base + c0, v);
             tc::tmem_ld_wait();
-            if (!valid) continue;
-            const int lim = min(16, jb.t3 - c0);
+            int *mine = acc + (half * 64 + r_in) * 17;
 #pragma unroll
-            for (int c = 0; c < 16; c++) {
-                if (c < lim) {
-                    const int p = jb.t2 + c0 + c;
-                    const float as = scl[p];
-                    const float g = __fmul_rn(__fmul_rn((float)vg[c], as), gsc);
-                    const float u = __fmul_rn(__fmul_rn((float)vu[c], as), usc);
-                    out[(size_t)p * rows + i] = __fmul_rn(silu_f(g), u);
-                }
+            for (int c = 0; c < 16; c++) mine[c] = v[c];
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            const int lim = min(16, jb.t3 - c0);
+            int ga[8], ua[8];
+            float as[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const int c = col0 + 2 * k;
+                ga[k] = acc[row * 17 + c];
+                ua[k] = acc[(64 + row) * 17 + c];
+                as[k] = c < lim ? scl[jb.t2 + c0 + c] : 0.0f;
             }
+            float res[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const float g = __fmul_rn(__fmul_rn((float)ga[k], as[k]), gsc);
+                const float u = __fmul_rn(__fmul_rn((float)ua[k], as[k]), usc);
+                res[k] = __fmul_rn(silu_f(g), u);
+            }
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const int c = col0 + 2 * k;
+                if (c < lim) out[(size_t)(jb.t2 + c0 + c) * rows + i] = res[k];
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
         }
     }
 };
 
 struct MoeDown {
-    static constexpr int NA = 1, BN = 128, STAGES = 6;
-    using Iter = TileIter;
+    static constexpr int NA = 1, BN = 128, STAGES = 6, EPI_SMEM = 0, JOB_SMEM = MOE_JOB_SMEM;
+    static constexpr int NBUF = 4;
+    static constexpr uint32_t KERNEL_ID = 3;
+    TraceBuf trace;
     CUtensorMap td, tsd;
     CUtensorMap ta[NBOX], tsa[NBOX];
     int H, I, S, E, T, topk, htiles;
     const int32_t *offsets, *pair_tok, *pair_slot;
     const int32_t *active;   // as in MoeGateUp
+    int *sched;
     const float *down_s, *sh_down_s, *as2, *sh_as, *w;
     float *part, *sh_y;
     int *err;
 
-    __device__ void iter_init(Iter &it) const {
-        it.tile = blockIdx.x;
-        it.chunk = 0;
+    __device__ void prefetch() const {
+        tc::prefetch_tmap(&td);
+        if (S) tc::prefetch_tmap(&tsd);
+        for (int b = 0; b < NBOX; b++) tc::prefetch_tmap(&ta[b]);
     }
 
-    __device__ bool iter_next(Iter &it, TcJob &jb) const {
-        // shared-expert tiles (twice the K of a routed tile) first, then the
-        // active experts' tiles
-        const int na = active[E];
+    using Iter = DynIter;
+    __device__ void load_job_state(void *js) const { sched_stage(*this, js); }
+    __device__ void iter_init(Iter &it, void *js) const { sched_init<MoeDown>(it, js); }
+    __device__ bool iter_next(Iter &it, TcJob &jb) const { return sched_next(*this, it, jb); }
+
+    // tiles: the shared expert's first (twice the K of a routed tile), then the
+    // active experts' in the prep kernel's order (most pairs first)
+    __device__ int num_tiles(const SchedSmem *sm) const {
+        return sm->active[E] * htiles + (S ? htiles : 0);
+    }
+    __device__ void tile_info(int t, const SchedSmem *sm, int &e, int &rt, int &p0,
+                              int &cnt) const {
         const int sh = S ? htiles : 0;
-        const int ntiles = sh + na * htiles;
-        while (it.tile < ntiles) {
-            const int t = it.tile;
-            const bool routed = t >= sh;
-            const int e = routed ? active[(t - sh) / htiles] : -1;
-            const int rt = routed ? (t - sh) % htiles : t;
-            const int p0 = routed ? offsets[e] : 0;
-            const int cnt = routed ? offsets[e + 1] - p0 : T;
-            if (it.chunk * BN >= cnt) {
-                it.tile += gridDim.x;
-                it.chunk = 0;
-                continue;
-            }
-            const int nv = min(BN, cnt - it.chunk * BN);
-            const int bi = box_index(nv);
-            jb.a[0] = routed ? &td : &tsd;
-            jb.a[1] = nullptr;
-            jb.b = routed ? &ta[bi] : &tsa[bi];
-            jb.b_box = box_rows(bi);
-            jb.a_row = routed ? e * H + rt * 128 : rt * 128;
-            jb.b_row = p0 + it.chunk * BN;
-            jb.kblocks = ((routed ? I : S) + tc::BK - 1) / tc::BK;
-            jb.n_mma = (nv + 15) & ~15;
-            jb.t0 = e;
-            jb.t1 = rt;
-            jb.t2 = jb.b_row;
-            jb.t3 = nv;
-            it.chunk++;
-            return true;
+        if (t < sh) {
+            e = -1; rt = t; p0 = 0; cnt = T;
+        } else {
+            e = sm->active[(t - sh) / htiles];
+            rt = (t - sh) % htiles;
+            p0 = sm->offsets[e];
+            cnt = sm->offsets[e + 1] - p0;
         }
-        return false;
+    }
+    __device__ int num_chunks(int t, const SchedSmem *sm) const {
+        int e, rt, p0, cnt;
+        tile_info(t, sm, e, rt, p0, cnt);
+        return (cnt + BN - 1) / BN;
+    }
+    __device__ void make_job(int t, int chunk, const SchedSmem *sm, TcJob &jb) const {
+        int e, rt, p0, cnt;
+        tile_info(t, sm, e, rt, p0, cnt);
+        const bool routed = e >= 0;
+        const int nv = min(BN, cnt - chunk * BN);
+        const int bi = box_index(nv);
+        jb.a[0] = routed ? &td : &tsd;
+        jb.a[1] = nullptr;
+        jb.a_kbt = ((routed ? I : S) + tc::BK - 1) / tc::BK;
+        jb.b = routed ? &ta[bi] : &tsa[bi];
+        jb.b_box = box_rows(bi);
+        jb.a_row = routed ? e * H + rt * 128 : rt * 128;
+        jb.b_row = p0 + chunk * BN;
+        jb.kblocks = ((routed ? I : S) + tc::BK - 1) / tc::BK;
+        jb.n_mma = (nv + 15) & ~15;
+        jb.t0 = e;
+        jb.t1 = rt;
+        jb.t2 = jb.b_row;
+        jb.t3 = nv;
     }
 
-    __device__ void epilogue(const TcJob &jb, uint32_t tmem, int q, int lane) const {
+    __device__ void epilogue(const TcJob &jb, uint32_t tmem, int q, int lane, void *) const {
         const bool routed = jb.t0 >= 0;
         const int c = jb.t1 * 128 + 32 * q + lane;
         const bool valid = c < H;
@@ -178,20 +321,34 @@ struct MoeDown {
             int v[16];
             tc::tmem_ld16(lane_base + c0, v);
             tc::tmem_ld_wait();
-            if (!valid) continue;
             const int lim = min(16, jb.t3 - c0);
+            // per-column pair data: one load per lane, broadcast by shuffle
+            // (keeps global-load latency out of the column loop)
+            float my_as = 0.0f, my_w = 0.0f;
+            int my_dst = 0;
+            if (lane < lim) {
+                const int p = jb.t2 + c0 + lane;
+                if (routed) {
+                    const int slot_row = pair_tok[p] * topk + pair_slot[p];
+                    my_as = as2[p];
+                    my_w = w[slot_row];
+                    my_dst = slot_row;
+                } else {
+                    my_as = sh_as[p];
+                    my_dst = p;
+                }
+            }
 #pragma unroll
             for (int k = 0; k < 16; k++) {
-                if (k < lim) {
-                    const int p = jb.t2 + c0 + k;
-                    if (routed) {
-                        const int tok = pair_tok[p], slot = pair_slot[p];
-                        const float y = __fmul_rn(__fmul_rn((float)v[k], as2[p]), dsc);
-                        part[((size_t)tok * topk + slot) * H + c] =
-                            __fmul_rn(y, w[(size_t)tok * topk + slot]);
-                    } else {
-                        sh_y[(size_t)p * H + c] = __fmul_rn(__fmul_rn((float)v[k], sh_as[p]), dsc);
-                    }
+                const float as = __shfl_sync(0xffffffffu, my_as, k);
+                const float wk = __shfl_sync(0xffffffffu, my_w, k);
+                const int dst = __shfl_sync(0xffffffffu, my_dst, k);
+                if (valid && k < lim) {
+                    const float y = __fmul_rn(__fmul_rn((float)v[k], as), dsc);
+                    if (routed)
+                        part[(size_t)dst * H + c] = __fmul_rn(y, wk);
+                    else
+                        sh_y[(size_t)dst * H + c] = y;
                 }
             }
         }
@@ -212,7 +369,8 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(
     int expert_begin, int8_t *__restrict__ xq, float *__restrict__ xs,
     int32_t *__restrict__ offsets, int32_t *__restrict__ pair_tok,
     int32_t *__restrict__ pair_slot, int8_t *__restrict__ xq_sorted,
-    float *__restrict__ xs_sorted, int32_t *__restrict__ active, int32_t *err) {
+    float *__restrict__ xs_sorted, int32_t *__restrict__ active, int *__restrict__ sched,
+    int32_t *err) {
     __shared__ int cnt[1025];
     __shared__ int rank[8];
     __shared__ float red[8];
@@ -224,9 +382,17 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(
     for (int e = tid; e <= E; e += blockDim.x) cnt[e] = 0;
     if (tid < 8) rank[tid] = 0;
     // quantise row t (decoder.rs:1588-1597): amax, scale = amax/127, round half away
+    // (H <= 2048: the row stays in registers until it is quantised)
     const float *row = x + (size_t)t * H;
+    constexpr int V = 2048 / 256;
+    float v[V];
     float m = 0.0f;
-    for (int i = tid; i < H; i += blockDim.x) m = fmaxf(m, fabsf(row[i]));
+#pragma unroll
+    for (int u = 0; u < V; u++) {
+        const int i = tid + u * 256;
+        v[u] = i < H ? row[i] : 0.0f;
+        m = fmaxf(m, fabsf(v[u]));
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if (lane == 0) red[warp] = m;
@@ -280,17 +446,35 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(
     __syncthreads();
     if (t == 0) {
         for (int e = tid; e <= E; e += blockDim.x) offsets[e] = cnt[e];
+        // active experts, most pairs first (ties: lower id first) so the
+        // dynamically scheduled GEMMs start the longest tiles first: expert
+        // e's position is the number of experts that sort before it
+        for (int e = tid; e < E; e += blockDim.x) {
+            const int c = cnt[e + 1] - cnt[e];
+            if (!c) continue;
+            int pos = 0;
+            for (int f = 0; f < E; f++) {
+                const int cf = cnt[f + 1] - cnt[f];
+                pos += (cf > c) || (cf == c && f < e);
+            }
+            active[pos] = e;
+        }
         if (tid == 0) {
             int na = 0;
-            for (int e = 0; e < E; e++)
-                if (cnt[e + 1] > cnt[e]) active[na++] = e;
+            for (int e = 0; e < E; e++) na += cnt[e + 1] > cnt[e];
             active[E] = na;
+            sched[0] = 0;
+            sched[1] = 0;
         }
     }
     const float inv = s_inv;
     const float sc = s_scale;
     int8_t *qrow = xq + (size_t)t * H;
-    for (int i = tid; i < H; i += blockDim.x) qrow[i] = (int8_t)quant_i8(row[i], inv, false);
+#pragma unroll
+    for (int u = 0; u < V; u++) {
+        const int i = tid + u * 256;
+        if (i < H) qrow[i] = (int8_t)quant_i8(v[u], inv, false);
+    }
     __syncthreads();
     // scatter this token's pairs and copy its quantised row to each pair slot
     const int H16 = H >> 4;
@@ -397,8 +581,16 @@ __global__ void __launch_bounds__(128) act_quant_rows_kernel(
     } else {
         return;
     }
+    // the row (K <= 2048) stays in registers between the amax and quantise passes
+    constexpr int V = 2048 / 128;
+    float v[V];
     float m = 0.0f;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) m = fmaxf(m, fabsf(row[i]));
+#pragma unroll
+    for (int u = 0; u < V; u++) {
+        const int i = threadIdx.x + u * 128;
+        v[u] = i < K ? row[i] : 0.0f;
+        m = fmaxf(m, fabsf(v[u]));
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if (lane == 0) red[warp] = m;
@@ -406,8 +598,67 @@ __global__ void __launch_bounds__(128) act_quant_rows_kernel(
     m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
     const float s = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;
     const float inv = __fdiv_rn(1.0f, s);
-    for (int i = threadIdx.x; i < K; i += blockDim.x) q[i] = (int8_t)quant_i8(row[i], inv, false);
+#pragma unroll
+    for (int u = 0; u < V; u++) {
+        const int i = threadIdx.x + u * 128;
+        if (i < K) q[i] = (int8_t)quant_i8(v[u], inv, false);
+    }
     if (threadIdx.x == 0) *sc = s;
+}
+
+// Weight re-layout for the tensor-core path: dst holds, for every 128-row
+// block rb and 128-byte K block kb (rb-major), the 128 x 128-byte sub-matrix
+// as one contiguous 16 KB chunk at row ((rb * KB + kb) * 128) of a
+// [rows * KB, 128] matrix.  rows and K are multiples of 128.
+__global__ void tile_rows_kernel(const int8_t *__restrict__ src, long rows, int K,
+                                 int8_t *__restrict__ dst) {
+    const int KB = K / 128;
+    const long chunks16 = rows * (long)K / 16;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < chunks16;
+         i += (long)gridDim.x * blockDim.x) {
+        const long dst_row = i / 8;          // 8 x 16 B per 128-byte row
+        const int c16 = (int)(i % 8);
+        const long blk = dst_row / 128;      // rb * KB + kb
+        const int r = (int)(dst_row % 128);
+        const long rb = blk / KB;
+        const int kb = (int)(blk % KB);
+        const int4 v = reinterpret_cast<const int4 *>(src + (rb * 128 + r) * (long)K + kb * 128)[c16];
+        reinterpret_cast<int4 *>(dst)[i] = v;
+    }
+}
+
+// Gate/up interleaved re-layout: 128-row block b holds gate rows
+// [64b, 64b+64) then up rows [64b, 64b+64), each (block, 128-byte K block)
+// one contiguous 16 KB chunk as in tile_rows_kernel.  rows % 64 == 0.
+__global__ void tile_gate_up_kernel(const int8_t *__restrict__ gate, const int8_t *__restrict__ up,
+                                    long rows, int K, int8_t *__restrict__ dst) {
+    const int KB = K / 128;
+    const long chunks16 = 2 * rows * (long)K / 16;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < chunks16;
+         i += (long)gridDim.x * blockDim.x) {
+        const long dst_row = i / 8;
+        const int c16 = (int)(i % 8);
+        const long blk = dst_row / 128;
+        const int r = (int)(dst_row % 128);
+        const long b = blk / KB;
+        const int kb = (int)(blk % KB);
+        const int8_t *src = r < 64 ? gate + (b * 64 + r) * (long)K : up + (b * 64 + r - 64) * (long)K;
+        reinterpret_cast<int4 *>(dst)[i] = reinterpret_cast<const int4 *>(src + kb * 128)[c16];
+    }
+}
+
+static int tiled_gate_up(const int8_t *gate, const int8_t *up, long rows, int K, int8_t **dst) {
+    FOCR_CUDA_TRY(cudaMalloc((void **)dst, 2 * rows * (size_t)K));
+    tile_gate_up_kernel<<<num_sms() * 4, 256>>>(gate, up, rows, K, *dst);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    return FOCR_OK;
+}
+
+static int tiled_copy(const int8_t *src, long rows, int K, int8_t **dst) {
+    FOCR_CUDA_TRY(cudaMalloc((void **)dst, rows * (size_t)K));
+    tile_rows_kernel<<<num_sms() * 4, 256>>>(src, rows, K, *dst);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    return FOCR_OK;
 }
 
 struct MoeTcState {
@@ -424,31 +675,38 @@ int moe_tc_setup(focr_moe_layer *L) {
     MoeGateUp &g = st->gu;
     MoeDown &d = st->dn;
     int rc = 0;
-    rc = rc ? rc : make_tmap_i8(&g.tg, L->gate_w, (uint64_t)E * I, H, 128);
-    rc = rc ? rc : make_tmap_i8(&g.tu, L->up_w, (uint64_t)E * I, H, 128);
-    rc = rc ? rc : make_tmap_i8(&d.td, L->down_w, (uint64_t)E * H, I, 128);
+    // TMA-tiled weights: every (128-row block, 128-byte K block) chunk is one
+    // contiguous 16 KB read (row-major boxes read 128 B from each of 128 rows)
+    const int KBh = H / 128, KBi = I / 128, KBs = S / 128;
+    rc = rc ? rc : tiled_gate_up(L->gate_w, L->up_w, (long)E * I, H, &L->gate_t);
+    rc = rc ? rc : tiled_copy(L->down_w, (long)E * H, I, &L->down_t);
+    rc = rc ? rc : make_tmap_i8(&g.tgu, L->gate_t, (uint64_t)2 * E * I * KBh, 128, 128);
+    rc = rc ? rc : make_tmap_i8(&d.td, L->down_t, (uint64_t)E * H * KBi, 128, 128);
     for (int b = 0; b < NBOX; b++) {
         rc = rc ? rc : make_tmap_i8(&g.tx[b], L->xq_sorted, Pp, H, box_rows(b));
         rc = rc ? rc : make_tmap_i8(&d.ta[b], L->aq, Pp, I, box_rows(b));
     }
     if (S) {
-        rc = rc ? rc : make_tmap_i8(&g.tsg, L->sh_gate_w, S, H, 128);
-        rc = rc ? rc : make_tmap_i8(&g.tsu, L->sh_up_w, S, H, 128);
-        rc = rc ? rc : make_tmap_i8(&d.tsd, L->sh_down_w, H, S, 128);
+        rc = rc ? rc : tiled_gate_up(L->sh_gate_w, L->sh_up_w, S, H, &L->sh_gate_t);
+        rc = rc ? rc : tiled_copy(L->sh_down_w, H, S, &L->sh_down_t);
+        rc = rc ? rc : make_tmap_i8(&g.tsgu, L->sh_gate_t, (uint64_t)2 * S * KBh, 128, 128);
+        rc = rc ? rc : make_tmap_i8(&d.tsd, L->sh_down_t, (uint64_t)H * KBs, 128, 128);
         for (int b = 0; b < NBOX; b++) {
             rc = rc ? rc : make_tmap_i8(&g.txt[b], L->xq, Tp, H, box_rows(b));
             rc = rc ? rc : make_tmap_i8(&d.tsa[b], L->sh_aq, Tp, S, box_rows(b));
         }
     }
+    cudaDeviceSynchronize();
     if (rc) {
         delete st;
         return rc;
     }
     g.H = H; g.I = I; g.S = S; g.E = E; g.T = 0;
-    g.itiles = (I + 127) / 128;
-    g.stiles = S ? (S + 127) / 128 : 0;
+    g.itiles = I / 64;
+    g.stiles = S / 64;
     g.offsets = L->offsets;
     g.active = L->counts;
+    g.sched = L->sched;
     g.gate_s = L->gate_s; g.up_s = L->up_s; g.sh_gate_s = L->sh_gate_s; g.sh_up_s = L->sh_up_s;
     g.xs_sorted = L->xs_sorted; g.xs = L->xs;
     g.act = L->act; g.sh_act = L->sh_act;
@@ -457,6 +715,7 @@ int moe_tc_setup(focr_moe_layer *L) {
     d.htiles = (H + 127) / 128;
     d.offsets = L->offsets; d.pair_tok = L->pair_tok; d.pair_slot = L->pair_slot;
     d.active = L->counts;
+    d.sched = L->sched + 1;
     d.down_s = L->down_s; d.sh_down_s = L->sh_down_s; d.as2 = L->as2; d.sh_as = L->sh_as;
     d.w = nullptr;
     d.part = L->part; d.sh_y = L->sh_y;
@@ -481,13 +740,14 @@ int moe_tc_experts(focr_moe_layer *L, const float *x, int m, const int32_t *idx,
         FOCR_CUDA_TRY(launch_pdl(moe_prep_kernel, dim3(m), dim3(256), 0, st, x, idx, m, H, K,
                                  (int)L->E, (int)L->cfg.expert_begin, L->xq, L->xs, L->offsets,
                                  L->pair_tok, L->pair_slot, L->xq_sorted, L->xs_sorted, L->counts,
-                                 L->err));
+                                 L->sched, L->err));
     } else {
         int rc = launch_quantize_rows(x, m, H, false, L->xq, L->xs, st);
         if (rc) return rc;
         moe_bucket_kernel<<<1, 1024, 0, st>>>(idx, m, K, (int)L->E, (int)L->cfg.expert_begin,
                                               L->offsets, L->pair_tok, L->pair_slot, L->counts,
                                               L->err);
+        FOCR_CUDA_TRY(cudaMemsetAsync(L->sched, 0, 2 * sizeof(int), st));
         gather_pairs_kernel<<<P, 128, 0, st>>>(L->xq, L->xs, L->pair_tok, L->offsets + L->E, H,
                                                L->xq_sorted, L->xs_sorted);
     }

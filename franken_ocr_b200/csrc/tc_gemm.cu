@@ -43,7 +43,10 @@ int make_tmap_i8(CUtensorMap *map, const void *base, uint64_t rows, uint64_t col
 
 template <int BN_, int STAGES_>
 struct RawIgemm {
-    static constexpr int NA = 1, BN = BN_, STAGES = STAGES_;
+    static constexpr int NA = 1, BN = BN_, STAGES = STAGES_, EPI_SMEM = 0, JOB_SMEM = 0;
+    static constexpr uint32_t KERNEL_ID = 1;
+    static constexpr int NBUF = 512 / BN_ >= 4 ? 4 : 2;   // TMEM accumulator buffers
+    TraceBuf trace;
     struct Iter {
         long tile;
     };
@@ -53,7 +56,12 @@ struct RawIgemm {
     int32_t *out;
     int *err;
 
-    __device__ void iter_init(Iter &it) const { it.tile = blockIdx.x; }
+    __device__ void prefetch() const {
+        tc::prefetch_tmap(&ta);
+        tc::prefetch_tmap(&tb);
+    }
+    __device__ void load_job_state(void *) const {}
+    __device__ void iter_init(Iter &it, const void *) const { it.tile = blockIdx.x; }
 
     // Persistent: CTA c takes tiles c, c + grid, ...; the A (activation) tile
     // index runs fastest so concurrently running CTAs share one B tile in L2.
@@ -65,6 +73,7 @@ struct RawIgemm {
         jb.a[1] = nullptr;
         jb.b = &tb;
         jb.b_box = BN;
+        jb.a_kbt = 0;
         jb.a_row = mt * 128;
         jb.b_row = nt * BN;
         jb.kblocks = (K + tc::BK - 1) / tc::BK;
@@ -74,7 +83,7 @@ struct RawIgemm {
         return true;
     }
 
-    __device__ void epilogue(const TcJob &jb, uint32_t tmem, int q, int lane) const {
+    __device__ void epilogue(const TcJob &jb, uint32_t tmem, int q, int lane, void *) const {
         const int row = jb.a_row + 32 * q + lane;
         const int nv = jb.t0;
         int32_t *orow = out + (size_t)row * N + jb.b_row;

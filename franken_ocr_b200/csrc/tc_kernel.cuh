@@ -4,9 +4,13 @@
 //   static constexpr int NA      -- A operands sharing one B tile (1 or 2)
 //   static constexpr int BN      -- max B rows (MMA N) per job, multiple of 16
 //   static constexpr int STAGES  -- shared-memory pipeline depth
-//   struct Iter;  __device__ void iter_init(Iter &) const;
+//   static constexpr int JOB_SMEM -- shared-memory bytes for job-scheduling state
+//   __device__ void prefetch() const          -- prefetch tensor-map descriptors
+//   __device__ void load_job_state(void *) const -- all threads stage that state
+//   struct Iter;  __device__ void iter_init(Iter &, const void *job_state) const;
 //   __device__ bool iter_next(Iter &, TcJob &) const -- the CTA's next tile job
-//   __device__ void epilogue(const TcJob &, uint32_t tmem, int quarter, int lane) const
+//   static constexpr int EPI_SMEM -- shared-memory bytes the epilogue may use
+//   __device__ void epilogue(const TcJob &, uint32_t tmem, int quarter, int lane, void *smem) const
 //   int *err                     -- status word (bit 4: a bounded wait expired)
 // A job computes D[128 x n_mma] = sum over kblocks of A[a_row.., k] . B[b_row.., k]
 // for every A operand (accumulator a at TMEM column offset a*BN of its buffer).
@@ -15,11 +19,12 @@
 // Roles (192 threads): warp 0 lane 0 issues TMA loads, warp 1 lane 0 issues
 // MMAs, warps 2..5 run the epilogue; epilogue warp w may only touch TMEM lanes
 // 32*(w%4)..+31, so it owns accumulator rows 32*(w%4)..+31.  Accumulators are
-// double-buffered in TMEM (job j uses buffer j&1), so the epilogue of job j
-// overlaps the loads and MMAs of job j+1.
+// held in P::NBUF TMEM buffers (job j uses buffer j % NBUF), so the epilogue
+// of job j overlaps the loads and MMAs of the following jobs.
 #pragma once
 
 #include "tc.cuh"
+#include "trace.cuh"
 
 namespace focr {
 
@@ -28,19 +33,22 @@ struct TcJob {
     const CUtensorMap *b;
     int a_row, b_row, kblocks, n_mma;
     int b_box;            // rows in the B box (TMA transfer size), >= n_mma
+    int a_kbt;            // 0: A maps are row-major [rows, K]; else A is TMA-tiled with
+                          // a_kbt K blocks per 128-row block (see tile_rows_kernel)
     int t0, t1, t2, t3;   // problem-specific tags (expert, tile, pair base, count)
 };
 
-template <int NA, int BN>
+template <int NA, int BN, int NBUF>
 struct TcCols {
-    static constexpr int need = 2 * NA * BN;
+    static constexpr int need = NBUF * NA * BN;
     static constexpr uint32_t value = need <= 32 ? 32 : need <= 64 ? 64 : need <= 128 ? 128
                                     : need <= 256 ? 256 : 512;
 };
 
 template <class P>
 constexpr size_t tc_smem_bytes() {
-    return (size_t)P::STAGES * (P::NA * 128 * 128 + P::BN * 128) + 1024 + 256;
+    return (size_t)P::STAGES * (P::NA * 128 * 128 + P::BN * 128) + 1024 + 256 + P::EPI_SMEM +
+           P::JOB_SMEM;
 }
 
 template <class P>
@@ -48,18 +56,24 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__
     constexpr int NA = P::NA, BN = P::BN, S = P::STAGES;
     constexpr uint32_t A_BYTES = 128 * 128, B_BYTES = BN * 128;
     constexpr uint32_t STAGE_BYTES = NA * A_BYTES + B_BYTES;
-    constexpr uint32_t NCOLS = TcCols<NA, BN>::value;
+    constexpr int NBUF = P::NBUF;
+    constexpr uint32_t NCOLS = TcCols<NA, BN, NBUF>::value;
     static_assert(BN % 16 == 0 && BN <= 256, "MMA N must be a multiple of 16 in [16, 256]");
-    static_assert(2 * NA * BN <= 512, "double-buffered accumulators exceed tensor memory");
+    static_assert(NBUF * NA * BN <= 512, "accumulator buffers exceed tensor memory");
+    static_assert(2 * S + 2 * NBUF <= 30, "barriers exceed their 256-byte area");
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                 ~uintptr_t(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(base + S * STAGE_BYTES);
     uint64_t *empty = full + S;
-    uint64_t *tfull = empty + S;    // [2]
-    uint64_t *tempty = tfull + 2;   // [2]
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(tempty + 2);
+    uint64_t *tfull = empty + S;       // [NBUF]
+    uint64_t *tempty = tfull + NBUF;   // [NBUF]
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(tempty + NBUF);
+    // epilogue scratch (P::EPI_SMEM bytes, 16-byte aligned) after the barriers
+    void *epi_smem = reinterpret_cast<uint8_t *>(full) + 256;
+    // job-scheduling state the problem stages once per CTA (P::JOB_SMEM bytes)
+    void *job_smem = reinterpret_cast<uint8_t *>(epi_smem) + P::EPI_SMEM;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int *err = p.err;
@@ -69,7 +83,7 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__
             tc::mbar_init(&full[s], 1);
             tc::mbar_init(&empty[s], 1);
         }
-        for (int b = 0; b < 2; b++) {
+        for (int b = 0; b < NBUF; b++) {
             tc::mbar_init(&tfull[b], 1);
             tc::mbar_init(&tempty[b], 4);
         }
@@ -80,8 +94,17 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__
     __syncthreads();
     tc::fence_after();
     const uint32_t tmem = *tslot;
+    const TraceBuf &tb = p.trace;
+    constexpr uint32_t KID = P::KERNEL_ID;
+    if (threadIdx.x == 0) {
+        p.prefetch();
+        trace_event(tb, KID, 0, TR_KERNEL_START);
+    }
     pdl_trigger();
     pdl_wait();   // inputs written by the preceding kernel are visible from here on
+    if (threadIdx.x == 0) trace_event(tb, KID, 0, TR_DEPS_READY);
+    p.load_job_state(job_smem);
+    __syncthreads();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -89,8 +112,9 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__
             bool ok = true;
             TcJob jb;
             typename P::Iter itr;
-            p.iter_init(itr);
-            while (ok && p.iter_next(itr, jb)) {
+            p.iter_init(itr, job_smem);
+            for (int j = 0; ok && p.iter_next(itr, jb); j++) {
+                trace_event(tb, KID, j, TR_JOB_LOAD);
                 const uint32_t bytes = NA * A_BYTES + (uint32_t)jb.b_box * 128;
                 for (int kb = 0; kb < jb.kblocks; kb++, it++) {
                     const uint32_t s = it % S;
@@ -99,8 +123,14 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__
                     tc::mbar_arrive_expect_tx(&full[s], bytes);
                     uint8_t *st = base + s * STAGE_BYTES;
 #pragma unroll
-                    for (int a = 0; a < NA; a++)
-                        tc::tma_load_2d(st + a * A_BYTES, jb.a[a], kb * tc::BK, jb.a_row, &full[s]);
+                    for (int a = 0; a < NA; a++) {
+                        if (jb.a_kbt)   // tiled: chunk (row block, kb) is 128 contiguous rows of 128 B
+                            tc::tma_load_2d(st + a * A_BYTES, jb.a[a], 0,
+                                            ((jb.a_row >> 7) * jb.a_kbt + kb) * 128, &full[s]);
+                        else
+                            tc::tma_load_2d(st + a * A_BYTES, jb.a[a], kb * tc::BK, jb.a_row,
+                                            &full[s]);
+                    }
                     tc::tma_load_2d(st + NA * A_BYTES, jb.b, kb * tc::BK, jb.b_row, &full[s]);
                 }
             }
@@ -112,10 +142,11 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__
             bool ok = true;
             TcJob jb;
             typename P::Iter itr;
-            p.iter_init(itr);
+            p.iter_init(itr, job_smem);
             for (int j = 0; ok && p.iter_next(itr, jb); j++) {
-                const int buf = j & 1;
-                if (j >= 2 && !(ok = tc::mbar_wait(&tempty[buf], ((j >> 1) - 1) & 1, err))) break;
+                const int buf = j % NBUF;
+                if (j >= NBUF && !(ok = tc::mbar_wait(&tempty[buf], ((j / NBUF) - 1) & 1, err)))
+                    break;
                 tc::fence_after();
                 const uint32_t acc = tmem + (uint32_t)(buf * NA * BN);
                 const uint32_t idesc = tc::idesc_i8(128, jb.n_mma);
@@ -123,6 +154,7 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__
                     const uint32_t s = it % S;
                     if (!(ok = tc::mbar_wait(&full[s], (it / S) & 1, err))) break;
                     tc::fence_after();
+                    if (kb == 0) trace_event(tb, KID, j, TR_JOB_MMA);
                     const uint32_t st = tc::smem_u32(base + s * STAGE_BYTES);
 #pragma unroll
                     for (int kk = 0; kk < tc::BK / 32; kk++) {
@@ -136,6 +168,7 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__
                     tc::mma_commit(&empty[s]);
                 }
                 if (ok) tc::mma_commit(&tfull[buf]);
+                trace_event(tb, KID, j, TR_JOB_MMA_DONE);
             }
         }
         __syncwarp();
@@ -143,21 +176,24 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__
         // epilogue warps 2..5
         TcJob jb;
         typename P::Iter itr;
-        p.iter_init(itr);
+        p.iter_init(itr, job_smem);
         for (int j = 0; p.iter_next(itr, jb); j++) {
-            const int buf = j & 1;
-            if (!tc::mbar_wait(&tfull[buf], (j >> 1) & 1, err)) break;
+            const int buf = j % NBUF;
+            if (!tc::mbar_wait(&tfull[buf], (j / NBUF) & 1, err)) break;
             tc::fence_after();
-            p.epilogue(jb, tmem + (uint32_t)(buf * NA * BN), warp & 3, lane);
+            if (threadIdx.x == 64) trace_event(tb, KID, j, TR_JOB_EPI);
+            p.epilogue(jb, tmem + (uint32_t)(buf * NA * BN), warp & 3, lane, epi_smem);
             tc::fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&tempty[buf]);
+            if (threadIdx.x == 64) trace_event(tb, KID, j, TR_JOB_EPI_DONE);
         }
     }
     tc::fence_before();
     __syncthreads();
     tc::fence_after();
     if (warp == 0) tc::tmem_dealloc(tmem, NCOLS);
+    if (threadIdx.x == 0) trace_event(tb, KID, 0, TR_KERNEL_END);
 }
 
 template <class P>
@@ -171,7 +207,9 @@ int launch_tc(const P &p, int grid, cudaStream_t st) {
         attr = true;
     }
     if (grid < 1) grid = 1;
-    FOCR_CUDA_TRY(launch_pdl(tc_gemm_kernel<P>, dim3(grid), dim3(192), smem, st, p));
+    P q = p;
+    q.trace = host_trace();
+    FOCR_CUDA_TRY(launch_pdl(tc_gemm_kernel<P>, dim3(grid), dim3(192), smem, st, q));
     return FOCR_OK;
 }
 

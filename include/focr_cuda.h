@@ -184,6 +184,14 @@ int focr_lmhead_top1(focr_lmhead *h, const float *x, size_t m, float *best_val,
 int focr_top1_combine(const float *vals, const int32_t *idx, size_t shards,
                       size_t m, uint32_t *token);
 
+/* ---- device event trace (GPU counterpart of FOCR_PROFILE_DECODE,
+ * native_engine/decoder.rs:986-1024) ------------------------------------
+ * Register a device buffer of `capacity` 16-byte events {u32 tag, u32 phase,
+ * u64 globaltimer ns} and a device u64 counter (zeroed by the caller); the
+ * tensor-core kernels launched afterwards append one event per (CTA, job,
+ * phase).  tag = kernel << 24 | cta << 12 | job.  NULL unregisters. */
+int focr_trace_set(void *events, unsigned long long *count, size_t capacity);
+
 /* ---- runtime self-test (dispatch.rs:340-431, `focr robot selftest`) --- */
 
 /* Runs the reference's selftest battery (12 shapes x {s8s8, u8s8}) on the
