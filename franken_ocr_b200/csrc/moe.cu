@@ -20,6 +20,7 @@ constexpr int MOE_MAX_CH = 4;  // 16-byte chunks per lane: K <= 32*16*4 = 2048
 
 struct MoeDev {
     int H, I, S, E, topk, T;
+    int sh0;   // the shared expert applies to rows [sh0, T)
     int expert_begin;
     const int8_t *gate_w, *up_w, *down_w;
     const float *gate_s, *up_s, *down_s;
@@ -241,7 +242,7 @@ __global__ void __launch_bounds__(MOE_THREADS) expert_gateup_kernel(MoeDev d) {
             act = d.act;
         } else {
             i = (int)(r - routed_rows);
-            p0 = 0;
+            p0 = d.sh0;
             p1 = d.T;
             grow = d.sh_gate_w + (size_t)i * d.H;
             urow = d.sh_up_w + (size_t)i * d.H;
@@ -321,7 +322,7 @@ __global__ void __launch_bounds__(MOE_THREADS) expert_down_kernel(MoeDev d) {
             dsc = d.down_s[(size_t)e * d.H + c];
         } else {
             c = (int)(r - routed_rows);
-            p0 = 0;
+            p0 = d.sh0;
             p1 = d.T;
             K = d.S;
             drow = d.sh_down_w + (size_t)c * d.S;
@@ -348,22 +349,28 @@ __global__ void __launch_bounds__(MOE_THREADS) expert_down_kernel(MoeDev d) {
 }
 
 // out = (((0 + p_0) + p_1) + ... + p_{k-1}) + s   (decoder.rs:2253-2261)
-__global__ void combine_kernel(const float *__restrict__ part, const float *__restrict__ sh_y,
-                               int H, int topk, float *__restrict__ y) {
+// rows (optional) maps pair t*topk+j to its partial's row in `part`;
+// the shared term is added for rows t >= sh0 when sh_y is given.
+__global__ void combine_kernel(const float *__restrict__ part, const int32_t *__restrict__ rows,
+                               const float *__restrict__ sh_y, int sh0, int H, int topk,
+                               float *__restrict__ y) {
     pdl_wait();
     pdl_trigger();
     const int t = blockIdx.y;
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= H) return;
     float o = 0.0f;
-    for (int j = 0; j < topk; j++) o = __fadd_rn(o, part[((size_t)t * topk + j) * H + c]);
-    if (sh_y) o = __fadd_rn(o, sh_y[(size_t)t * H + c]);
+    for (int j = 0; j < topk; j++) {
+        const size_t pr = rows ? (size_t)rows[(size_t)t * topk + j] : (size_t)t * topk + j;
+        o = __fadd_rn(o, part[pr * H + c]);
+    }
+    if (sh_y && t >= sh0) o = __fadd_rn(o, sh_y[(size_t)t * H + c]);
     y[(size_t)t * H + c] = o;
 }
 
 __global__ void check_idx_kernel(const int32_t *idx, int P, int lo, int hi, int32_t *err) {
     for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < P; p += gridDim.x * blockDim.x)
-        if (idx[p] < lo || idx[p] >= hi) atomicOr(err, 2);
+        if (idx[p] >= 0 && (idx[p] < lo || idx[p] >= hi)) atomicOr(err, 2);
 }
 
 // ---------------------------------------------------------------------------
@@ -372,6 +379,7 @@ __global__ void check_idx_kernel(const int32_t *idx, int P, int lo, int hi, int3
 
 static MoeDev make_dev(focr_moe_layer *L, int T, const float *w, float *part) {
     MoeDev d;
+    d.sh0 = 0;
     d.H = L->cfg.hidden;
     d.I = L->cfg.inter;
     d.S = L->cfg.shared_inter;
@@ -395,12 +403,13 @@ static MoeDev make_dev(focr_moe_layer *L, int T, const float *w, float *part) {
 
 static int moe_grid() { return num_sms() * 8; }
 
-void launch_act_quant(focr_moe_layer *L, int m, cudaStream_t st) {
+void launch_act_quant(focr_moe_layer *L, int m, int sh0, cudaStream_t st) {
     act_quant_kernel<<<m * L->cfg.topk, 256, 0, st>>>(L->act, L->cfg.inter, L->offsets + L->E,
                                                       L->aq, L->as2);
-    if (L->cfg.shared_inter)
-        act_quant_kernel<<<m, 256, 0, st>>>(L->sh_act, L->cfg.shared_inter, nullptr, L->sh_aq,
-                                            L->sh_as);
+    const size_t S = L->cfg.shared_inter;
+    if (S && m > sh0)
+        act_quant_kernel<<<m - sh0, 256, 0, st>>>(L->sh_act + sh0 * S, (int)S, nullptr,
+                                                  L->sh_aq + sh0 * S, L->sh_as + sh0);
 }
 
 int moe_route_dev(focr_moe_layer *L, const float *x, int m, int32_t *idx, float *w,
@@ -415,11 +424,11 @@ int moe_route_dev(focr_moe_layer *L, const float *x, int m, int32_t *idx, float 
 }
 
 int moe_forward_dev(focr_moe_layer *L, const float *x, int m, const int32_t *idx,
-                    const float *w, float *y, cudaStream_t st) {
+                    const float *w, float *y, cudaStream_t st, int sh0) {
     const int H = L->cfg.hidden, K = L->cfg.topk;
     int rc;
     if (L->tc_state) {
-        rc = moe_tc_experts(L, x, m, idx, w, st);
+        rc = moe_tc_experts(L, x, m, idx, w, sh0, st);
         if (rc) return rc;
     } else {
         check_idx_kernel<<<1, 256, 0, st>>>(idx, m * K, (int)L->cfg.expert_begin,
@@ -428,14 +437,19 @@ int moe_forward_dev(focr_moe_layer *L, const float *x, int m, const int32_t *idx
         if (rc) return rc;
         bucket_kernel<<<1, 1024, 0, st>>>(idx, m, K, L->E, L->cfg.expert_begin, L->offsets,
                                           L->pair_tok, L->pair_slot);
+        // empty slots (negative ids) contribute +0 to the combine
+        FOCR_CUDA_TRY(cudaMemsetAsync(L->part, 0, (size_t)m * K * H * sizeof(float), st));
         MoeDev d = make_dev(L, m, w, L->part);
+        d.sh0 = sh0;
         expert_gateup_kernel<<<moe_grid(), MOE_THREADS, 0, st>>>(d);
-        launch_act_quant(L, m, st);
+        launch_act_quant(L, m, sh0, st);
         expert_down_kernel<<<moe_grid(), MOE_THREADS, 0, st>>>(d);
     }
     dim3 gc((H + 255) / 256, m);
     FOCR_CUDA_TRY(launch_pdl(combine_kernel, gc, dim3(256), 0, st, (const float *)L->part,
-                             (const float *)(L->cfg.shared_inter ? L->sh_y : nullptr), H, K, y));
+                             (const int32_t *)nullptr,
+                             (const float *)(L->cfg.shared_inter ? L->sh_y : nullptr), sh0, H, K,
+                             y));
     return FOCR_OK;
 }
 
@@ -647,6 +661,27 @@ int focr_moe_decode(focr_moe_layer *L, const float *x, size_t m, float *y, int32
         return read_status(L, st);
     }
     return FOCR_OK;
+}
+
+int focr_moe_combine(const float *part, const int32_t *rows, const float *shared, size_t m,
+                     size_t topk, size_t hidden, float *y, void *stream) {
+    if (m == 0 || hidden == 0) return FOCR_OK;
+    if (!part || !y || topk == 0) return fail(FOCR_E_ARG, "moe_combine: null pointer or topk 0");
+    if (m > 65535 || hidden > (size_t)INT32_MAX || topk > 64)
+        return fail(FOCR_E_UNSUPPORTED, "moe_combine: shape too large");
+    dim3 gc((unsigned)((hidden + 255) / 256), (unsigned)m);
+    FOCR_CUDA_TRY(launch_pdl(combine_kernel, gc, dim3(256), 0, (cudaStream_t)stream, part, rows,
+                             shared, 0, (int)hidden, (int)topk, y));
+    return FOCR_OK;
+}
+
+int focr_moe_forward_rows(focr_moe_layer *L, const float *x, size_t m, const int32_t *idx,
+                          const float *w, float *y, size_t shared_begin, void *stream) {
+    if (!L) return fail(FOCR_E_ARG, "moe_forward_rows: null layer");
+    if (m == 0) return FOCR_OK;
+    if (m > L->cfg.max_tokens) return fail(FOCR_E_SHAPE, "moe_forward_rows: m > max_tokens");
+    if (shared_begin > m) return fail(FOCR_E_SHAPE, "moe_forward_rows: shared_begin > m");
+    return moe_forward_dev(L, x, (int)m, idx, w, y, (cudaStream_t)stream, (int)shared_begin);
 }
 
 }  // extern "C"

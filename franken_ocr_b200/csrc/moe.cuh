@@ -51,14 +51,14 @@ namespace focr {
 int moe_route_dev(focr_moe_layer *L, const float *x, int m, int32_t *idx, float *w,
                   cudaStream_t st);
 int moe_forward_dev(focr_moe_layer *L, const float *x, int m, const int32_t *idx,
-                    const float *w, float *y, cudaStream_t st);
+                    const float *w, float *y, cudaStream_t st, int sh0 = 0);
 int moe_decode_fused_m1(focr_moe_layer *L, const float *x, float *y, int32_t *idx, float *w,
                         cudaStream_t st);
 bool moe_fused_eligible(const focr_moe_layer *L);
 int moe_tc_setup(focr_moe_layer *L);
 void moe_tc_free(focr_moe_layer *L);
 int moe_tc_experts(focr_moe_layer *L, const float *x, int m, const int32_t *idx, const float *w,
-                   cudaStream_t st);
-void launch_act_quant(focr_moe_layer *L, int m, cudaStream_t st);
+                   int sh0, cudaStream_t st);
+void launch_act_quant(focr_moe_layer *L, int m, int sh0, cudaStream_t st);
 
 }  // namespace focr

@@ -127,6 +127,7 @@ struct MoeGateUp {
     CUtensorMap tgu, tsgu;
     CUtensorMap tx[NBOX], txt[NBOX];
     int H, I, S, E, T, itiles, stiles;   // itiles = I / 64, stiles = S / 64
+    int sh0;                             // the shared expert applies to rows [sh0, T)
     const int32_t *offsets;
     const int32_t *active;   // [E] local ids of experts with >= 1 pair, most pairs first; [E] = count
     int *sched;              // tile-claim counter (zeroed by the prep kernel)
@@ -154,7 +155,7 @@ struct MoeGateUp {
                               int &cnt) const {
         const int sh = S ? stiles : 0;
         if (t < sh) {
-            e = -1; rt = t; p0 = 0; cnt = T;
+            e = -1; rt = t; p0 = sh0; cnt = T - sh0;   // shared expert: rows [sh0, T)
         } else {
             e = sm->active[(t - sh) / itiles];
             rt = (t - sh) % itiles;
@@ -250,6 +251,7 @@ struct MoeDown {
     CUtensorMap td, tsd;
     CUtensorMap ta[NBOX], tsa[NBOX];
     int H, I, S, E, T, topk, htiles;
+    int sh0;                             // the shared expert applies to rows [sh0, T)
     const int32_t *offsets, *pair_tok, *pair_slot;
     const int32_t *active;   // as in MoeGateUp
     int *sched;
@@ -277,7 +279,7 @@ struct MoeDown {
                               int &cnt) const {
         const int sh = S ? htiles : 0;
         if (t < sh) {
-            e = -1; rt = t; p0 = 0; cnt = T;
+            e = -1; rt = t; p0 = sh0; cnt = T - sh0;   // shared expert: rows [sh0, T)
         } else {
             e = sm->active[(t - sh) / htiles];
             rt = (t - sh) % htiles;
@@ -370,7 +372,7 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(
     int32_t *__restrict__ offsets, int32_t *__restrict__ pair_tok,
     int32_t *__restrict__ pair_slot, int8_t *__restrict__ xq_sorted,
     float *__restrict__ xs_sorted, int32_t *__restrict__ active, int *__restrict__ sched,
-    int32_t *err) {
+    float *__restrict__ part, int32_t *err) {
     __shared__ int cnt[1025];
     __shared__ int rank[8];
     __shared__ float red[8];
@@ -418,8 +420,8 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(
         const int e = ge - expert_begin;
         if (e >= 0 && e < E)
             atomicAdd(&cnt[e], 1);
-        else
-            bad = 1;
+        else if (ge >= 0)
+            bad = 1;   // a negative id marks an empty slot
 #pragma unroll
         for (int j = 0; j < 8; j++)
             if (j < topk && p < mine0 + j && ge == my_e[j]) lrank[j]++;
@@ -476,10 +478,16 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(
         if (i < H) qrow[i] = (int8_t)quant_i8(v[u], inv, false);
     }
     __syncthreads();
-    // scatter this token's pairs and copy its quantised row to each pair slot
+    // scatter this token's pairs and copy its quantised row to each pair slot;
+    // an empty slot (negative id) contributes +0 to the combine
     const int H16 = H >> 4;
     for (int j = 0; j < topk; j++) {
         const int e = my_e[j] - expert_begin;
+        if (my_e[j] < 0) {
+            float4 *pr = reinterpret_cast<float4 *>(part + ((size_t)t * topk + j) * H);
+            for (int i = tid; i < H / 4; i += blockDim.x) pr[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            continue;
+        }
         if (e < 0 || e >= E) continue;
         const int pos = cnt[e] + rank[j];
         if (tid == 0) {
@@ -508,8 +516,8 @@ __global__ void moe_bucket_kernel(const int32_t *__restrict__ idx, int T, int to
         const int e = idx[p] - expert_begin;
         if (e >= 0 && e < E)
             atomicAdd(&cnt[e], 1);
-        else
-            bad = 1;
+        else if (idx[p] >= 0)
+            bad = 1;   // a negative id marks an empty slot
     }
     if (bad) atomicOr(err, 2);
     __syncthreads();
@@ -552,11 +560,11 @@ __global__ void gather_pairs_kernel(const int8_t *__restrict__ xq, const float *
 
 // Requantise activation rows (decoder.rs:1751, quantize_row_i8 of the SwiGLU
 // output), one block per row: rows [0, P) are routed pairs (rows >= the live
-// pair count are skipped), rows [P, P+T) the shared expert's tokens.
+// pair count are skipped), rows [P, P+T) the shared expert's tokens sh0.. .
 __global__ void __launch_bounds__(128) act_quant_rows_kernel(
     const float *__restrict__ act, int I, int P, const int32_t *__restrict__ count,
     int8_t *__restrict__ aq, float *__restrict__ as, const float *__restrict__ sh_act, int S,
-    int T, int8_t *__restrict__ sh_aq, float *__restrict__ sh_as) {
+    int T, int sh0, int8_t *__restrict__ sh_aq, float *__restrict__ sh_as) {
     __shared__ float red[4];
     pdl_wait();
     pdl_trigger();
@@ -573,7 +581,7 @@ __global__ void __launch_bounds__(128) act_quant_rows_kernel(
         sc = as + r;
         K = I;
     } else if (r < P + T) {
-        const int t = r - P;
+        const int t = sh0 + (r - P);
         row = sh_act + (size_t)t * S;
         q = sh_aq + (size_t)t * S;
         sc = sh_as + t;
@@ -732,7 +740,7 @@ void moe_tc_free(focr_moe_layer *L) {
 // Quantise + bucket + gather, then the two tensor-core GEMMs and the
 // activation requantisation between them.
 int moe_tc_experts(focr_moe_layer *L, const float *x, int m, const int32_t *idx, const float *w,
-                   cudaStream_t st) {
+                   int sh0, cudaStream_t st) {
     MoeTcState *s = static_cast<MoeTcState *>(L->tc_state);
     const int H = L->cfg.hidden, K = L->cfg.topk, S = L->cfg.shared_inter;
     const int P = m * K;
@@ -740,7 +748,7 @@ int moe_tc_experts(focr_moe_layer *L, const float *x, int m, const int32_t *idx,
         FOCR_CUDA_TRY(launch_pdl(moe_prep_kernel, dim3(m), dim3(256), 0, st, x, idx, m, H, K,
                                  (int)L->E, (int)L->cfg.expert_begin, L->xq, L->xs, L->offsets,
                                  L->pair_tok, L->pair_slot, L->xq_sorted, L->xs_sorted, L->counts,
-                                 L->sched, L->err));
+                                 L->sched, L->part, L->err));
     } else {
         int rc = launch_quantize_rows(x, m, H, false, L->xq, L->xs, st);
         if (rc) return rc;
@@ -748,22 +756,27 @@ int moe_tc_experts(focr_moe_layer *L, const float *x, int m, const int32_t *idx,
                                               L->offsets, L->pair_tok, L->pair_slot, L->counts,
                                               L->err);
         FOCR_CUDA_TRY(cudaMemsetAsync(L->sched, 0, 2 * sizeof(int), st));
+        // empty slots (negative ids) contribute +0 to the combine
+        FOCR_CUDA_TRY(cudaMemsetAsync(L->part, 0, (size_t)P * H * sizeof(float), st));
         gather_pairs_kernel<<<P, 128, 0, st>>>(L->xq, L->xs, L->pair_tok, L->offsets + L->E, H,
                                                L->xq_sorted, L->xs_sorted);
     }
     const int sms = num_sms();
     MoeGateUp g = s->gu;
     g.T = m;
+    g.sh0 = sh0;
     int tiles = (int)L->E * g.itiles + (S ? g.stiles : 0);
     int rc = launch_tc(g, tiles < sms ? tiles : sms, st);
     if (rc) return rc;
-    const int rows = P + (S ? m : 0);
+    const int rows = P + (S ? m - sh0 : 0);
     FOCR_CUDA_TRY(launch_pdl(act_quant_rows_kernel, dim3(rows), dim3(128), 0, st,
                              (const float *)L->act, (int)L->cfg.inter, P,
                              (const int32_t *)(L->offsets + L->E), L->aq, L->as2,
-                             (const float *)L->sh_act, S, S ? m : 0, L->sh_aq, L->sh_as));
+                             (const float *)L->sh_act, S, S ? m - sh0 : 0, sh0, L->sh_aq,
+                             L->sh_as));
     MoeDown d = s->dn;
     d.T = m;
+    d.sh0 = sh0;
     d.w = w;
     tiles = (int)L->E * d.htiles + (S ? d.htiles : 0);
     return launch_tc(d, tiles < sms ? tiles : sms, st);

@@ -96,6 +96,18 @@ class MoeLayer:
                                    _stream(mem)))
         return y
 
+    def forward_rows(self, x, idx, w, shared_begin, y=None):
+        """forward with the shared expert on rows >= shared_begin only; ids < 0
+        are empty slots (device tensors)."""
+        import torch
+
+        m = x.shape[0]
+        y = torch.empty((m, self.hidden), dtype=torch.float32, device=x.device) if y is None else y
+        check(lib.focr_moe_forward_rows(self._h, x.data_ptr(), m, idx.data_ptr(), w.data_ptr(),
+                                        y.data_ptr(), shared_begin,
+                                        torch.cuda.current_stream().cuda_stream))
+        return y
+
     def decode(self, x, y=None, idx=None, w=None):
         m = x.shape[0]
         y = self._out(x, (m, self.hidden), np.float32) if y is None else y

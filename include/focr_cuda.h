@@ -161,6 +161,37 @@ int focr_moe_forward(focr_moe_layer *layer, const float *x, size_t m,
 int focr_moe_decode(focr_moe_layer *layer, const float *x, size_t m, float *y,
                     int32_t *idx, float *w, int mem, void *stream);
 
+/* focr_moe_forward with the shared expert applied only to rows
+ * [shared_begin, m) (rows below get none).  Routing ids < 0 mark empty slots
+ * (no expert; they contribute +0).  Device pointers.  Used by expert
+ * parallelism: received (token, slot) pairs are one-slot rows before
+ * shared_begin, the rank's own tokens (ids -1) follow. */
+int focr_moe_forward_rows(focr_moe_layer *layer, const float *x, size_t m,
+                          const int32_t *idx, const float *w, float *y,
+                          size_t shared_begin, void *stream);
+
+/* Slot-ordered combine of per-slot partials: y[t][c] = ((((0 + P(t,0)[c]) +
+ * P(t,1)[c]) + ...) + P(t,k-1)[c]) + s[t][c] with P(t,j) = part row
+ * rows[t*k+j] (row t*k+j when rows is NULL); s may be NULL -- the
+ * decode_mlp_i8 combine (decoder.rs:2253-2261) for partials computed
+ * elsewhere (expert parallelism).  Device pointers. */
+int focr_moe_combine(const float *part, const int32_t *rows, const float *shared, size_t m,
+                     size_t topk, size_t hidden, float *y, void *stream);
+
+/* Expert-parallel dispatch packing (no counterpart in the single-process
+ * reference).  For T tokens x [T][hidden] with routing idx/w [T][topk]:
+ * pair p = t*topk + j goes to rank dest = idx[p] / experts_per_rank, into
+ * row dest*cap + (number of earlier pairs with that dest) of send_x
+ * [world*cap][hidden] / send_meta [world*cap][2] = {expert id, weight bits};
+ * other send_meta rows get id -1.  rows[p] receives that row.  The tokens
+ * themselves are copied to rows [world*cap, world*cap + T) of recv_x /
+ * recv_meta (id -1).  status bit 2 is set for an out-of-range expert id.
+ * Device pointers; enqueued on `stream`. */
+int focr_ep_pack(const float *x, const int32_t *idx, const float *w, size_t T, size_t topk,
+                 size_t hidden, size_t experts_per_rank, size_t world, size_t cap,
+                 float *send_x, int32_t *send_meta, float *recv_x, int32_t *recv_meta,
+                 int32_t *rows, int32_t *status, void *stream);
+
 /* ---- lm-head (decoder.rs:2275-2296, 1851-1927; sampler.rs:168-186) ---- */
 
 typedef struct focr_lmhead focr_lmhead;
