@@ -12,6 +12,7 @@
 
 #include "gemv.cuh"
 #include "moe.cuh"
+#include "router.cuh"
 
 namespace focr {
 
@@ -71,84 +72,16 @@ __global__ void router_logits_kernel(const float *__restrict__ x, const float *_
     if (lane == 0) logits[(size_t)t * E + e] = s;
 }
 
-// Softmax + greedy top-k + optional renorm + scaling for one token (one
-// warp).  Tie/NaN rules of next_router_expert (moe.rs:245-266): the first
-// maximum among not-taken experts wins, NaN scores are skipped.
-__device__ void topk_warp(const float *__restrict__ l, int E, int topk, int norm, float scaling,
-                          float *ev /* smem [E] */, unsigned *taken /* smem [(E+31)/32] */,
-                          int32_t *idx_out, float *w_out, int *bad) {
-    const int lane = threadIdx.x & 31;
-    float m = -INFINITY;
-    for (int e = lane; e < E; e += 32) m = fmaxf(m, l[e]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    for (int e = lane; e < E; e += 32) ev[e] = dexpf(__fsub_rn(l[e], m));
-    for (int i = lane; i < (E + 31) / 32; i += 32) taken[i] = 0u;
-    __syncwarp();
-    float sum = 0.0f;
-    if (lane == 0)
-        for (int e = 0; e < E; e++) sum = __fadd_rn(sum, ev[e]);
-    sum = __shfl_sync(0xffffffffu, sum, 0);
-    for (int e = lane; e < E; e += 32) ev[e] = __fdiv_rn(ev[e], sum);
-    __syncwarp();
-    float wsel[8];
-    int isel[8];
-    int fail_any = 0;
-    for (int s = 0; s < topk; s++) {
-        int be = -1;
-        float bv = 0.0f;
-        for (int e = lane; e < E; e += 32) {
-            const float v = ev[e];
-            if ((taken[e >> 5] >> (e & 31)) & 1u) continue;
-            if (v != v) continue;
-            if (be >= 0 && v <= bv) continue;
-            be = e;
-            bv = v;
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const int oe = __shfl_xor_sync(0xffffffffu, be, o);
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const bool take = oe >= 0 && (be < 0 || ov > bv || (ov == bv && oe < be));
-            if (take) {
-                be = oe;
-                bv = ov;
-            }
-        }
-        if (be < 0) {
-            fail_any = 1;
-            isel[s] = -1;
-            wsel[s] = 0.0f;
-            continue;
-        }
-        if (lane == 0) taken[be >> 5] |= 1u << (be & 31);
-        __syncwarp();
-        isel[s] = be;
-        wsel[s] = bv;
-    }
-    if (lane == 0) {
-        if (norm && !fail_any) {
-            float d = 0.0f;
-            for (int s = 0; s < topk; s++) d = __fadd_rn(d, wsel[s]);
-            d = __fadd_rn(d, 1e-20f);
-            for (int s = 0; s < topk; s++) wsel[s] = __fdiv_rn(wsel[s], d);
-        }
-        for (int s = 0; s < topk; s++) {
-            idx_out[s] = isel[s];
-            w_out[s] = __fmul_rn(wsel[s], scaling);
-        }
-        *bad = fail_any;
-    }
-}
-
 __global__ void topk_kernel(const float *__restrict__ logits, int E, int topk, int norm,
                             float scaling, int32_t *__restrict__ idx, float *__restrict__ w,
                             int32_t *err) {
-    __shared__ float ev[1024];
+    __shared__ __align__(16) float ev[1024];
     __shared__ unsigned taken[32];
+    __shared__ int32_t si[8];
+    __shared__ float sw[8];
     const int t = blockIdx.x;
     int bad = 0;
-    topk_warp(logits + (size_t)t * E, E, topk, norm, scaling, ev, taken, idx + (size_t)t * topk,
+    topk_warp(logits + (size_t)t * E, E, topk, norm, scaling, ev, taken, si, sw, idx + (size_t)t * topk,
               w + (size_t)t * topk, &bad);
     if (threadIdx.x == 0 && bad) atomicOr(err, 1);
 }
@@ -498,7 +431,7 @@ int focr_moe_destroy(focr_moe_layer *L) {
                     L->counts, L->offsets, L->pair_tok, L->pair_slot, L->act, L->amax, L->aq,
                     L->as2, L->part, L->sh_act, L->sh_amax, L->sh_as, L->sh_y, L->sh_aq, L->err,
                     L->sync, L->sched, L->xq_sorted, L->xs_sorted, L->gate_t, L->up_t, L->down_t,
-                    L->sh_gate_t, L->sh_up_t, L->sh_down_t};
+                    L->sh_gate_t, L->sh_up_t, L->sh_down_t, L->tagged};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     delete L;
@@ -566,7 +499,8 @@ int focr_moe_create(const focr_moe_config *cfg, const focr_moe_weights *wt,
     TRY(dev_alloc(&L->as2, P));
     TRY(dev_alloc(&L->part, T * K * H));
     TRY(dev_alloc(&L->err, 4));
-    TRY(dev_alloc(&L->sync, 64));
+    TRY(dev_alloc(&L->sync, 256));   // four words, one 128-byte line each
+    TRY(dev_alloc(&L->tagged, moe_fused_tagged_words(c)));
     TRY(dev_alloc(&L->sched, 2));
     TRY(dev_alloc(&L->xq_sorted, (P < 128 ? 128 : P) * H));
     TRY(dev_alloc(&L->xs_sorted, P));

@@ -41,7 +41,10 @@ struct focr_moe_layer {
     void *tc_state = nullptr;                      // tensor-core path (tensor maps)
     int32_t *err = nullptr;                        // device status word
     // fused M=1 path
-    unsigned int *sync = nullptr;                  // grid-barrier counters
+    unsigned int *sync = nullptr;                  // epoch word (fused M=1 kernel)
+    // fused M=1 kernel: (value bits, epoch) words -- [topk*inter +
+    // shared_inter] act values, then one router-logit mailbox row per CTA
+    unsigned long long *tagged = nullptr;
     int *sched = nullptr;                          // [2] tile-claim counters (gate+up, down)
     int fused_ok = 0;
 };
@@ -55,6 +58,7 @@ int moe_forward_dev(focr_moe_layer *L, const float *x, int m, const int32_t *idx
 int moe_decode_fused_m1(focr_moe_layer *L, const float *x, float *y, int32_t *idx, float *w,
                         cudaStream_t st);
 bool moe_fused_eligible(const focr_moe_layer *L);
+size_t moe_fused_tagged_words(const focr_moe_config &c);
 int moe_tc_setup(focr_moe_layer *L);
 void moe_tc_free(focr_moe_layer *L);
 int moe_tc_experts(focr_moe_layer *L, const float *x, int m, const int32_t *idx, const float *w,

@@ -26,6 +26,7 @@ enum TracePhase : uint32_t {
     TR_JOB_EPI = 5,        // epilogue sees the accumulator
     TR_JOB_EPI_DONE = 6,   // epilogue released the accumulator
     TR_KERNEL_END = 7,
+    TR_MARK = 8,           // numbered checkpoint of a single-pass kernel (job = checkpoint)
 };
 
 struct TraceBuf {
@@ -54,6 +55,18 @@ __device__ __forceinline__ void trace_event(const TraceBuf &tb, uint32_t kernel,
     e.phase = phase;
     e.ns = globaltimer_ns();
     tb.ev[i] = e;
+}
+
+// Record into a fixed slot (no counter): for kernels whose events have a
+// known place, e.g. (CTA, checkpoint); `count` is left to the caller.
+__device__ __forceinline__ void trace_event_slot(const TraceBuf &tb, unsigned long long slot,
+                                                 uint32_t kernel, uint32_t job, uint32_t phase) {
+    if (!tb.ev || slot >= tb.cap) return;
+    TraceEvent e;
+    e.tag = (kernel << 24) | ((blockIdx.x & 0xFFFu) << 12) | (job & 0xFFFu);
+    e.phase = phase;
+    e.ns = globaltimer_ns();
+    tb.ev[slot] = e;
 }
 
 }  // namespace focr
