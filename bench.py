@@ -192,6 +192,17 @@ def run_ours(args, ws, rank, local):
     if ws > 1:
         return run_ep(args, ws, rank, local)
     hbm_peak, peak_kind = peaks()
+    if args.workload == "config0":
+        m1 = m1_decode(dev, hbm_peak, peak_kind, steps=args.steps)
+        print(json.dumps({
+            "metric": "int8 MoE decode layer-tokens/s (config 0: M=1 single-token layer)",
+            "value": m1["layer_tokens_per_s"], "unit": "layer-tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": 3 * 8, "ms_per_step": m1["us_per_token_layer"] / 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 (i32 accumulate, f32 dequant)", "data": "synthetic",
+            "config": {"workload": m1["workload"], "l2": m1["l2"], "cuda_graph": m1["cuda_graph"]},
+            "roofline": m1["roofline"], "gpu_launches": args.steps}), flush=True)
+        return
     # ring of layers so that consecutive steps stream from HBM
     R = 2
     layers = [MoeLayer(synth.moe_layer(100 + r, shared_inter=SHARED), max_tokens=TOKENS)
@@ -253,6 +264,7 @@ def run_ours(args, ws, rank, local):
     h2d = TOKENS * HIDDEN * 4 + TOKENS * TOPK * 8
     d2h = TOKENS * HIDDEN * 4
 
+    m1 = None if args.no_m1 else m1_decode(dev, hbm_peak, peak_kind)
     cpu = cpu_baseline() if rank == 0 and not args.no_cpu else None
     launches_per_step = 8
     line = {
@@ -277,8 +289,60 @@ def run_ours(args, ws, rank, local):
     }
     if cpu:
         line["cpu_baseline"] = cpu
+    if m1:
+        line["m1_decode"] = m1
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def m1_decode(dev, hbm_peak, peak_kind, steps=200):
+    """Config 0 beside the headline: one token through one MoE layer
+    (64 experts, top-6 renormalised, no shared expert) with focr_moe_decode,
+    i.e. the fused single-token kernel.  A ring of 8 layers (1.8 GB) keeps
+    the weights streaming from HBM; timed as one CUDA graph of `steps`
+    decodes.  Algorithmic bytes per token-layer: 6 routed experts (weights +
+    scales) + router + x/y."""
+    import torch
+
+    from franken_ocr_b200 import synth
+    from franken_ocr_b200.moe import MoeLayer
+
+    R = 8
+    layers = [MoeLayer(synth.moe_layer(1000 + r), max_tokens=1) for r in range(R)]
+    xs = [torch.from_numpy(synth.hidden_states(50 + r, 1)).to(dev) for r in range(R)]
+    ys = [torch.empty((1, HIDDEN), device=dev) for _ in range(R)]
+    ids = [torch.empty((1, TOPK), dtype=torch.int32, device=dev) for _ in range(R)]
+    ws_ = [torch.empty((1, TOPK), device=dev) for _ in range(R)]
+
+    def step(i):
+        r = i % R
+        layers[r].decode(xs[r], ys[r], ids[r], ws_[r])
+
+    for i in range(3 * R):
+        step(i)
+    torch.cuda.synchronize()
+    graph = capture(step, range(steps))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st = torch.cuda.current_stream()
+    e0.record(st)
+    if graph is not None:
+        graph.replay()
+    else:
+        for i in range(steps):
+            step(i)
+    e1.record(st)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / steps
+    bytes_tok = 6 * expert_bytes() + NEXP * HIDDEN * 4 + 2 * HIDDEN * 4
+    achieved = bytes_tok / (us / 1e6) / 1e9
+    for L in layers:
+        L.close()
+    return {"workload": "config0_moe_layer_m1 (fused single-token kernel, moe_m1_fused_kernel)",
+            "us_per_token_layer": us, "layer_tokens_per_s": 1e6 / us,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak, "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_launch": bytes_tok},
+            "cuda_graph": graph is not None, "l2": f"ring of {R} layers x 220 MB (> L2)"}
 
 
 def capture(step, idxs):
@@ -425,6 +489,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--no-m1", action="store_true", help="skip the config-0 single-token line")
+    ap.add_argument("--workload", default="config2", choices=["config2", "config0"],
+                    help="config0: only the single-token layer (profiling runs)")
     args = ap.parse_args()
     ws, rank, local = dist_init()
     if args.impl == "reference":

@@ -57,7 +57,8 @@ constexpr int NCH = 4;             // gate/up row chunks, one mbarrier each
 constexpr uint32_t PIECE = 8192;   // bulk-copy piece
 constexpr int XPT = 4;             // x values per thread (H <= XPT * FT)
 constexpr int SLOT_PAIRS = 2;      // 16-byte tagged loads per thread for one slot (len <= 4 * FT)
-constexpr int MAX_E = FT / 8;      // the block top-k ranks each expert with 8 threads
+constexpr int MAX_E = 64;          // the block top-k: 16 warps x 4 experts
+static_assert(FT == 512, "topk_block ranks 64 experts with 16 warps");
 constexpr int MAX_CTAS = 1024;     // mailbox rows
 constexpr int MAX_COMB = 16;       // combine columns per CTA
 
@@ -142,6 +143,7 @@ struct FusedArgs {
 };
 
 struct FusedMisc {
+    __align__(16) float ev16[FW][64];   // per-warp softmax rows of the block top-k
     uint64_t bars[1 + NCH];   // [0] down rows, [1 + g] gate/up chunk g
     int seg[9][4];            // this CTA's act-row segments {slot, i0, n, r0} (thread 0)
     int nseg;
@@ -393,7 +395,7 @@ __global__ void __launch_bounds__(FT, 1) moe_m1_fused_kernel(const FusedArgs A) 
         if (lane == 0) FMARK(FM_LOGITS);
     }
     __syncthreads();
-    const int bad = topk_block(ev, E, K, A.norm, A.scaling, M.si, M.sw, M.sel_i, M.sel_w);
+    const int bad = topk_block(ev, &M.ev16[0][0], E, K, A.norm, A.scaling, M.si, M.sw, M.sel_i, M.sel_w);
     if (tid == 0) {
         int ok = 1;
         for (int j = 0; j < K; j++) ok &= M.sel_i[j] >= 0 && M.sel_i[j] < E;

@@ -195,6 +195,7 @@ struct MoeGateUp {
     // memory (named barrier 1 over the 4 epilogue warps); then thread t
     // finishes row t % 64 for columns t / 64 + 2k (k < 8): 8 independent
     // SwiGLU evaluations per thread, all loads before any store.
+    __device__ void epilogue_done(int, int) const {}
     __device__ void epilogue(const TcJob &jb, uint32_t tmem, int q, int lane, void *smem) const {
         int *acc = static_cast<int *>(smem);   // [2 halves][64 rows][17] (padded)
         const bool routed = jb.t0 >= 0;
@@ -313,6 +314,7 @@ struct MoeDown {
         jb.t3 = nv;
     }
 
+    __device__ void epilogue_done(int, int) const {}
     __device__ void epilogue(const TcJob &jb, uint32_t tmem, int q, int lane, void *) const {
         const bool routed = jb.t0 >= 0;
         const int c = jb.t1 * 128 + 32 * q + lane;

@@ -177,57 +177,67 @@ __device__ __forceinline__ void topk_warp(const float *__restrict__ l, int E, in
 
 namespace focr {
 
-// Softmax + top-k + renorm + scaling for one token with a whole CTA of at
-// least 8 * E threads (E <= 64): the same arithmetic as topk_warp (max,
-// exp, slot-ordered sum, division by warp 0), then every expert ranked by 8
-// threads at once.  `ev` holds the logits on entry (shared, 16-byte
-// aligned); si/sw: shared [topk] scratch; idx_out/w_out written by threads
-// 0..topk-1.  Returns (to every thread) 1 when fewer than topk scores are
-// finite.  Contains __syncthreads: every thread of the CTA must call it.
-__device__ __forceinline__ int topk_block(float *ev, int E, int topk, int norm, float scaling,
-                                          int32_t *si, float *sw, int32_t *idx_out, float *w_out) {
-    const int tid = threadIdx.x, lane = tid & 31;
-    if (tid < 32) {
-        float l[2];
+// Softmax + top-k + renorm + scaling for one token with a whole CTA of 512
+// threads (E <= 64): the same arithmetic as topk_warp.  Every warp computes
+// the max, the exponentials and the slot-ordered sum itself (lane 0 sums its
+// warp's own copy in ev16), so no block barrier sits inside the softmax; warp
+// w then ranks experts 4w..4w+3 with 8 lanes each through shuffles.
+// ev: shared [E] logits on entry (16-byte aligned); ev16: shared [16][64]
+// scratch (16-byte aligned); si/sw: shared [topk] scratch; idx_out/w_out
+// written by threads 0..topk-1.  Returns (to every thread) 1 when fewer than
+// topk scores are finite.  Contains __syncthreads: every thread must call it.
+__device__ __forceinline__ int topk_block(const float *ev, float *ev16, int E, int topk, int norm,
+                                          float scaling, int32_t *si, float *sw, int32_t *idx_out,
+                                          float *w_out) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const bool h0 = lane < E, h1 = lane + 32 < E;
+    const float l0 = h0 ? ev[lane] : -INFINITY, l1 = h1 ? ev[lane + 32] : -INFINITY;
+    float m = fmaxf(l0, l1);
 #pragma unroll
-        for (int k = 0; k < 2; k++) l[k] = lane + 32 * k < E ? ev[lane + 32 * k] : -INFINITY;
-        float m = fmaxf(l[0], l[1]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-#pragma unroll
-        for (int k = 0; k < 2; k++)
-            if (lane + 32 * k < E) ev[lane + 32 * k] = dexpf(__fsub_rn(l[k], m));
-        __syncwarp();
-        float sum = 0.0f;
-        if (lane == 0) sum = seq_sum(ev, E);
-        sum = __shfl_sync(0xffffffffu, sum, 0);
-#pragma unroll
-        for (int k = 0; k < 2; k++)
-            if (lane + 32 * k < E) ev[lane + 32 * k] = __fdiv_rn(ev[lane + 32 * k], sum);
-        if (lane < topk) {
-            si[lane] = -1;
-            sw[lane] = 0.0f;
-        }
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float e0 = h0 ? dexpf(__fsub_rn(l0, m)) : 0.0f, e1 = h1 ? dexpf(__fsub_rn(l1, m)) : 0.0f;
+    float *row = ev16 + warp * 64;
+    if (h0) row[lane] = e0;
+    if (h1) row[lane + 32] = e1;
+    if (tid < topk) {
+        si[tid] = -1;
+        sw[tid] = 0.0f;
     }
-    __syncthreads();
-    // rank of expert e = tid / 8 among all E: (probability desc, index asc);
-    // NaN never selected, never counted
-    const int e = tid >> 3, sub = tid & 7;
-    const float v = e < E ? ev[e] : __int_as_float(0x7fc00000);
-    const bool live = v == v;
+    __syncwarp();
+    float sum = 0.0f;
+    if (lane == 0) sum = seq_sum(row, E);
+    sum = __shfl_sync(0xffffffffu, sum, 0);
+    // probabilities; non-finite ones get key 0 (never selected, never
+    // counted: finite keys are >= 1 << 32); key = (bits + 1) << 32 | ~index
+    // orders (probability desc, index asc)
+    const float p0 = __fdiv_rn(e0, sum), p1 = __fdiv_rn(e1, sum);
+    const unsigned long long k0 =
+        h0 && p0 == p0 ? ((unsigned long long)(__float_as_uint(p0) + 1u) << 32) | (0xFFFFFFFFu - lane) : 0ull;
+    const unsigned long long k1 =
+        h1 && p1 == p1 ? ((unsigned long long)(__float_as_uint(p1) + 1u) << 32) | (0xFFFFFFFFu - lane - 32)
+                       : 0ull;
+    // expert x = 4 * warp + lane / 8; this lane compares it with experts
+    // f = sub + 8t, t < 8
+    const int x = 4 * warp + (lane >> 3), sub = lane & 7;
+    const unsigned long long kx =
+        x < 32 ? __shfl_sync(0xffffffffu, k0, x & 31) : __shfl_sync(0xffffffffu, k1, x & 31);
     int rank = 0;
-    for (int f = sub; f < E; f += 8) {
-        const float u = ev[f];
-        rank += (u > v) || (u == v && f < e);
+#pragma unroll
+    for (int t = 0; t < 8; t++) {
+        const int f = sub + 8 * t;
+        const unsigned long long kf =
+            t < 4 ? __shfl_sync(0xffffffffu, k0, f & 31) : __shfl_sync(0xffffffffu, k1, f & 31);
+        rank += kf > kx;
     }
     rank += __shfl_xor_sync(0xffffffffu, rank, 1);
     rank += __shfl_xor_sync(0xffffffffu, rank, 2);
     rank += __shfl_xor_sync(0xffffffffu, rank, 4);
-    if (sub == 0 && live && rank < topk) {
-        si[rank] = e;
-        sw[rank] = v;
+    const bool live = sub == 0 && x < E && kx != 0ull;
+    if (live && rank < topk) {
+        si[rank] = x;
+        sw[rank] = __uint_as_float((unsigned)(kx >> 32) - 1u);
     }
-    const int valid = __syncthreads_count(sub == 0 && live);
+    const int valid = __syncthreads_count(live);
     const int fail_any = valid < topk;
     if (tid < topk) {
         float d = 0.0f;

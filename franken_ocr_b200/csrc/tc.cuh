@@ -121,6 +121,28 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
         : "memory");
 }
 
+// TMA reduce-add of a shared-memory box into a 2-D global tensor (bulk
+// group completion); x, y = element coordinates of the box origin.
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *map, const void *src, int x,
+                                                  int y) {
+    asm volatile(
+        "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(x), "r"(y), "r"(smem_u32(src))
+        : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until at most N bulk groups still read shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// make generic-proxy shared-memory writes visible to the async (TMA) proxy
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ void fence_before() {
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }

@@ -41,16 +41,46 @@ int make_tmap_i8(CUtensorMap *map, const void *base, uint64_t rows, uint64_t col
     return FOCR_OK;
 }
 
-template <int BN_, int STAGES_>
+// int32 output map for the TMA reduce-add epilogue: [rows][cols] s32, box
+// 32 x 32 (128-byte rows, 128-byte swizzle).
+static int make_tmap_out_s32(CUtensorMap *map, int32_t *base, uint64_t rows, uint64_t cols) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void *fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    if (!encode) return fail(FOCR_E_CUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * 4};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_INT32, 2, base, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(FOCR_E_CUDA, "cuTensorMapEncodeTiled (out) failed");
+    return FOCR_OK;
+}
+
+// TMA_EPI: the epilogue stages each warp's 32 rows x 32 columns in a
+// swizzled shared-memory box (two per warp, alternating) and adds it onto
+// `out` with one TMA reduce-add (out must be 16-byte aligned, N % 4 == 0);
+// otherwise each lane adds its row in place.
+template <int BN_, int STAGES_, bool TMA_EPI = false>
 struct RawIgemm {
-    static constexpr int NA = 1, BN = BN_, STAGES = STAGES_, EPI_SMEM = 0, JOB_SMEM = 0;
+    static constexpr int NA = 1, BN = BN_, STAGES = STAGES_, JOB_SMEM = 0;
+    static constexpr int EPI_SMEM = TMA_EPI ? 4 * 2 * 4096 + 1024 : 0;
     static constexpr uint32_t KERNEL_ID = 1;
     static constexpr int NBUF = 512 / BN_ >= 4 ? 4 : 2;   // TMEM accumulator buffers
     TraceBuf trace;
     struct Iter {
         long tile;
     };
-    CUtensorMap ta, tb;
+    CUtensorMap ta, tb, to;
     int M, N, K, mtiles;
     long ntiles;
     int32_t *out;
@@ -83,7 +113,42 @@ struct RawIgemm {
         return true;
     }
 
-    __device__ void epilogue(const TcJob &jb, uint32_t tmem, int q, int lane, void *) const {
+    __device__ void epilogue_done(int, int lane) const {
+        if (TMA_EPI && lane == 0) tc::bulk_wait_all();
+    }
+
+    __device__ void epilogue(const TcJob &jb, uint32_t tmem, int q, int lane, void *smem) const {
+        if constexpr (TMA_EPI) {
+            uint8_t *stg = reinterpret_cast<uint8_t *>(
+                (reinterpret_cast<uintptr_t>(smem) + 1023) & ~uintptr_t(1023)) + q * 8192;
+            const int nb = (jb.t0 + 31) / 32;
+            for (int b = 0; b < nb; b++) {
+                int v[32];
+                tc::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + 32 * b, *reinterpret_cast<int(*)[16]>(v));
+                tc::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + 32 * b + 16,
+                              *reinterpret_cast<int(*)[16]>(v + 16));
+                tc::tmem_ld_wait();
+                uint8_t *box = stg + (b & 1) * 4096;
+                // the box written two iterations ago must have been read
+                if (lane == 0) tc::bulk_wait_read<1>();
+                __syncwarp();
+                // row `lane`, 16-byte chunk j at chunk j ^ (lane & 7) (128-byte swizzle)
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    *reinterpret_cast<int4 *>(box + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                        make_int4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                tc::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tc::tma_reduce_add_2d(&to, box, jb.b_row + 32 * b, jb.a_row + 32 * q);
+                    tc::bulk_commit();
+                }
+            }
+            // the staging boxes are reused by this warp's next job
+            if (lane == 0) tc::bulk_wait_read<0>();
+            __syncwarp();
+            return;
+        }
         const int row = jb.a_row + 32 * q + lane;
         const int nv = jb.t0;
         int32_t *orow = out + (size_t)row * N + jb.b_row;
@@ -110,12 +175,13 @@ bool tc_igemm_eligible(const void *A, const int8_t *B, size_t M, size_t K, size_
            K <= (size_t)INT32_MAX / 2;
 }
 
-template <int BN, int S>
+template <int BN, int S, bool TMA_EPI>
 static int run_raw(const void *A, const int8_t *B, size_t M, size_t K, size_t N, int32_t *out,
                    int *err, cudaStream_t st) {
-    RawIgemm<BN, S> p;
+    RawIgemm<BN, S, TMA_EPI> p;
     int rc = make_tmap_i8(&p.ta, A, M, K, 128);
     if (!rc) rc = make_tmap_i8(&p.tb, B, N, K, BN);
+    if (!rc && TMA_EPI) rc = make_tmap_out_s32(&p.to, out, M, N);
     if (rc) return rc;
     p.M = (int)M;
     p.N = (int)N;
@@ -140,12 +206,17 @@ int launch_tc_igemm(const void *A, bool au8, const int8_t *B, size_t M, size_t K
     int *err = tc_status_word();
     const size_t mt = (M + 127) / 128;
     const int sms = num_sms();
-    // widest tile that still gives every SM a CTA
+    // widest tile that still gives every SM a CTA; the TMA reduce-add
+    // epilogue when the output rows are 16-byte aligned
+    const bool tma_epi = N % 4 == 0 && (uintptr_t)out % 16 == 0 && !getenv("FOCR_SCALAR_EPILOGUE");
     if (N >= 256 && mt * ((N + 255) / 256) >= (size_t)sms)
-        return run_raw<256, 4>(A, B, M, K, N, out, err, st);
+        return tma_epi ? run_raw<256, 4, true>(A, B, M, K, N, out, err, st)
+                       : run_raw<256, 4, false>(A, B, M, K, N, out, err, st);
     if (N >= 128 && mt * ((N + 127) / 128) >= (size_t)sms)
-        return run_raw<128, 6>(A, B, M, K, N, out, err, st);
-    return run_raw<64, 8>(A, B, M, K, N, out, err, st);
+        return tma_epi ? run_raw<128, 6, true>(A, B, M, K, N, out, err, st)
+                       : run_raw<128, 6, false>(A, B, M, K, N, out, err, st);
+    return tma_epi ? run_raw<64, 8, true>(A, B, M, K, N, out, err, st)
+                   : run_raw<64, 8, false>(A, B, M, K, N, out, err, st);
 }
 
 }  // namespace focr

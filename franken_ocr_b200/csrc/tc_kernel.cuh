@@ -11,6 +11,7 @@
 //   __device__ bool iter_next(Iter &, TcJob &) const -- the CTA's next tile job
 //   static constexpr int EPI_SMEM -- shared-memory bytes the epilogue may use
 //   __device__ void epilogue(const TcJob &, uint32_t tmem, int quarter, int lane, void *smem) const
+//   __device__ void epilogue_done(int quarter, int lane) const  -- after the warp's last job
 //   int *err                     -- status word (bit 4: a bounded wait expired)
 // A job computes D[128 x n_mma] = sum over kblocks of A[a_row.., k] . B[b_row.., k]
 // for every A operand (accumulator a at TMEM column offset a*BN of its buffer).
@@ -188,6 +189,7 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__
             if (lane == 0) tc::mbar_arrive(&tempty[buf]);
             if (threadIdx.x == 64) trace_event(tb, KID, j, TR_JOB_EPI_DONE);
         }
+        p.epilogue_done(warp & 3, lane);
     }
     tc::fence_before();
     __syncthreads();

@@ -141,3 +141,29 @@ def test_quantize_rows_and_gemv(cuda, oracle):
     simd.gemv_i8(x, 5, 1280, w, ws, 896, y)
     for r in range(5):
         assert np.array_equal(y[r].view(np.uint32), oracle.gemv_i8(x[r], w, ws).view(np.uint32))
+
+
+@pytest.mark.parametrize("m,n,k", [(300, 1000, 256), (129, 130, 144), (257, 260, 128),
+                                   (4096, 1792, 1280), (640, 6000, 896)])
+def test_tc_accumulate_ragged(cuda, m, n, k):
+    """Tensor-core path, += onto a seeded int32 out, ragged M/N edges: the
+    TMA reduce-add epilogue (N % 4 == 0) and the per-row one (N % 4 != 0)."""
+    import torch
+
+    from franken_ocr_b200 import simd
+
+    g = torch.Generator(device="cuda").manual_seed(m + 31 * n + k)
+    a = torch.randint(-127, 128, (m, k), dtype=torch.int8, device="cuda", generator=g)
+    b = torch.randint(-127, 128, (n, k), dtype=torch.int8, device="cuda", generator=g)
+    seed = torch.randint(-1000, 1000, (m, n), dtype=torch.int32, device="cuda", generator=g)
+    out = seed.clone()
+    simd.igemm_s8s8(a, b, m, k, n, out)
+    torch.cuda.synchronize()
+    a64, b64, s64 = a.to(torch.int64).cpu(), b.to(torch.int64).cpu(), seed.to(torch.int64).cpu()
+    o64 = out.to(torch.int64).cpu()
+    if m * n * k <= 1 << 28:
+        assert torch.equal(o64, a64 @ b64.T + s64)
+    else:
+        assert torch.equal(o64.sum(1), a64 @ b64.sum(0) + s64.sum(1))
+        rows = torch.cat([torch.arange(4), torch.arange(m - 4, m)])
+        assert torch.equal(o64[rows], a64[rows] @ b64.T + s64[rows])
