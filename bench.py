@@ -192,6 +192,18 @@ def run_ours(args, ws, rank, local):
     if ws > 1:
         return run_ep(args, ws, rank, local)
     hbm_peak, peak_kind = peaks()
+    if args.workload == "config1":
+        int8_peak, rows = igemm_sweep(dev, hbm_peak, peak_kind, reps=max(1, args.steps))
+        tot_us = sum(r["us"] for r in rows)
+        print(json.dumps({
+            "metric": "int8 GEMM sweep (config 1): sum of per-shape times", "value": tot_us,
+            "unit": "us", "n_gpus": 1, "steps": args.steps, "warmup": 2,
+            "ms_per_step": tot_us / 1e3, "higher_is_better": False, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8 (i32 accumulate)", "data": "synthetic",
+            "config": {"workload": "config1_igemm_sweep", "out": "+= int32"},
+            "int8_peak_tops_own_kernel": int8_peak, "hbm_peak": hbm_peak, "peak_kind": peak_kind,
+            "shapes": rows}), flush=True)
+        return
     if args.workload == "config0":
         m1 = m1_decode(dev, hbm_peak, peak_kind, steps=args.steps)
         print(json.dumps({
@@ -345,6 +357,51 @@ def m1_decode(dev, hbm_peak, peak_kind, steps=200):
             "cuda_graph": graph is not None, "l2": f"ring of {R} layers x 220 MB (> L2)"}
 
 
+def igemm_sweep(dev, hbm_peak, peak_kind, reps=5):
+    """Config 1: the raw int8 x int8 -> int32 GEMM sweep through
+    focr_igemm_s8s8 on device tensors (out += A.B^T), each shape timed as one
+    CUDA graph of `reps` calls.  Each shape's floor is
+    max(bytes / HBM peak, ops / int8 peak); the int8 peak is the one this
+    build's own tcgen05 kernel reaches on a compute-bound shape (8192 x 8192 x
+    16384) in the same run.  Inputs: a, b uniform in [-127, 127]."""
+    import torch
+
+    from franken_ocr_b200 import simd
+
+    def timed(m, n, k):
+        g = torch.Generator(device=dev).manual_seed(m * 31 + n)
+        a = torch.randint(-127, 128, (m, k), dtype=torch.int8, device=dev, generator=g)
+        b = torch.randint(-127, 128, (n, k), dtype=torch.int8, device=dev, generator=g)
+        o = torch.zeros((m, n), dtype=torch.int32, device=dev)
+        for _ in range(2):
+            simd.igemm_s8s8(a, b, m, k, n, o)
+        torch.cuda.synchronize()
+        # one CUDA graph of `reps` calls: the host-side call cost stays out
+        graph = capture(lambda i: simd.igemm_s8s8(a, b, m, k, n, o), range(reps))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        if graph is not None:
+            graph.replay()
+        else:
+            for _ in range(reps):
+                simd.igemm_s8s8(a, b, m, k, n, o)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / reps
+
+    us_peak = timed(8192, 8192, 16384)
+    int8_peak = 2 * 8192 * 8192 * 16384 / us_peak / 1e6   # TOPS
+    rows = []
+    for (n, k) in [(1792, 1280), (1280, 896), (129280, 1280)]:
+        for m in (1, 8, 64, 512, 4096):
+            us = timed(m, n, k)
+            ops, byt = 2 * m * n * k, m * k + n * k + 8 * m * n
+            floor_us = max(byt / hbm_peak / 1e3, ops / int8_peak / 1e6)
+            rows.append({"m": m, "n": n, "k": k, "us": round(us, 2), "tops": ops / us / 1e6,
+                         "gbs": byt / us / 1e3, "floor_us": floor_us, "frac": floor_us / us})
+    return int8_peak, rows
+
+
 def capture(step, idxs):
     """One CUDA graph holding the given steps (their launches, and NCCL
     collectives for N > 1), so host-side launch overhead leaves the timed
@@ -490,8 +547,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-m1", action="store_true", help="skip the config-0 single-token line")
-    ap.add_argument("--workload", default="config2", choices=["config2", "config0"],
-                    help="config0: only the single-token layer (profiling runs)")
+    ap.add_argument("--workload", default="config2", choices=["config2", "config0", "config1"],
+                    help="config0: only the single-token layer; config1: the raw igemm sweep")
     args = ap.parse_args()
     ws, rank, local = dist_init()
     if args.impl == "reference":

@@ -104,13 +104,15 @@ template <int MT, bool AU8, int EPI>
 static void launch_rows(const int8_t *A, const int8_t *B, int M, int K, int N, int32_t *out,
                         float *y, const float *as, const float *ws, bool fast, cudaStream_t st) {
     const int warps = GEMV_THREADS / 32;
+    const unsigned chunks = (unsigned)((M + MT - 1) / MT);
+    const int mc = M < MT ? M : MT;
     if (fast) {
-        size_t smem = (size_t)M * K;
-        gemv16_kernel<MT, AU8, EPI><<<gemv_grid(N, warps * 2), GEMV_THREADS, smem, st>>>(
+        size_t smem = (size_t)mc * K;
+        gemv16_kernel<MT, AU8, EPI><<<dim3(gemv_grid(N, warps * 2), chunks), GEMV_THREADS, smem, st>>>(
             A, B, M, K, N, out, y, as, ws);
     } else {
-        size_t smem = ((size_t)M * K + 15) / 16 * 16;
-        gemv_any_kernel<MT, AU8, EPI><<<gemv_grid(N, warps), GEMV_THREADS, smem, st>>>(
+        size_t smem = ((size_t)mc * K + 15) / 16 * 16;
+        gemv_any_kernel<MT, AU8, EPI><<<dim3(gemv_grid(N, warps), chunks), GEMV_THREADS, smem, st>>>(
             A, B, M, K, N, out, y, as, ws);
     }
 }
@@ -119,7 +121,8 @@ template <bool AU8, int EPI>
 static int launch_chunk(const int8_t *A, const int8_t *B, int M, int K, int N, int32_t *out,
                         float *y, const float *as, const float *ws, cudaStream_t st) {
     const bool fast = (K % 16 == 0) && ((uintptr_t)A % 16 == 0) && ((uintptr_t)B % 16 == 0);
-    size_t smem = (size_t)M * K;
+    if (M > 65535 * 8) return fail(FOCR_E_UNSUPPORTED, "gemv: too many activation rows");
+    size_t smem = (size_t)(M < 8 ? M : 8) * K;
     static bool attr_done[2][2][4] = {};
     if (smem > 48 * 1024) {
         // opt-in to large dynamic shared memory once per instantiation
@@ -149,8 +152,8 @@ static int launch_chunk(const int8_t *A, const int8_t *B, int M, int K, int N, i
     return FOCR_OK;
 }
 
-int launch_tc_igemm(const void *A, bool au8, const int8_t *B, size_t M, size_t K, size_t N,
-                    int32_t *out, cudaStream_t st);
+int launch_tc_igemm(const void *A, size_t a_rows, bool au8, const int8_t *B, size_t M, size_t K,
+                    size_t N, int32_t *out, cudaStream_t st);
 bool tc_igemm_eligible(const void *A, const int8_t *B, size_t M, size_t K, size_t N,
                        const int32_t *out);
 
@@ -158,34 +161,35 @@ int launch_igemm(const void *A, bool au8, const int8_t *B, size_t M, size_t K, s
                  int32_t *out, cudaStream_t st) {
     if (M == 0 || N == 0) return FOCR_OK;
     if (K == 0) return FOCR_OK;  // every dot is empty: out += 0
-    if (!au8 && tc_igemm_eligible(A, B, M, K, N, out)) return launch_tc_igemm(A, au8, B, M, K, N, out, st);
+    if (!au8 && tc_igemm_eligible(A, B, M, K, N, out))
+        return launch_tc_igemm(A, M, au8, B, M, K, N, out, st);
+    // 4 < M < 128 with more than 16 rows or a large weight matrix (>= 32 MB,
+    // beyond one L2-resident pass per 8-row chunk): stage A in a zero-padded
+    // 128-row scratch and run the tensor-core path (the output rows past M
+    // are never written).  Otherwise the GEMV tier streams the weights, in
+    // 8-row chunks of one launch.
+    if (!au8 && M > 4 && M < 128 && (M > 16 || N * K >= ((size_t)32 << 20)) &&
+        tc_igemm_eligible(A, B, 128, K, N, out)) {
+        DevBuf pad;
+        FOCR_CUDA_TRY(pad.alloc(128 * K, st));
+        FOCR_CUDA_TRY(cudaMemsetAsync((uint8_t *)pad.p + M * K, 0, (128 - M) * K, st));
+        FOCR_CUDA_TRY(cudaMemcpyAsync(pad.p, A, M * K, cudaMemcpyDeviceToDevice, st));
+        return launch_tc_igemm(pad.p, 128, au8, B, M, K, N, out, st);
+    }
     if (K > (size_t)INT32_MAX || N > (size_t)INT32_MAX)
         return fail(FOCR_E_UNSUPPORTED, "igemm: dimension exceeds int32 range");
-    for (size_t m0 = 0; m0 < M; m0 += 8) {
-        const int mc = (int)((M - m0) < 8 ? (M - m0) : 8);
-        const int8_t *Ac = reinterpret_cast<const int8_t *>(A) + m0 * K;
-        int32_t *oc = out + m0 * N;
-        int rc = au8 ? launch_chunk<true, EPI_ADD_I32>(Ac, B, mc, (int)K, (int)N, oc, nullptr,
-                                                       nullptr, nullptr, st)
-                     : launch_chunk<false, EPI_ADD_I32>(Ac, B, mc, (int)K, (int)N, oc, nullptr,
-                                                        nullptr, nullptr, st);
-        if (rc) return rc;
-    }
-    return FOCR_OK;
+    return au8 ? launch_chunk<true, EPI_ADD_I32>(reinterpret_cast<const int8_t *>(A), B, (int)M,
+                                                 (int)K, (int)N, out, nullptr, nullptr, nullptr, st)
+               : launch_chunk<false, EPI_ADD_I32>(reinterpret_cast<const int8_t *>(A), B, (int)M,
+                                                  (int)K, (int)N, out, nullptr, nullptr, nullptr, st);
 }
 
 int launch_gemv_dequant(const int8_t *xq, const float *a_scale, const int8_t *B,
                         const float *w_scale, size_t M, size_t K, size_t N, float *y,
                         cudaStream_t st) {
     if (M == 0 || N == 0) return FOCR_OK;
-    for (size_t m0 = 0; m0 < M; m0 += 8) {
-        const int mc = (int)((M - m0) < 8 ? (M - m0) : 8);
-        int rc = launch_chunk<false, EPI_DEQUANT_F32>(xq + m0 * K, B, mc, (int)K, (int)N,
-                                                      nullptr, y + m0 * N, a_scale + m0,
-                                                      w_scale, st);
-        if (rc) return rc;
-    }
-    return FOCR_OK;
+    return launch_chunk<false, EPI_DEQUANT_F32>(xq, B, (int)M, (int)K, (int)N, nullptr, y, a_scale,
+                                                w_scale, st);
 }
 
 int launch_quantize_rows(const float *x, size_t M, size_t K, bool te, int8_t *xq,

@@ -29,15 +29,32 @@ __device__ __forceinline__ int dot16(const int4 a, const int4 b, int acc) {
     return acc;
 }
 
-// out[m, n] (+)= A[m,:] . B[n,:] for m < M <= MT.  Requires K % 16 == 0 and
-// 16-byte aligned A and B.  Two weight rows per warp per iteration, each
-// lane keeping GEMV_UNROLL 16-byte loads of each row in flight.
+// Rows [MT * blockIdx.y, + MT) of A (M rows in all): the grid's y dimension
+// walks chunks of MT activation rows, all chunks streaming the same weights
+// (L2-resident after the first pass) in one launch.
+#define FOCR_GEMV_CHUNK()                                                                   \
+    do {                                                                                    \
+        const int row0_ = blockIdx.y * MT;                                                  \
+        A += (size_t)row0_ * K;                                                             \
+        M = min(MT, M - row0_);                                                             \
+        if (EPI == EPI_ADD_I32)                                                             \
+            out += (size_t)row0_ * N;                                                       \
+        else {                                                                              \
+            y += (size_t)row0_ * N;                                                         \
+            a_scale += row0_;                                                               \
+        }                                                                                   \
+    } while (0)
+
+// out[m, n] (+)= A[m,:] . B[n,:] for the block's MT-row chunk.  Requires
+// K % 16 == 0 and 16-byte aligned A and B.  Two weight rows per warp per
+// iteration, each lane keeping GEMV_UNROLL 16-byte loads of each row in flight.
 template <int MT, bool AU8, int EPI>
 __global__ void __launch_bounds__(GEMV_THREADS)
 gemv16_kernel(const int8_t *__restrict__ A, const int8_t *__restrict__ B, int M, int K, int N,
               int32_t *__restrict__ out, float *__restrict__ y,
               const float *__restrict__ a_scale, const float *__restrict__ w_scale) {
     extern __shared__ int4 sA[];
+    FOCR_GEMV_CHUNK();
     const int K16 = K >> 4;
     for (int i = threadIdx.x; i < M * K16; i += blockDim.x)
         sA[i] = reinterpret_cast<const int4 *>(A)[i];
@@ -100,7 +117,7 @@ gemv16_kernel(const int8_t *__restrict__ A, const int8_t *__restrict__ B, int M,
 }
 
 // Any K, any alignment: byte-granular correctness path (selftest tails,
-// odd shapes).  One weight row per warp.
+// odd shapes).  One weight row per warp; chunks of MT rows as gemv16_kernel.
 template <int MT, bool AU8, int EPI>
 __global__ void __launch_bounds__(GEMV_THREADS)
 gemv_any_kernel(const int8_t *__restrict__ A, const int8_t *__restrict__ B, int M, int K, int N,
@@ -108,6 +125,7 @@ gemv_any_kernel(const int8_t *__restrict__ A, const int8_t *__restrict__ B, int 
                 const float *__restrict__ a_scale, const float *__restrict__ w_scale) {
     extern __shared__ int4 sAraw[];
     int8_t *sA = reinterpret_cast<int8_t *>(sAraw);
+    FOCR_GEMV_CHUNK();
     for (int i = threadIdx.x; i < M * K; i += blockDim.x) sA[i] = A[i];
     __syncthreads();
     const int lane = threadIdx.x & 31;

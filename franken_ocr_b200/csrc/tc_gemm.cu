@@ -176,10 +176,10 @@ bool tc_igemm_eligible(const void *A, const int8_t *B, size_t M, size_t K, size_
 }
 
 template <int BN, int S, bool TMA_EPI>
-static int run_raw(const void *A, const int8_t *B, size_t M, size_t K, size_t N, int32_t *out,
-                   int *err, cudaStream_t st) {
+static int run_raw(const void *A, size_t a_rows, const int8_t *B, size_t M, size_t K, size_t N,
+                   int32_t *out, int *err, cudaStream_t st) {
     RawIgemm<BN, S, TMA_EPI> p;
-    int rc = make_tmap_i8(&p.ta, A, M, K, 128);
+    int rc = make_tmap_i8(&p.ta, A, a_rows, K, 128);
     if (!rc) rc = make_tmap_i8(&p.tb, B, N, K, BN);
     if (!rc && TMA_EPI) rc = make_tmap_out_s32(&p.to, out, M, N);
     if (rc) return rc;
@@ -200,8 +200,10 @@ static int *tc_status_word() {
     return w;
 }
 
-int launch_tc_igemm(const void *A, bool au8, const int8_t *B, size_t M, size_t K, size_t N,
-                    int32_t *out, cudaStream_t st) {
+// A has a_rows >= M rows (rows past M, if any, are padding; at least 128
+// when M < 128 so every A box lies inside its tensor).
+int launch_tc_igemm(const void *A, size_t a_rows, bool au8, const int8_t *B, size_t M, size_t K,
+                    size_t N, int32_t *out, cudaStream_t st) {
     if (au8) return fail(FOCR_E_UNSUPPORTED, "tc igemm: u8 activations use the GEMV tier");
     int *err = tc_status_word();
     const size_t mt = (M + 127) / 128;
@@ -210,13 +212,13 @@ int launch_tc_igemm(const void *A, bool au8, const int8_t *B, size_t M, size_t K
     // epilogue when the output rows are 16-byte aligned
     const bool tma_epi = N % 4 == 0 && (uintptr_t)out % 16 == 0 && !getenv("FOCR_SCALAR_EPILOGUE");
     if (N >= 256 && mt * ((N + 255) / 256) >= (size_t)sms)
-        return tma_epi ? run_raw<256, 4, true>(A, B, M, K, N, out, err, st)
-                       : run_raw<256, 4, false>(A, B, M, K, N, out, err, st);
+        return tma_epi ? run_raw<256, 4, true>(A, a_rows, B, M, K, N, out, err, st)
+                       : run_raw<256, 4, false>(A, a_rows, B, M, K, N, out, err, st);
     if (N >= 128 && mt * ((N + 127) / 128) >= (size_t)sms)
-        return tma_epi ? run_raw<128, 6, true>(A, B, M, K, N, out, err, st)
-                       : run_raw<128, 6, false>(A, B, M, K, N, out, err, st);
-    return tma_epi ? run_raw<64, 8, true>(A, B, M, K, N, out, err, st)
-                   : run_raw<64, 8, false>(A, B, M, K, N, out, err, st);
+        return tma_epi ? run_raw<128, 6, true>(A, a_rows, B, M, K, N, out, err, st)
+                       : run_raw<128, 6, false>(A, a_rows, B, M, K, N, out, err, st);
+    return tma_epi ? run_raw<64, 8, true>(A, a_rows, B, M, K, N, out, err, st)
+                   : run_raw<64, 8, false>(A, a_rows, B, M, K, N, out, err, st);
 }
 
 }  // namespace focr

@@ -144,10 +144,15 @@ def test_quantize_rows_and_gemv(cuda, oracle):
 
 
 @pytest.mark.parametrize("m,n,k", [(300, 1000, 256), (129, 130, 144), (257, 260, 128),
-                                   (4096, 1792, 1280), (640, 6000, 896)])
+                                   (4096, 1792, 1280), (640, 6000, 896),
+                                   (64, 1792, 1280), (9, 700, 96), (100, 40000, 1024),
+                                   (37, 33000, 1040)])
 def test_tc_accumulate_ragged(cuda, m, n, k):
-    """Tensor-core path, += onto a seeded int32 out, ragged M/N edges: the
-    TMA reduce-add epilogue (N % 4 == 0) and the per-row one (N % 4 != 0)."""
+    """+= onto a seeded int32 out with ragged edges on every multi-row route:
+    the tensor-core path with the TMA reduce-add epilogue (N % 4 == 0) and
+    the per-row one (N % 4 != 0); 8 < M < 128 through the chunked GEMV grid
+    (small weights) and through the zero-padded tensor-core path (weights of
+    32 MB and more)."""
     import torch
 
     from franken_ocr_b200 import simd
