@@ -117,6 +117,13 @@ __device__ __forceinline__ int warp_sum_i32(int v) {
     return v;
 }
 
+// Streaming 4-byte load that does not allocate in L1.
+__device__ __forceinline__ uint32_t ld_stream_u32(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+
 // Streaming 16-byte load that does not allocate in L1 (weights are read once).
 __device__ __forceinline__ int4 ld_stream16(const void *p) {
     int4 r;

@@ -35,6 +35,10 @@ struct MoeDev {
     const float *as2, *sh_as;
     const float *w;   // routing weights [T][topk]
     float *part, *sh_y;
+    // int4 experts (group != 0): packed [E][rows][cols/2], scales [E][rows][cols/group]
+    int group;
+    const uint8_t *gate_p, *up_p, *down_p;
+    const float *gate_gs, *up_gs, *down_gs;
 };
 
 // ---------------------------------------------------------------------------
@@ -281,6 +285,125 @@ __global__ void __launch_bounds__(MOE_THREADS) expert_down_kernel(MoeDev d) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// int4 experts (group-quantised; simd/int4.rs:304-343 per projection)
+// ---------------------------------------------------------------------------
+
+// One packed weight row (K nibbles, K / GROUP groups) held by a warp: lane
+// l owns groups l, l + 32, ... (GPL of them) with their words and scales;
+// 8 words per lane cover K <= 2048.
+template <int GROUP>
+struct S4Row {
+    static constexpr int WPG = GROUP / 8;   // 32-bit words per group
+    static constexpr int GPL = 8 / WPG;     // groups per lane
+    uint32_t w[8];
+    float s[GPL];
+};
+
+template <int GROUP>
+__device__ __forceinline__ void load_s4_row(const uint8_t *prow, const float *srow, int K,
+                                            int lane, S4Row<GROUP> &r) {
+    constexpr int WPG = S4Row<GROUP>::WPG, GPL = S4Row<GROUP>::GPL;
+    const int G = K / GROUP;
+    const uint32_t *words = reinterpret_cast<const uint32_t *>(prow);
+#pragma unroll
+    for (int q = 0; q < GPL; q++) {
+        const int g = lane + 32 * q;
+        r.s[q] = g < G ? __ldg(srow + g) : 0.0f;
+#pragma unroll
+        for (int wi = 0; wi < WPG; wi++) r.w[q * WPG + wi] = g < G ? ld_stream_u32(words + g * WPG + wi) : 0u;
+    }
+}
+
+// f32 result of one packed-int4 row against int8 activations a[K]: the exact
+// int32 dot of each group, t_g = scale_g * (f32)dot_g, then acc = acc + t_g
+// in increasing g (every lane ends with the same value).
+template <int GROUP>
+__device__ __forceinline__ float s4_row_dot(const S4Row<GROUP> &r, const int8_t *a, int K,
+                                            int lane) {
+    constexpr int WPG = S4Row<GROUP>::WPG, GPL = S4Row<GROUP>::GPL;
+    const int G = K / GROUP;
+    float acc = 0.0f;
+#pragma unroll
+    for (int q = 0; q < GPL; q++) {
+        const int g0 = 32 * q;
+        if (g0 >= G) break;
+        const int g = g0 + lane;
+        int dot = 0;
+        if (g < G) {
+            const int *ar = reinterpret_cast<const int *>(a + g * GROUP);
+#pragma unroll
+            for (int wi = 0; wi < WPG; wi++) {
+                int lo, hi;
+                unpack8_s4(r.w[q * WPG + wi], lo, hi);
+                dot = dp4a_ss(ar[2 * wi], lo, dot);
+                dot = dp4a_ss(ar[2 * wi + 1], hi, dot);
+            }
+        }
+        const float t = __fmul_rn(r.s[q], (float)dot);
+        const int cnt = min(32, G - g0);
+        for (int l = 0; l < cnt; l++) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, t, l));
+    }
+    return acc;
+}
+
+// Gate + up + SwiGLU for int4 routed experts: one warp per (expert, row i),
+// its two packed rows in registers, applied to every pair routed to the
+// expert: g = packed(xq, gate) * a_scale, u likewise, act = silu(g) * u.
+template <int GROUP>
+__global__ void __launch_bounds__(MOE_THREADS) expert_gateup_s4_kernel(MoeDev d) {
+    const int lane = threadIdx.x & 31;
+    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int nw = gridDim.x * (blockDim.x >> 5);
+    const long rows = (long)d.E * d.I;
+    const int Gk = d.H / GROUP;
+    for (long r = gw; r < rows; r += nw) {
+        const int e = (int)(r / d.I), i = (int)(r % d.I);
+        const int p0 = d.offsets[e], p1 = d.offsets[e + 1];
+        if (p0 == p1) continue;
+        const size_t row = (size_t)e * d.I + i;
+        S4Row<GROUP> gr, ur;
+        load_s4_row<GROUP>(d.gate_p + row * (d.H / 2), d.gate_gs + row * Gk, d.H, lane, gr);
+        load_s4_row<GROUP>(d.up_p + row * (d.H / 2), d.up_gs + row * Gk, d.H, lane, ur);
+        for (int p = p0; p < p1; p++) {
+            const int tok = d.pair_tok[p];
+            const int8_t *xr = d.xq + (size_t)tok * d.H;
+            const float as = d.xs[tok];
+            const float g = __fmul_rn(s4_row_dot<GROUP>(gr, xr, d.H, lane), as);
+            const float u = __fmul_rn(s4_row_dot<GROUP>(ur, xr, d.H, lane), as);
+            if (lane == 0) d.act[(size_t)p * d.I + i] = __fmul_rn(silu_f(g), u);
+        }
+    }
+}
+
+// Down for int4 routed experts: one warp per (expert, output column c):
+// y = packed(aq, down) * act_scale, p = y * w_j.
+template <int GROUP>
+__global__ void __launch_bounds__(MOE_THREADS) expert_down_s4_kernel(MoeDev d) {
+    const int lane = threadIdx.x & 31;
+    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int nw = gridDim.x * (blockDim.x >> 5);
+    const long rows = (long)d.E * d.H;
+    const int Gi = d.I / GROUP;
+    for (long r = gw; r < rows; r += nw) {
+        const int e = (int)(r / d.H), c = (int)(r % d.H);
+        const int p0 = d.offsets[e], p1 = d.offsets[e + 1];
+        if (p0 == p1) continue;
+        const size_t row = (size_t)e * d.H + c;
+        S4Row<GROUP> dr;
+        load_s4_row<GROUP>(d.down_p + row * (d.I / 2), d.down_gs + row * Gi, d.I, lane, dr);
+        for (int p = p0; p < p1; p++) {
+            const float yv =
+                __fmul_rn(s4_row_dot<GROUP>(dr, d.aq + (size_t)p * d.I, d.I, lane), d.as2[p]);
+            if (lane == 0) {
+                const int tok = d.pair_tok[p], slot = d.pair_slot[p];
+                d.part[((size_t)tok * d.topk + slot) * d.H + c] =
+                    __fmul_rn(yv, d.w[(size_t)tok * d.topk + slot]);
+            }
+        }
+    }
+}
+
 // out = (((0 + p_0) + p_1) + ... + p_{k-1}) + s   (decoder.rs:2253-2261)
 // rows (optional) maps pair t*topk+j to its partial's row in `part`;
 // the shared term is added for rows t >= sh0 when sh_y is given.
@@ -331,6 +454,9 @@ static MoeDev make_dev(focr_moe_layer *L, int T, const float *w, float *part) {
     d.as2 = L->as2; d.sh_as = L->sh_as;
     d.w = w;
     d.part = part; d.sh_y = L->sh_y;
+    d.group = L->cfg.group;
+    d.gate_p = L->gate_p; d.up_p = L->up_p; d.down_p = L->down_p;
+    d.gate_gs = L->gate_gs; d.up_gs = L->up_gs; d.down_gs = L->down_gs;
     return d;
 }
 
@@ -374,9 +500,27 @@ int moe_forward_dev(focr_moe_layer *L, const float *x, int m, const int32_t *idx
         FOCR_CUDA_TRY(cudaMemsetAsync(L->part, 0, (size_t)m * K * H * sizeof(float), st));
         MoeDev d = make_dev(L, m, w, L->part);
         d.sh0 = sh0;
-        expert_gateup_kernel<<<moe_grid(), MOE_THREADS, 0, st>>>(d);
-        launch_act_quant(L, m, sh0, st);
-        expert_down_kernel<<<moe_grid(), MOE_THREADS, 0, st>>>(d);
+        if (d.group) {
+            // int4 routed experts; the shared expert stays int8 (E = 0 leaves
+            // only its rows to the int8 kernels)
+            MoeDev dsh = d;
+            dsh.E = 0;
+            if (d.group == 16)
+                expert_gateup_s4_kernel<16><<<moe_grid(), MOE_THREADS, 0, st>>>(d);
+            else
+                expert_gateup_s4_kernel<32><<<moe_grid(), MOE_THREADS, 0, st>>>(d);
+            if (d.S && m > sh0) expert_gateup_kernel<<<moe_grid(), MOE_THREADS, 0, st>>>(dsh);
+            launch_act_quant(L, m, sh0, st);
+            if (d.group == 16)
+                expert_down_s4_kernel<16><<<moe_grid(), MOE_THREADS, 0, st>>>(d);
+            else
+                expert_down_s4_kernel<32><<<moe_grid(), MOE_THREADS, 0, st>>>(d);
+            if (d.S && m > sh0) expert_down_kernel<<<moe_grid(), MOE_THREADS, 0, st>>>(dsh);
+        } else {
+            expert_gateup_kernel<<<moe_grid(), MOE_THREADS, 0, st>>>(d);
+            launch_act_quant(L, m, sh0, st);
+            expert_down_kernel<<<moe_grid(), MOE_THREADS, 0, st>>>(d);
+        }
     }
     dim3 gc((H + 255) / 256, m);
     FOCR_CUDA_TRY(launch_pdl(combine_kernel, gc, dim3(256), 0, st, (const float *)L->part,
@@ -455,7 +599,10 @@ int focr_moe_create(const focr_moe_config *cfg, const focr_moe_weights *wt,
         return fail(FOCR_E_ARG, "moe_create: bad expert_begin/expert_count");
     if (c.max_tokens == 0 || c.max_tokens > 65536)
         return fail(FOCR_E_ARG, "moe_create: max_tokens must be 1..65536");
-    if (c.group != 0) return fail(FOCR_E_UNSUPPORTED, "moe_create: int4 experts not built yet");
+    if (c.group != 0 && c.group != 16 && c.group != 32)
+        return fail(FOCR_E_ARG, "moe_create: group must be 0 (int8), 16 or 32 (int4)");
+    if (c.group && (c.hidden % c.group || c.inter % c.group))
+        return fail(FOCR_E_SHAPE, "moe_create: group must divide hidden and inter");
     focr_moe_layer *L = new focr_moe_layer();
     L->cfg = c;
     L->E = c.expert_count;
@@ -463,12 +610,22 @@ int focr_moe_create(const focr_moe_config *cfg, const focr_moe_weights *wt,
     const size_t H = c.hidden, I = c.inter, S = c.shared_inter, E = c.expert_count;
     const size_t T = c.max_tokens, K = c.topk, P = T * K;
     TRY(dev_upload(&L->router, wt->router, (size_t)c.n_experts * H));
-    TRY(dev_upload(&L->gate_w, wt->gate_w, E * I * H));
-    TRY(dev_upload(&L->up_w, wt->up_w, E * I * H));
-    TRY(dev_upload(&L->down_w, wt->down_w, E * H * I));
-    TRY(dev_upload(&L->gate_s, wt->gate_s, E * I));
-    TRY(dev_upload(&L->up_s, wt->up_s, E * I));
-    TRY(dev_upload(&L->down_s, wt->down_s, E * H));
+    if (c.group) {
+        const size_t g = c.group;
+        TRY(dev_upload(&L->gate_p, wt->gate_p, E * I * (H / 2)));
+        TRY(dev_upload(&L->up_p, wt->up_p, E * I * (H / 2)));
+        TRY(dev_upload(&L->down_p, wt->down_p, E * H * (I / 2)));
+        TRY(dev_upload(&L->gate_gs, wt->gate_gs, E * I * (H / g)));
+        TRY(dev_upload(&L->up_gs, wt->up_gs, E * I * (H / g)));
+        TRY(dev_upload(&L->down_gs, wt->down_gs, E * H * (I / g)));
+    } else {
+        TRY(dev_upload(&L->gate_w, wt->gate_w, E * I * H));
+        TRY(dev_upload(&L->up_w, wt->up_w, E * I * H));
+        TRY(dev_upload(&L->down_w, wt->down_w, E * H * I));
+        TRY(dev_upload(&L->gate_s, wt->gate_s, E * I));
+        TRY(dev_upload(&L->up_s, wt->up_s, E * I));
+        TRY(dev_upload(&L->down_s, wt->down_s, E * H));
+    }
     if (S) {
         TRY(dev_upload(&L->sh_gate_w, wt->sh_gate_w, S * H));
         TRY(dev_upload(&L->sh_up_w, wt->sh_up_w, S * H));
@@ -507,7 +664,7 @@ int focr_moe_create(const focr_moe_config *cfg, const focr_moe_weights *wt,
     // Tensor-core expert path: every TMA box (128 rows x 128 bytes) fits inside
     // its tensor when hidden/inter/shared_inter are multiples of 128 (all model
     // shapes are); other shapes use the GEMV-grouped kernels.
-    if (!getenv("FOCR_DISABLE_TC") && H % 128 == 0 && I % 128 == 0 && S % 128 == 0)
+    if (!c.group && !getenv("FOCR_DISABLE_TC") && H % 128 == 0 && I % 128 == 0 && S % 128 == 0)
         TRY(moe_tc_setup(L));
     L->fused_ok = moe_fused_eligible(L) ? 1 : 0;
     *out = L;

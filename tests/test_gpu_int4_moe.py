@@ -1,0 +1,56 @@
+"""GPU parity of the MoE layer with int4 group-quantised experts (config 4):
+every routed projection is the packed int4 GEMM of simd/int4.rs:304-343
+(exact int32 per group, f32 accumulation over groups in increasing order)
+dequantised by the activation scale; the shared expert stays int8.  The
+oracle's expert_s4 defines the driver (the reference ships the primitive,
+not an int4 expert)."""
+import numpy as np
+import pytest
+
+from tests.test_gpu_moe import assert_close_rel
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("group,shared", [(32, 0), (16, 0), (32, 1792)])
+@pytest.mark.parametrize("m", [1, 5, 16])
+def test_int4_decode_matches_oracle(cuda, oracle, group, shared, m):
+    from franken_ocr_b200 import synth
+    from franken_ocr_b200.moe import MoeLayer
+    from oracle.oracle import MoeOracle
+
+    W = synth.moe_layer(4000 + group + shared, shared_inter=shared, group=group)
+    L = MoeLayer(W, max_tokens=m)
+    O = MoeOracle(W)
+    for step in range(2):
+        x = synth.hidden_states(600 + step, m)
+        y, idx, w = L.decode(x)
+        rc, oy, oi, ow = O.decode(x)
+        assert rc == 0
+        assert np.array_equal(idx, oi)
+        # the router's exp is correctly rounded on the device and libm's expf
+        # in the oracle; a 1-ulp routing weight changes a whole token row of
+        # p_j = y * w_j, so the exact fraction is per token, the bound is not
+        assert_close_rel(y, oy, f"int4 g{group} m={m}", min_exact=0.5)
+        # with the oracle's own routing the expert path is bit-identical
+        yf = L.forward(x, oi, ow)
+        assert np.array_equal(yf.view(np.uint32), O.forward(x, oi, ow).view(np.uint32))
+    L.close()
+
+
+def test_int4_forward_routed_zipf(cuda, oracle):
+    """Batched forward with given (Zipf) routing: experts with many tokens."""
+    from franken_ocr_b200 import synth
+    from franken_ocr_b200.moe import MoeLayer
+    from oracle.oracle import MoeOracle
+
+    m = 48
+    W = synth.moe_layer(4100, group=32, shared_inter=896)
+    L = MoeLayer(W, max_tokens=m)
+    x = synth.hidden_states(601, m)
+    idx, w = synth.zipf_routing(601, m)
+    y = L.forward(x, idx, w)
+    want = MoeOracle(W).forward(x, idx, w)
+    assert np.array_equal(y.view(np.uint32), want.view(np.uint32)), "int4 forward m=48"
+    assert_close_rel(y, want, "int4 forward m=48", min_exact=1.0)
+    L.close()
