@@ -27,7 +27,7 @@ EXPORTS = [
     "focr_last_error", "focr_tier_string", "focr_igemm_s8s8", "focr_igemm_u8s8",
     "focr_igemm_s4s8_packed", "focr_quantize_rows_i8", "focr_gemv_i8", "focr_gemv_i8_noalloc",
     "focr_moe_create", "focr_moe_destroy", "focr_moe_route", "focr_moe_forward",
-    "focr_moe_decode", "focr_moe_forward_rows", "focr_moe_combine", "focr_ep_pack",
+    "focr_moe_decode", "focr_moe_prefill", "focr_moe_forward_rows", "focr_moe_combine", "focr_ep_pack",
     "focr_lmhead_create", "focr_lmhead_destroy", "focr_lmhead_top1",
     "focr_top1_combine", "focr_selftest", "focr_trace_set",
 ]
@@ -83,6 +83,7 @@ lib.focr_moe_destroy.argtypes = [vp]
 lib.focr_moe_route.argtypes = [vp, vp, sz, vp, vp, i32, vp]
 lib.focr_moe_forward.argtypes = [vp, vp, sz, vp, vp, vp, i32, vp]
 lib.focr_moe_decode.argtypes = [vp, vp, sz, vp, vp, vp, i32, vp]
+lib.focr_moe_prefill.argtypes = [vp, vp, sz, vp, vp, vp, i32, vp]
 lib.focr_moe_combine.argtypes = [vp, vp, vp, sz, sz, sz, vp, vp]
 lib.focr_moe_forward_rows.argtypes = [vp, vp, sz, vp, vp, vp, sz, vp]
 lib.focr_ep_pack.argtypes = [vp, vp, vp, sz, sz, sz, sz, sz, sz, vp, vp, vp, vp, vp, vp, vp]

@@ -211,7 +211,7 @@ __global__ void __launch_bounds__(MOE_THREADS) expert_gateup_kernel(MoeDev d) {
 // Requantise activation rows (pairs, then shared tokens).  One block per row;
 // rows >= the live pair count are skipped.
 __global__ void act_quant_kernel(const float *__restrict__ act, int I, const int32_t *__restrict__ count,
-                                 int8_t *__restrict__ aq, float *__restrict__ as) {
+                                 int8_t *__restrict__ aq, float *__restrict__ as, int te) {
     if (count && (int)blockIdx.x >= *count) return;
     __shared__ float red[32];
     __shared__ float s_inv;
@@ -232,7 +232,7 @@ __global__ void act_quant_kernel(const float *__restrict__ act, int I, const int
     }
     __syncthreads();
     const float inv = s_inv;
-    for (int i = threadIdx.x; i < I; i += blockDim.x) q[i] = (int8_t)quant_i8(row[i], inv, false);
+    for (int i = threadIdx.x; i < I; i += blockDim.x) q[i] = (int8_t)quant_i8(row[i], inv, te != 0);
 }
 
 // Down GEMV: one warp per down row c of a local expert (K = I) or of the
@@ -406,17 +406,34 @@ __global__ void __launch_bounds__(MOE_THREADS) expert_down_s4_kernel(MoeDev d) {
 
 // out = (((0 + p_0) + p_1) + ... + p_{k-1}) + s   (decoder.rs:2253-2261)
 // rows (optional) maps pair t*topk+j to its partial's row in `part`;
-// the shared term is added for rows t >= sh0 when sh_y is given.
+// the shared term is added for rows t >= sh0 when sh_y is given.  With
+// order_idx (the routing), the slots are summed in ascending expert id
+// instead: moe_block_i8's `out[t] += w * y` over experts (decoder.rs:2164-2175).
 __global__ void combine_kernel(const float *__restrict__ part, const int32_t *__restrict__ rows,
                                const float *__restrict__ sh_y, int sh0, int H, int topk,
-                               float *__restrict__ y) {
+                               float *__restrict__ y, const int32_t *__restrict__ order_idx) {
     pdl_wait();
     pdl_trigger();
     const int t = blockIdx.y;
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= H) return;
+    int ord[8];
+    for (int j = 0; j < topk; j++) ord[j] = j;
+    if (order_idx) {   // insertion sort of <= 8 slots by expert id
+        const int32_t *ti = order_idx + (size_t)t * topk;
+        for (int j = 1; j < topk; j++) {
+            const int v = ord[j];
+            int q = j - 1;
+            while (q >= 0 && ti[ord[q]] > ti[v]) {
+                ord[q + 1] = ord[q];
+                q--;
+            }
+            ord[q + 1] = v;
+        }
+    }
     float o = 0.0f;
-    for (int j = 0; j < topk; j++) {
+    for (int jj = 0; jj < topk; jj++) {
+        const int j = ord[jj];
         const size_t pr = rows ? (size_t)rows[(size_t)t * topk + j] : (size_t)t * topk + j;
         o = __fadd_rn(o, part[pr * H + c]);
     }
@@ -462,13 +479,13 @@ static MoeDev make_dev(focr_moe_layer *L, int T, const float *w, float *part) {
 
 static int moe_grid() { return num_sms() * 8; }
 
-void launch_act_quant(focr_moe_layer *L, int m, int sh0, cudaStream_t st) {
+void launch_act_quant(focr_moe_layer *L, int m, int sh0, cudaStream_t st, bool te) {
     act_quant_kernel<<<m * L->cfg.topk, 256, 0, st>>>(L->act, L->cfg.inter, L->offsets + L->E,
-                                                      L->aq, L->as2);
+                                                      L->aq, L->as2, (int)te);
     const size_t S = L->cfg.shared_inter;
     if (S && m > sh0)
         act_quant_kernel<<<m - sh0, 256, 0, st>>>(L->sh_act + sh0 * S, (int)S, nullptr,
-                                                  L->sh_aq + sh0 * S, L->sh_as + sh0);
+                                                  L->sh_aq + sh0 * S, L->sh_as + sh0, (int)te);
 }
 
 int moe_route_dev(focr_moe_layer *L, const float *x, int m, int32_t *idx, float *w,
@@ -483,16 +500,16 @@ int moe_route_dev(focr_moe_layer *L, const float *x, int m, int32_t *idx, float 
 }
 
 int moe_forward_dev(focr_moe_layer *L, const float *x, int m, const int32_t *idx,
-                    const float *w, float *y, cudaStream_t st, int sh0) {
+                    const float *w, float *y, cudaStream_t st, int sh0, bool prefill) {
     const int H = L->cfg.hidden, K = L->cfg.topk;
     int rc;
     if (L->tc_state) {
-        rc = moe_tc_experts(L, x, m, idx, w, sh0, st);
+        rc = moe_tc_experts(L, x, m, idx, w, sh0, st, prefill);
         if (rc) return rc;
     } else {
         check_idx_kernel<<<1, 256, 0, st>>>(idx, m * K, (int)L->cfg.expert_begin,
                                             (int)(L->cfg.expert_begin + L->E), L->err);
-        rc = launch_quantize_rows(x, m, H, false, L->xq, L->xs, st);
+        rc = launch_quantize_rows(x, m, H, prefill, L->xq, L->xs, st);
         if (rc) return rc;
         bucket_kernel<<<1, 1024, 0, st>>>(idx, m, K, L->E, L->cfg.expert_begin, L->offsets,
                                           L->pair_tok, L->pair_slot);
@@ -510,7 +527,7 @@ int moe_forward_dev(focr_moe_layer *L, const float *x, int m, const int32_t *idx
             else
                 expert_gateup_s4_kernel<32><<<moe_grid(), MOE_THREADS, 0, st>>>(d);
             if (d.S && m > sh0) expert_gateup_kernel<<<moe_grid(), MOE_THREADS, 0, st>>>(dsh);
-            launch_act_quant(L, m, sh0, st);
+            launch_act_quant(L, m, sh0, st, prefill);
             if (d.group == 16)
                 expert_down_s4_kernel<16><<<moe_grid(), MOE_THREADS, 0, st>>>(d);
             else
@@ -518,7 +535,7 @@ int moe_forward_dev(focr_moe_layer *L, const float *x, int m, const int32_t *idx
             if (d.S && m > sh0) expert_down_kernel<<<moe_grid(), MOE_THREADS, 0, st>>>(dsh);
         } else {
             expert_gateup_kernel<<<moe_grid(), MOE_THREADS, 0, st>>>(d);
-            launch_act_quant(L, m, sh0, st);
+            launch_act_quant(L, m, sh0, st, prefill);
             expert_down_kernel<<<moe_grid(), MOE_THREADS, 0, st>>>(d);
         }
     }
@@ -526,7 +543,7 @@ int moe_forward_dev(focr_moe_layer *L, const float *x, int m, const int32_t *idx
     FOCR_CUDA_TRY(launch_pdl(combine_kernel, gc, dim3(256), 0, st, (const float *)L->part,
                              (const int32_t *)nullptr,
                              (const float *)(L->cfg.shared_inter ? L->sh_y : nullptr), sh0, H, K,
-                             y));
+                             y, prefill ? idx : (const int32_t *)nullptr));
     return FOCR_OK;
 }
 
@@ -754,6 +771,36 @@ int focr_moe_decode(focr_moe_layer *L, const float *x, size_t m, float *y, int32
     return FOCR_OK;
 }
 
+int focr_moe_prefill(focr_moe_layer *L, const float *x, size_t m, float *y, int32_t *idx,
+                     float *w, int mem, void *stream) {
+    if (!L) return fail(FOCR_E_ARG, "moe_prefill: null layer");
+    if (m == 0) return FOCR_OK;
+    if (m > L->cfg.max_tokens) return fail(FOCR_E_SHAPE, "moe_prefill: m > max_tokens");
+    if (L->E != L->cfg.n_experts)
+        return fail(FOCR_E_ARG, "moe_prefill: layer holds a subset of experts");
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t H = L->cfg.hidden, K = L->cfg.topk;
+    const float *dx = x;
+    float *dy = y;
+    if (mem == FOCR_MEM_HOST) {
+        FOCR_CUDA_TRY(cudaMemcpyAsync(L->x, x, m * H * 4, cudaMemcpyHostToDevice, st));
+        dx = L->x;
+        dy = L->y;
+    }
+    int32_t *di = (mem == FOCR_MEM_DEVICE && idx) ? idx : L->idx;
+    float *dw = (mem == FOCR_MEM_DEVICE && w) ? w : L->w;
+    int rc = moe_route_dev(L, dx, (int)m, di, dw, st);
+    if (!rc) rc = moe_forward_dev(L, dx, (int)m, di, dw, dy, st, 0, true);
+    if (rc) return rc;
+    if (mem == FOCR_MEM_HOST) {
+        FOCR_CUDA_TRY(cudaMemcpyAsync(y, L->y, m * H * 4, cudaMemcpyDeviceToHost, st));
+        if (idx) FOCR_CUDA_TRY(cudaMemcpyAsync(idx, L->idx, m * K * 4, cudaMemcpyDeviceToHost, st));
+        if (w) FOCR_CUDA_TRY(cudaMemcpyAsync(w, L->w, m * K * 4, cudaMemcpyDeviceToHost, st));
+        return read_status(L, st);
+    }
+    return FOCR_OK;
+}
+
 int focr_moe_combine(const float *part, const int32_t *rows, const float *shared, size_t m,
                      size_t topk, size_t hidden, float *y, void *stream) {
     if (m == 0 || hidden == 0) return FOCR_OK;
@@ -762,7 +809,7 @@ int focr_moe_combine(const float *part, const int32_t *rows, const float *shared
         return fail(FOCR_E_UNSUPPORTED, "moe_combine: shape too large");
     dim3 gc((unsigned)((hidden + 255) / 256), (unsigned)m);
     FOCR_CUDA_TRY(launch_pdl(combine_kernel, gc, dim3(256), 0, (cudaStream_t)stream, part, rows,
-                             shared, 0, (int)hidden, (int)topk, y));
+                             shared, 0, (int)hidden, (int)topk, y, (const int32_t *)nullptr));
     return FOCR_OK;
 }
 

@@ -53,8 +53,12 @@ namespace focr {
 
 int moe_route_dev(focr_moe_layer *L, const float *x, int m, int32_t *idx, float *w,
                   cudaStream_t st);
+// prefill: moe_block_i8 semantics (decoder.rs:2142-2181) -- ties-even
+// activation quantisation and each token's partials summed in ascending
+// expert order; otherwise decode_mlp_i8's (half-away quantisation, slot order)
 int moe_forward_dev(focr_moe_layer *L, const float *x, int m, const int32_t *idx,
-                    const float *w, float *y, cudaStream_t st, int sh0 = 0);
+                    const float *w, float *y, cudaStream_t st, int sh0 = 0,
+                    bool prefill = false);
 int moe_decode_fused_m1(focr_moe_layer *L, const float *x, float *y, int32_t *idx, float *w,
                         cudaStream_t st);
 bool moe_fused_eligible(const focr_moe_layer *L);
@@ -62,7 +66,7 @@ size_t moe_fused_tagged_words(const focr_moe_config &c);
 int moe_tc_setup(focr_moe_layer *L);
 void moe_tc_free(focr_moe_layer *L);
 int moe_tc_experts(focr_moe_layer *L, const float *x, int m, const int32_t *idx, const float *w,
-                   int sh0, cudaStream_t st);
-void launch_act_quant(focr_moe_layer *L, int m, int sh0, cudaStream_t st);
+                   int sh0, cudaStream_t st, bool te = false);
+void launch_act_quant(focr_moe_layer *L, int m, int sh0, cudaStream_t st, bool te = false);
 
 }  // namespace focr

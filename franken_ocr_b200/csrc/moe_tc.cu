@@ -374,7 +374,7 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(
     int32_t *__restrict__ offsets, int32_t *__restrict__ pair_tok,
     int32_t *__restrict__ pair_slot, int8_t *__restrict__ xq_sorted,
     float *__restrict__ xs_sorted, int32_t *__restrict__ active, int *__restrict__ sched,
-    float *__restrict__ part, int32_t *err) {
+    float *__restrict__ part, int32_t *err, int te) {
     __shared__ int cnt[1025];
     __shared__ int rank[8];
     __shared__ float red[8];
@@ -477,7 +477,7 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(
 #pragma unroll
     for (int u = 0; u < V; u++) {
         const int i = tid + u * 256;
-        if (i < H) qrow[i] = (int8_t)quant_i8(v[u], inv, false);
+        if (i < H) qrow[i] = (int8_t)quant_i8(v[u], inv, te != 0);
     }
     __syncthreads();
     // scatter this token's pairs and copy its quantised row to each pair slot;
@@ -566,7 +566,7 @@ __global__ void gather_pairs_kernel(const int8_t *__restrict__ xq, const float *
 __global__ void __launch_bounds__(128) act_quant_rows_kernel(
     const float *__restrict__ act, int I, int P, const int32_t *__restrict__ count,
     int8_t *__restrict__ aq, float *__restrict__ as, const float *__restrict__ sh_act, int S,
-    int T, int sh0, int8_t *__restrict__ sh_aq, float *__restrict__ sh_as) {
+    int T, int sh0, int8_t *__restrict__ sh_aq, float *__restrict__ sh_as, int te) {
     __shared__ float red[4];
     pdl_wait();
     pdl_trigger();
@@ -611,7 +611,7 @@ __global__ void __launch_bounds__(128) act_quant_rows_kernel(
 #pragma unroll
     for (int u = 0; u < V; u++) {
         const int i = threadIdx.x + u * 128;
-        if (i < K) q[i] = (int8_t)quant_i8(v[u], inv, false);
+        if (i < K) q[i] = (int8_t)quant_i8(v[u], inv, te != 0);
     }
     if (threadIdx.x == 0) *sc = s;
 }
@@ -742,7 +742,7 @@ void moe_tc_free(focr_moe_layer *L) {
 // Quantise + bucket + gather, then the two tensor-core GEMMs and the
 // activation requantisation between them.
 int moe_tc_experts(focr_moe_layer *L, const float *x, int m, const int32_t *idx, const float *w,
-                   int sh0, cudaStream_t st) {
+                   int sh0, cudaStream_t st, bool te) {
     MoeTcState *s = static_cast<MoeTcState *>(L->tc_state);
     const int H = L->cfg.hidden, K = L->cfg.topk, S = L->cfg.shared_inter;
     const int P = m * K;
@@ -750,9 +750,9 @@ int moe_tc_experts(focr_moe_layer *L, const float *x, int m, const int32_t *idx,
         FOCR_CUDA_TRY(launch_pdl(moe_prep_kernel, dim3(m), dim3(256), 0, st, x, idx, m, H, K,
                                  (int)L->E, (int)L->cfg.expert_begin, L->xq, L->xs, L->offsets,
                                  L->pair_tok, L->pair_slot, L->xq_sorted, L->xs_sorted, L->counts,
-                                 L->sched, L->part, L->err));
+                                 L->sched, L->part, L->err, (int)te));
     } else {
-        int rc = launch_quantize_rows(x, m, H, false, L->xq, L->xs, st);
+        int rc = launch_quantize_rows(x, m, H, te, L->xq, L->xs, st);
         if (rc) return rc;
         moe_bucket_kernel<<<1, 1024, 0, st>>>(idx, m, K, (int)L->E, (int)L->cfg.expert_begin,
                                               L->offsets, L->pair_tok, L->pair_slot, L->counts,
@@ -775,7 +775,7 @@ int moe_tc_experts(focr_moe_layer *L, const float *x, int m, const int32_t *idx,
                              (const float *)L->act, (int)L->cfg.inter, P,
                              (const int32_t *)(L->offsets + L->E), L->aq, L->as2,
                              (const float *)L->sh_act, S, S ? m - sh0 : 0, sh0, L->sh_aq,
-                             L->sh_as));
+                             L->sh_as, (int)te));
     MoeDown d = s->dn;
     d.T = m;
     d.sh0 = sh0;

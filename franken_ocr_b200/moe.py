@@ -117,3 +117,15 @@ class MoeLayer:
         check(lib.focr_moe_decode(self._h, _ptr(x), m, _ptr(y), _ptr(idx), _ptr(w), mem,
                                   _stream(mem)))
         return y, idx, w
+
+    def prefill(self, x, y=None, idx=None, w=None):
+        """moe_block_i8 (decoder.rs:2142-2181): ties-even activation
+        quantisation, partials summed in ascending expert order."""
+        m = x.shape[0]
+        y = self._out(x, (m, self.hidden), np.float32) if y is None else y
+        idx = self._out(x, (m, self.topk), np.int32) if idx is None else idx
+        w = self._out(x, (m, self.topk), np.float32) if w is None else w
+        mem = _mem(x)
+        check(lib.focr_moe_prefill(self._h, _ptr(x), m, _ptr(y), _ptr(idx), _ptr(w), mem,
+                                   _stream(mem)))
+        return y, idx, w

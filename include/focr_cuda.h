@@ -161,6 +161,14 @@ int focr_moe_forward(focr_moe_layer *layer, const float *x, size_t m,
 int focr_moe_decode(focr_moe_layer *layer, const float *x, size_t m, float *y,
                     int32_t *idx, float *w, int mem, void *stream);
 
+/* Prefill MoE block over m tokens -- replaces moe_block_i8
+ * (native_engine/decoder.rs:2142-2181): route, then per expert in ascending
+ * id the SwiGLU expert of its tokens (activations quantised ties-to-even,
+ * the prefill convention of decoder.rs:1647-1656), out[t] += w * y in that
+ * expert order, then + shared(x[t]).  idx/w outputs may be NULL. */
+int focr_moe_prefill(focr_moe_layer *layer, const float *x, size_t m, float *y,
+                     int32_t *idx, float *w, int mem, void *stream);
+
 /* focr_moe_forward with the shared expert applied only to rows
  * [shared_begin, m) (rows below get none).  Routing ids < 0 mark empty slots
  * (no expert; they contribute +0).  Device pointers.  Used by expert

@@ -216,21 +216,30 @@ void oracle_gemv_i8(const float *x, const int8_t *w, const float *w_scale,
 /* decoder.rs:1744-1755 expert_gemv_i8_serial (and :1711 expert_gemv_i8,
  * numerically identical: both quantise x once per GEMV with the same fn).
  * act[i] = silu(g[i]) * u[i]; act re-quantised; y = gemv(down). */
-void oracle_expert_i8(const float *x, size_t hidden, size_t inter,
-                      const int8_t *gate_w, const float *gate_s,
-                      const int8_t *up_w, const float *up_s,
-                      const int8_t *down_w, const float *down_s, float *y) {
+static void expert_i8_q(const float *x, size_t hidden, size_t inter,
+                        const int8_t *gate_w, const float *gate_s,
+                        const int8_t *up_w, const float *up_s,
+                        const int8_t *down_w, const float *down_s, int te, float *y) {
+    float (*quant)(const float *, size_t, int8_t *) =
+        te ? oracle_quantize_row_i8_te : oracle_quantize_row_i8;
     int8_t *xq = (int8_t *)malloc(hidden);
     float *g = (float *)malloc(inter * sizeof(float));
     float *u = (float *)malloc(inter * sizeof(float));
     int8_t *aq = (int8_t *)malloc(inter);
-    float a_scale = oracle_quantize_row_i8(x, hidden, xq);
+    float a_scale = quant(x, hidden, xq);
     oracle_gemv_i8_prequant(xq, a_scale, gate_w, gate_s, inter, hidden, g);
     oracle_gemv_i8_prequant(xq, a_scale, up_w, up_s, inter, hidden, u);
     for (size_t i = 0; i < inter; i++) g[i] = oracle_silu(g[i]) * u[i];
-    float s2 = oracle_quantize_row_i8(g, inter, aq);
+    float s2 = quant(g, inter, aq);
     oracle_gemv_i8_prequant(aq, s2, down_w, down_s, hidden, inter, y);
     free(xq); free(g); free(u); free(aq);
+}
+
+void oracle_expert_i8(const float *x, size_t hidden, size_t inter,
+                      const int8_t *gate_w, const float *gate_s,
+                      const int8_t *up_w, const float *up_s,
+                      const int8_t *down_w, const float *down_s, float *y) {
+    expert_i8_q(x, hidden, inter, gate_w, gate_s, up_w, up_s, down_w, down_s, 0, y);
 }
 
 /* int4 expert: the same SwiGLU expert with every GEMV replaced by the packed
@@ -239,19 +248,21 @@ void oracle_expert_i8(const float *x, size_t hidden, size_t inter,
  * primitive but no int4 expert driver; this is this project's definition. */
 static void expert_s4(const float *x, size_t hidden, size_t inter, size_t group,
                       const uint8_t *gp, const float *gs, const uint8_t *up,
-                      const float *us, const uint8_t *dp, const float *ds, float *y) {
+                      const float *us, const uint8_t *dp, const float *ds, int te, float *y) {
+    float (*quant)(const float *, size_t, int8_t *) =
+        te ? oracle_quantize_row_i8_te : oracle_quantize_row_i8;
     int8_t *xq = (int8_t *)malloc(hidden);
     float *g = (float *)malloc(inter * sizeof(float));
     float *u = (float *)malloc(inter * sizeof(float));
     int8_t *aq = (int8_t *)malloc(inter);
-    float a_scale = oracle_quantize_row_i8(x, hidden, xq);
+    float a_scale = quant(x, hidden, xq);
     oracle_igemm_s4s8_packed(xq, gp, gs, group, 1, hidden, inter, g);
     oracle_igemm_s4s8_packed(xq, up, us, group, 1, hidden, inter, u);
     for (size_t i = 0; i < inter; i++) {
         float gi = g[i] * a_scale, ui = u[i] * a_scale;
         g[i] = oracle_silu(gi) * ui;
     }
-    float s2 = oracle_quantize_row_i8(g, inter, aq);
+    float s2 = quant(g, inter, aq);
     oracle_igemm_s4s8_packed(aq, dp, ds, group, 1, inter, hidden, y);
     for (size_t o = 0; o < hidden; o++) y[o] = y[o] * s2;
     free(xq); free(g); free(u); free(aq);
@@ -359,19 +370,19 @@ int oracle_route(const float *x, size_t n_tok, size_t hidden, const float *gate,
 /* the batched reference semantics decoder.rs:2812-2933 (MoE per stream). */
 /* ===================================================================== */
 
-static void expert_dispatch(const oracle_moe_layer *L, int e, const float *x, float *y) {
+static void expert_dispatch(const oracle_moe_layer *L, int e, const float *x, int te, float *y) {
     size_t H = L->hidden, I = L->inter;
     if (L->group) {
         size_t gk = H / L->group, gi = I / L->group;
         expert_s4(x, H, I, L->group,
                   L->gate_p + (size_t)e * I * (H / 2), L->gate_gs + (size_t)e * I * gk,
                   L->up_p + (size_t)e * I * (H / 2), L->up_gs + (size_t)e * I * gk,
-                  L->down_p + (size_t)e * H * (I / 2), L->down_gs + (size_t)e * H * gi, y);
+                  L->down_p + (size_t)e * H * (I / 2), L->down_gs + (size_t)e * H * gi, te, y);
     } else {
-        oracle_expert_i8(x, H, I,
-                         L->gate_w + (size_t)e * I * H, L->gate_s + (size_t)e * I,
-                         L->up_w + (size_t)e * I * H, L->up_s + (size_t)e * I,
-                         L->down_w + (size_t)e * H * I, L->down_s + (size_t)e * H, y);
+        expert_i8_q(x, H, I,
+                    L->gate_w + (size_t)e * I * H, L->gate_s + (size_t)e * I,
+                    L->up_w + (size_t)e * I * H, L->up_s + (size_t)e * I,
+                    L->down_w + (size_t)e * H * I, L->down_s + (size_t)e * H, te, y);
     }
 }
 
@@ -387,7 +398,7 @@ int oracle_moe_decode_routed(const oracle_moe_layer *L, const float *x, size_t m
         for (size_t j = 0; j < L->topk; j++) {
             int e = idx[t * L->topk + j];
             if (e < 0 || (size_t)e >= L->n_experts) { free(p); free(s); return -2; }
-            expert_dispatch(L, e, xr, p);
+            expert_dispatch(L, e, xr, 0, p);
             float wj = w[t * L->topk + j];
             for (size_t c = 0; c < H; c++) {
                 float pc = p[c] * wj;       /* `*v *= w` per element */
@@ -410,6 +421,54 @@ int oracle_moe_decode(const oracle_moe_layer *L, const float *x, size_t m,
                           L->norm_topk_prob, L->routed_scaling_factor, idx, w);
     if (rc) return rc;
     return oracle_moe_decode_routed(L, x, m, idx, w, y);
+}
+
+/* decoder.rs:2142-2181 moe_block_i8 (prefill): for each expert in ascending
+ * id, its member tokens in token order (members are pushed t-major,
+ * :2153-2157) run expert_mlp_i8 (:2120-2135, whose linear_int8_dynamic
+ * quantises activations per row ties-to-even, the prefill convention of
+ * :1647-1656) and `out[t][c] += w * y[c]` (:2166-2172); then the shared
+ * expert is added at weight 1 (:2174-2177). */
+int oracle_moe_prefill_routed(const oracle_moe_layer *L, const float *x, size_t m,
+                              const int32_t *idx, const float *w, float *y) {
+    size_t H = L->hidden;
+    float *p = (float *)malloc(H * sizeof(float));
+    for (size_t i = 0; i < m * H; i++) y[i] = 0.0f;
+    for (size_t t = 0; t < m; t++)
+        for (size_t j = 0; j < L->topk; j++)
+            if (idx[t * L->topk + j] < 0 || (size_t)idx[t * L->topk + j] >= L->n_experts) {
+                free(p);
+                return -2;
+            }
+    for (size_t e = 0; e < L->n_experts; e++) {
+        for (size_t t = 0; t < m; t++) {
+            for (size_t j = 0; j < L->topk; j++) {
+                if ((size_t)idx[t * L->topk + j] != e) continue;
+                expert_dispatch(L, (int)e, x + t * H, 1, p);
+                float wj = w[t * L->topk + j];
+                float *out = y + t * H;
+                for (size_t c = 0; c < H; c++) out[c] = out[c] + wj * p[c];
+            }
+        }
+    }
+    if (L->shared_inter) {
+        for (size_t t = 0; t < m; t++) {
+            expert_i8_q(x + t * H, H, L->shared_inter, L->sh_gate_w, L->sh_gate_s, L->sh_up_w,
+                        L->sh_up_s, L->sh_down_w, L->sh_down_s, 1, p);
+            float *out = y + t * H;
+            for (size_t c = 0; c < H; c++) out[c] = out[c] + p[c];
+        }
+    }
+    free(p);
+    return 0;
+}
+
+int oracle_moe_prefill(const oracle_moe_layer *L, const float *x, size_t m,
+                       float *y, int32_t *idx, float *w) {
+    int rc = oracle_route(x, m, L->hidden, L->router, L->n_experts, L->topk,
+                          L->norm_topk_prob, L->routed_scaling_factor, idx, w);
+    if (rc) return rc;
+    return oracle_moe_prefill_routed(L, x, m, idx, w, y);
 }
 
 /* ===================================================================== */

@@ -89,6 +89,11 @@ int oracle_moe_decode(const oracle_moe_layer *L, const float *x, size_t m,
                       float *y, int32_t *idx, float *w);
 int oracle_moe_decode_routed(const oracle_moe_layer *L, const float *x, size_t m,
                              const int32_t *idx, const float *w, float *y);
+/* prefill moe_block_i8 (decoder.rs:2142-2181) */
+int oracle_moe_prefill(const oracle_moe_layer *L, const float *x, size_t m,
+                       float *y, int32_t *idx, float *w);
+int oracle_moe_prefill_routed(const oracle_moe_layer *L, const float *x, size_t m,
+                              const int32_t *idx, const float *w, float *y);
 
 /* ---- lm-head / sampler ------------------------------------------------- */
 void oracle_vocab_tile_ranges(size_t n, size_t tiles, size_t *starts, size_t *ends);

@@ -65,6 +65,10 @@ lib.oracle_router_logits.argtypes = [vp, sz, vp, sz, vp]
 lib.oracle_route.argtypes = [vp, sz, sz, vp, sz, sz, C.c_int, C.c_float, vp, vp]
 lib.oracle_moe_decode.argtypes = [C.POINTER(MoeLayerC), vp, sz, vp, vp, vp]
 lib.oracle_moe_decode_routed.argtypes = [C.POINTER(MoeLayerC), vp, sz, vp, vp, vp]
+lib.oracle_moe_prefill.argtypes = lib.oracle_moe_decode.argtypes
+lib.oracle_moe_prefill.restype = C.c_int
+lib.oracle_moe_prefill_routed.argtypes = lib.oracle_moe_decode_routed.argtypes
+lib.oracle_moe_prefill_routed.restype = C.c_int
 lib.oracle_cpu_moe_decode.argtypes = [C.POINTER(MoeLayerC), vp, sz, vp, vp, vp, C.c_int]
 lib.oracle_vocab_tile_ranges.argtypes = [sz, sz, vp, vp]
 lib.oracle_argmax_row.argtypes = [vp, sz]
@@ -220,6 +224,26 @@ class MoeOracle:
         y = np.empty((m, self.W.hidden), np.float32)
         rc = lib.oracle_moe_decode_routed(C.byref(self.L), _p(x), m, _p(_c(idx, np.int32)),
                                           _p(_c(w, np.float32)), _p(y))
+        assert rc == 0, rc
+        return y
+
+    def prefill(self, x):
+        """moe_block_i8 (decoder.rs:2142-2181): route, experts in ascending id
+        (ties-even activation quantisation), then the shared expert."""
+        x = _c(x, np.float32)
+        m = x.shape[0]
+        y = np.empty((m, self.W.hidden), np.float32)
+        idx = np.empty((m, self.W.topk), np.int32)
+        w = np.empty((m, self.W.topk), np.float32)
+        rc = lib.oracle_moe_prefill(C.byref(self.L), _p(x), m, _p(y), _p(idx), _p(w))
+        return rc, y, idx, w
+
+    def prefill_routed(self, x, idx, w):
+        x = _c(x, np.float32)
+        m = x.shape[0]
+        y = np.empty((m, self.W.hidden), np.float32)
+        rc = lib.oracle_moe_prefill_routed(C.byref(self.L), _p(x), m, _p(_c(idx, np.int32)),
+                                           _p(_c(w, np.float32)), _p(y))
         assert rc == 0, rc
         return y
 
