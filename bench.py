@@ -32,6 +32,11 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 HIDDEN, INTER, NEXP, TOPK, SHARED = 1280, 896, 64, 6, 1792
+# DRAM bytes (read + write) of one config-2 step's two tensor-core kernels,
+# from one ncu capture of this workload (dram__bytes.sum.per_second x
+# gpu__time_duration); see profiles/moe_forward_config2_traffic.md
+CFG2_TRAFFIC_BYTES = 203.4e6
+CFG2_TRAFFIC_SOURCE = "ncu: MoeGateUp 136.1 MB + MoeDown 67.3 MB per step"
 TOKENS = 64
 L2_BYTES = 126 * 2**20
 
@@ -292,7 +297,8 @@ def run_ours(args, ws, rank, local):
                    "l2": f"ring of {R} layers of {expert_bytes() * NEXP / 1e6:.0f} MB each (> L2)"},
         "roofline": {"bound": "hbm", "kernel": "moe_forward step (all expert kernels)",
                      "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                     "frac": achieved / hbm_peak, "peak_kind": peak_kind, "traffic": None,
+                     "frac": achieved / hbm_peak, "peak_kind": peak_kind,
+                     "traffic": CFG2_TRAFFIC_BYTES, "traffic_source": CFG2_TRAFFIC_SOURCE,
                      "algorithmic_bytes_per_step": bytes_per_step},
         "e2e": {"value": args.steps * TOKENS * ws / (e2e_ms / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
