@@ -196,8 +196,18 @@ struct MoeGateUp {
     // finishes row t % 64 for columns t / 64 + 2k (k < 8): 8 independent
     // SwiGLU evaluations per thread, all loads before any store.
     __device__ void epilogue_done(int, int) const {}
+    __device__ void before_loads(const TcJob &) const {}
     __device__ void epilogue(const TcJob &jb, uint32_t tmem, int q, int lane, void *smem) const {
+        epilogue_impl<false>(jb, tmem, q, lane, smem, nullptr, nullptr);
+    }
+    // AMAX: also fold the tile's per-column |act| max into amax (pairs) /
+    // sh_amax (tokens) as non-negative float bits (NaN skipped, as fmaxf
+    // drops it); `smem` then carries 16 extra ints after the accumulators.
+    template <bool AMAX>
+    __device__ void epilogue_impl(const TcJob &jb, uint32_t tmem, int q, int lane, void *smem,
+                                  float *amax, float *sh_amax_) const {
         int *acc = static_cast<int *>(smem);   // [2 halves][64 rows][17] (padded)
+        unsigned *cm = reinterpret_cast<unsigned *>(acc + 2 * 64 * 17);   // [16] column max
         const bool routed = jb.t0 >= 0;
         const int rows = routed ? I : S;
         const int tid = 32 * q + lane;          // 0..127
@@ -209,6 +219,7 @@ struct MoeGateUp {
         float *out = routed ? act : sh_act;
         const float *scl = routed ? xs_sorted : xs;
         const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
+        if (AMAX && tid < 16) cm[tid] = 0u;
         for (int c0 = 0; c0 < jb.t3; c0 += 16) {
             int v[16];
             tc::tmem_ld16(lane_base + c0, v);
@@ -238,8 +249,17 @@ struct MoeGateUp {
             for (int k = 0; k < 8; k++) {
                 const int c = col0 + 2 * k;
                 if (c < lim) out[(size_t)(jb.t2 + c0 + c) * rows + i] = res[k];
+                if (AMAX && c < lim) {
+                    const float mag = fabsf(res[k]);
+                    if (mag == mag) atomicMax(&cm[c], __float_as_uint(mag));
+                }
             }
             asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (AMAX && tid < lim) {
+                float *am = routed ? amax : sh_amax_;
+                atomicMax(reinterpret_cast<unsigned *>(am + jb.t2 + c0 + tid), cm[tid]);
+                cm[tid] = 0u;
+            }
         }
     }
 };
@@ -315,6 +335,7 @@ struct MoeDown {
     }
 
     __device__ void epilogue_done(int, int) const {}
+    __device__ void before_loads(const TcJob &) const {}
     __device__ void epilogue(const TcJob &jb, uint32_t tmem, int q, int lane, void *) const {
         const bool routed = jb.t0 >= 0;
         const int c = jb.t1 * 128 + 32 * q + lane;
@@ -334,11 +355,11 @@ struct MoeDown {
                 const int p = jb.t2 + c0 + lane;
                 if (routed) {
                     const int slot_row = pair_tok[p] * topk + pair_slot[p];
-                    my_as = as2[p];
+                    my_as = __ldcg(as2 + p);
                     my_w = w[slot_row];
                     my_dst = slot_row;
                 } else {
-                    my_as = sh_as[p];
+                    my_as = __ldcg(sh_as + p);
                     my_dst = p;
                 }
             }
@@ -360,6 +381,169 @@ struct MoeDown {
 };
 
 // ---------------------------------------------------------------------------
+// Gate+up, requantisation and down of one forward in ONE persistent launch.
+//
+// The tile queue holds every gate+up tile, then every down tile (each part in
+// the order of its own problem).  A gate+up job folds its tile's per-row
+// |act| max into amax; the job that completes an expert's last gate+up job
+// (per-expert job counter, acquire-release) requantises that expert's
+// activation rows (decoder.rs:1751, the act_quant_rows_kernel arithmetic),
+// fences them for the async proxy and releases the expert's ready flag; a
+// down job's producer acquires the flag before its first load.  All gate+up
+// tiles are claimed before any down tile and a producer issues all loads of
+// a job before claiming the next, so every flag is set by work that never
+// waits; the waits are bounded all the same (status bit 4).
+// ---------------------------------------------------------------------------
+
+struct MoeFusedTC {
+    static constexpr int NA = 1, BN = 128, STAGES = 6;
+    static constexpr int EPI_SMEM = MoeGateUp::EPI_SMEM + 16 * 4 + 16;
+    static constexpr int NBUF = 4;
+    static constexpr int JOB_SMEM = MOE_JOB_SMEM;
+    static constexpr uint32_t KERNEL_ID = 5;
+    static constexpr int DOWN = 1 << 30;   // TcJob::t1 flag of a down job
+    static constexpr int FLAG_STRIDE = 32;   // one 128-byte line per counter / flag
+    TraceBuf trace;
+    MoeGateUp g;
+    MoeDown d;
+    int *done, *ready;       // [E + 1] each, FLAG_STRIDE apart (index E = shared expert), zeroed by prep
+    float *amax, *sh_amax;   // per pair / per token |act| max bits, zeroed by prep
+    int8_t *aq, *sh_aq;
+    float *as2, *sh_as;
+    int te;
+    int *sched, *err;
+
+    __device__ void prefetch() const {
+        g.prefetch();
+        d.prefetch();
+    }
+    using Iter = DynIter;
+    __device__ void load_job_state(void *js) const { sched_stage(g, js); }
+    __device__ void iter_init(Iter &it, void *js) const { sched_init<MoeFusedTC>(it, js); }
+    __device__ bool iter_next(Iter &it, TcJob &jb) const { return sched_next(*this, it, jb); }
+
+    __device__ int num_tiles(const SchedSmem *sm) const {
+        return g.num_tiles(sm) + d.num_tiles(sm);
+    }
+    // down tiles run routed experts first and the shared expert's last: its
+    // gate+up tiles come first, so its (largest) requantisation has the most
+    // time to finish
+    __device__ int down_tile(int t, const SchedSmem *sm) const {
+        const int sh = d.S ? d.htiles : 0;
+        const int routed = d.num_tiles(sm) - sh;
+        return t < routed ? t + sh : t - routed;
+    }
+    __device__ int num_chunks(int t, const SchedSmem *sm) const {
+        const int gu = g.num_tiles(sm);
+        return t < gu ? g.num_chunks(t, sm) : d.num_chunks(down_tile(t - gu, sm), sm);
+    }
+    __device__ void make_job(int t, int chunk, const SchedSmem *sm, TcJob &jb) const {
+        const int gu = g.num_tiles(sm);
+        if (t < gu) {
+            g.make_job(t, chunk, sm, jb);
+        } else {
+            d.make_job(down_tile(t - gu, sm), chunk, sm, jb);
+            jb.t1 |= DOWN;
+        }
+    }
+
+    __device__ void before_loads(const TcJob &jb) const {
+        if (!(jb.t1 & DOWN)) return;
+        const int *f = ready + (jb.t0 < 0 ? g.E : jb.t0) * FLAG_STRIDE;
+        uint32_t n = 0;
+        for (;;) {   // relaxed polling, one acquire fence after it
+            int v;
+            asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+            if (v) break;
+            if (++n > (1u << 24)) {
+                atomicOr(err, 4);
+                break;
+            }
+        }
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        // the activation rows were written through the generic proxy
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+    }
+
+    __device__ void epilogue_done(int, int) const {}
+
+    __device__ void epilogue(const TcJob &jb, uint32_t tmem, int q, int lane, void *smem) const {
+        if (jb.t1 & DOWN) {
+            TcJob j2 = jb;
+            j2.t1 &= ~DOWN;
+            d.epilogue(j2, tmem, q, lane, smem);
+            return;
+        }
+        g.epilogue_impl<true>(jb, tmem, q, lane, smem, amax, sh_amax);
+        // job accounting: the last gate+up job of this expert requantises it
+        const int tid = 32 * q + lane;
+        int *flag = reinterpret_cast<int *>(static_cast<uint8_t *>(smem) + MoeGateUp::EPI_SMEM +
+                                            16 * 4);
+        const bool routed = jb.t0 >= 0;
+        const int ei = routed ? jb.t0 : g.E;
+        int p0, cnt;
+        if (routed) {
+            p0 = __ldg(g.offsets + jb.t0);
+            cnt = __ldg(g.offsets + jb.t0 + 1) - p0;
+        } else {
+            p0 = g.sh0;
+            cnt = g.T - g.sh0;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");   // every act store of this job issued
+        if (tid == 0) {
+            const int jobs = (routed ? g.itiles : g.stiles) * ((cnt + BN - 1) / BN);
+            __threadfence();
+            int old;
+            asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;"
+                         : "=r"(old)
+                         : "l"(done + ei * FLAG_STRIDE)
+                         : "memory");
+            *flag = old == jobs - 1;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (!*flag) return;
+        // requantise every row of the expert: warp q takes rows q, q+4, ...
+        const int L = routed ? g.I : g.S;
+        const float *act = routed ? g.act : g.sh_act;
+        const float *am = routed ? amax : sh_amax;
+        int8_t *aqo = routed ? aq : sh_aq;
+        float *aso = routed ? as2 : sh_as;
+        for (int r = p0 + q; r < p0 + cnt; r += 4) {
+            const float a = __uint_as_float(__ldcg(reinterpret_cast<const unsigned *>(am + r)));
+            const float sc = a > 0.0f ? __fdiv_rn(a, 127.0f) : 1.0f;
+            const float inv = __fdiv_rn(1.0f, sc);
+            const float4 *src = reinterpret_cast<const float4 *>(act + (size_t)r * L);
+            char4 *dst = reinterpret_cast<char4 *>(aqo + (size_t)r * L);
+            // the whole row in flight (L <= 2048: 16 float4 per lane)
+            float4 x4[16];
+#pragma unroll
+            for (int u = 0; u < 16; u++)
+                if (lane + 32 * u < L / 4) x4[u] = __ldcg(src + lane + 32 * u);
+#pragma unroll
+            for (int u = 0; u < 16; u++) {
+                if (lane + 32 * u < L / 4) {
+                    char4 o;
+                    o.x = (signed char)quant_i8(x4[u].x, inv, te != 0);
+                    o.y = (signed char)quant_i8(x4[u].y, inv, te != 0);
+                    o.z = (signed char)quant_i8(x4[u].z, inv, te != 0);
+                    o.w = (signed char)quant_i8(x4[u].w, inv, te != 0);
+                    dst[lane + 32 * u] = o;
+                }
+            }
+            if (lane == 0) aso[r] = sc;
+        }
+        // make the rows visible to the down jobs' TMA (async proxy), then
+        // release the expert
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (tid == 0)
+            asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(ready + ei * FLAG_STRIDE), "r"(1)
+                         : "memory");
+    }
+};
+
+// ---------------------------------------------------------------------------
 // Prep: quantise tokens, validate + bucket routing, gather pair rows.
 // ---------------------------------------------------------------------------
 
@@ -374,7 +558,8 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(
     int32_t *__restrict__ offsets, int32_t *__restrict__ pair_tok,
     int32_t *__restrict__ pair_slot, int8_t *__restrict__ xq_sorted,
     float *__restrict__ xs_sorted, int32_t *__restrict__ active, int *__restrict__ sched,
-    float *__restrict__ part, int32_t *err, int te) {
+    float *__restrict__ part, int32_t *err, int te, int *__restrict__ flags, int nflags,
+    float *__restrict__ amax, float *__restrict__ sh_amax) {
     __shared__ int cnt[1025];
     __shared__ int rank[8];
     __shared__ float red[8];
@@ -470,7 +655,11 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(
             sched[0] = 0;
             sched[1] = 0;
         }
+        // the fused launch's per-expert job counters and ready flags
+        if (flags)
+            for (int f = tid; f < nflags; f += blockDim.x) flags[f] = 0;
     }
+    if (sh_amax && tid == 0) sh_amax[t] = 0.0f;
     const float inv = s_inv;
     const float sc = s_scale;
     int8_t *qrow = xq + (size_t)t * H;
@@ -496,6 +685,7 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(
             pair_tok[pos] = t;
             pair_slot[pos] = j;
             xs_sorted[pos] = sc;
+            if (amax) amax[pos] = 0.0f;
         }
         const int4 *src = reinterpret_cast<const int4 *>(qrow);
         int4 *dst = reinterpret_cast<int4 *>(xq_sorted + (size_t)pos * H);
@@ -674,6 +864,11 @@ static int tiled_copy(const int8_t *src, long rows, int K, int8_t **dst) {
 struct MoeTcState {
     MoeGateUp gu;
     MoeDown dn;
+    MoeFusedTC fu;
+    int *flags = nullptr;    // [2 (E + 1) FLAG_STRIDE]: per-expert job counters, ready flags
+    ~MoeTcState() {
+        if (flags) cudaFree(flags);
+    }
 };
 
 int moe_tc_setup(focr_moe_layer *L) {
@@ -730,6 +925,23 @@ int moe_tc_setup(focr_moe_layer *L) {
     d.w = nullptr;
     d.part = L->part; d.sh_y = L->sh_y;
     d.err = L->err;
+    const size_t nfl = 2 * (size_t)(E + 1) * MoeFusedTC::FLAG_STRIDE;
+    if (cudaMalloc(&st->flags, nfl * sizeof(int)) != cudaSuccess) {
+        delete st;
+        return fail(FOCR_E_ALLOC, "moe_tc_setup: flags");
+    }
+    cudaMemset(st->flags, 0, nfl * sizeof(int));
+    MoeFusedTC &f = st->fu;
+    f.done = st->flags;
+    f.ready = st->flags + (size_t)(E + 1) * MoeFusedTC::FLAG_STRIDE;
+    f.amax = L->amax;
+    f.sh_amax = L->sh_amax;
+    f.aq = L->aq;
+    f.sh_aq = L->sh_aq;
+    f.as2 = L->as2;
+    f.sh_as = L->sh_as;
+    f.sched = L->sched;
+    f.err = L->err;
     L->tc_state = st;
     return FOCR_OK;
 }
@@ -739,19 +951,32 @@ void moe_tc_free(focr_moe_layer *L) {
     L->tc_state = nullptr;
 }
 
-// Quantise + bucket + gather, then the two tensor-core GEMMs and the
-// activation requantisation between them.
+// Quantise + bucket + gather, then the tensor-core GEMMs: the three-launch
+// sequence (gate+up, requantisation, down), or one fused launch.
 int moe_tc_experts(focr_moe_layer *L, const float *x, int m, const int32_t *idx, const float *w,
                    int sh0, cudaStream_t st, bool te) {
     MoeTcState *s = static_cast<MoeTcState *>(L->tc_state);
     const int H = L->cfg.hidden, K = L->cfg.topk, S = L->cfg.shared_inter;
     const int P = m * K;
+    // The three-launch sequence (gate+up, requantisation, down) by default;
+    // FOCR_MOE_FUSED=1 selects the single persistent launch, which measured
+    // slower on config 2 (the per-expert requantisation by the last gate+up
+    // job serialises on one SM per expert)
+    const bool unfused = getenv("FOCR_MOE_FUSED") == nullptr;
+    const int nflags = 2 * ((int)L->E + 1) * MoeFusedTC::FLAG_STRIDE;
     if (m <= 4096) {
         FOCR_CUDA_TRY(launch_pdl(moe_prep_kernel, dim3(m), dim3(256), 0, st, x, idx, m, H, K,
                                  (int)L->E, (int)L->cfg.expert_begin, L->xq, L->xs, L->offsets,
                                  L->pair_tok, L->pair_slot, L->xq_sorted, L->xs_sorted, L->counts,
-                                 L->sched, L->part, L->err, (int)te));
+                                 L->sched, L->part, L->err, (int)te, unfused ? nullptr : s->flags,
+                                 nflags, unfused ? nullptr : L->amax,
+                                 unfused ? nullptr : L->sh_amax));
     } else {
+        if (!unfused) {
+            FOCR_CUDA_TRY(cudaMemsetAsync(s->flags, 0, nflags * sizeof(int), st));
+            FOCR_CUDA_TRY(cudaMemsetAsync(L->amax, 0, (size_t)P * sizeof(float), st));
+            if (S) FOCR_CUDA_TRY(cudaMemsetAsync(L->sh_amax, 0, (size_t)m * sizeof(float), st));
+        }
         int rc = launch_quantize_rows(x, m, H, te, L->xq, L->xs, st);
         if (rc) return rc;
         moe_bucket_kernel<<<1, 1024, 0, st>>>(idx, m, K, (int)L->E, (int)L->cfg.expert_begin,
@@ -764,6 +989,19 @@ int moe_tc_experts(focr_moe_layer *L, const float *x, int m, const int32_t *idx,
                                                L->xq_sorted, L->xs_sorted);
     }
     const int sms = num_sms();
+    if (!unfused) {
+        MoeFusedTC f = s->fu;
+        f.g = s->gu;
+        f.g.T = m;
+        f.g.sh0 = sh0;
+        f.d = s->dn;
+        f.d.T = m;
+        f.d.sh0 = sh0;
+        f.d.w = w;
+        f.te = te ? 1 : 0;
+        const int tiles = (int)L->E * (f.g.itiles + f.d.htiles) + (S ? f.g.stiles + f.d.htiles : 0);
+        return launch_tc(f, tiles < sms ? tiles : sms, st);
+    }
     MoeGateUp g = s->gu;
     g.T = m;
     g.sh0 = sh0;

@@ -116,6 +116,7 @@ struct RawIgemm {
     __device__ void epilogue_done(int, int lane) const {
         if (TMA_EPI && lane == 0) tc::bulk_wait_all();
     }
+    __device__ void before_loads(const TcJob &) const {}
 
     __device__ void epilogue(const TcJob &jb, uint32_t tmem, int q, int lane, void *smem) const {
         if constexpr (TMA_EPI) {

@@ -12,6 +12,7 @@
 //   static constexpr int EPI_SMEM -- shared-memory bytes the epilogue may use
 //   __device__ void epilogue(const TcJob &, uint32_t tmem, int quarter, int lane, void *smem) const
 //   __device__ void epilogue_done(int quarter, int lane) const  -- after the warp's last job
+//   __device__ void before_loads(const TcJob &) const  -- producer, before a job's first load
 //   int *err                     -- status word (bit 4: a bounded wait expired)
 // A job computes D[128 x n_mma] = sum over kblocks of A[a_row.., k] . B[b_row.., k]
 // for every A operand (accumulator a at TMEM column offset a*BN of its buffer).
@@ -115,6 +116,7 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__
             typename P::Iter itr;
             p.iter_init(itr, job_smem);
             for (int j = 0; ok && p.iter_next(itr, jb); j++) {
+                p.before_loads(jb);   // cross-CTA inputs of the job are ready
                 trace_event(tb, KID, j, TR_JOB_LOAD);
                 const uint32_t bytes = NA * A_BYTES + (uint32_t)jb.b_box * 128;
                 for (int kb = 0; kb < jb.kblocks; kb++, it++) {

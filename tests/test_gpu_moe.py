@@ -207,3 +207,22 @@ def test_forward_tc_token_counts(cuda, oracle, m):
     y = L.forward(x, idx, w)
     assert_close_rel(y, MoeOracle(W).forward(x, idx, w), f"tc forward m={m}")
     L.close()
+
+
+@pytest.mark.parametrize("m", [3, 64, 300])
+def test_forward_fused_launch(cuda, oracle, monkeypatch, m):
+    """The single persistent launch (FOCR_MOE_FUSED=1: gate+up, last-arriver
+    requantisation per expert, down) gives the same bits as the oracle."""
+    from franken_ocr_b200 import synth
+    from franken_ocr_b200.moe import MoeLayer
+    from oracle.oracle import MoeOracle
+
+    monkeypatch.setenv("FOCR_MOE_FUSED", "1")
+    W = synth.moe_layer(811, shared_inter=1792)
+    L = MoeLayer(W, max_tokens=m)
+    x = synth.hidden_states(812, m)
+    idx, w = synth.zipf_routing(812, m)
+    y = L.forward(x, idx, w)
+    want = MoeOracle(W).forward(x, idx, w)
+    assert np.array_equal(y.view(np.uint32), want.view(np.uint32))
+    L.close()
