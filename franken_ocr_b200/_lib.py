@@ -29,7 +29,8 @@ EXPORTS = [
     "focr_moe_create", "focr_moe_destroy", "focr_moe_route", "focr_moe_forward",
     "focr_moe_decode", "focr_moe_prefill", "focr_moe_forward_rows", "focr_moe_combine", "focr_ep_pack",
     "focr_lmhead_create", "focr_lmhead_destroy", "focr_lmhead_top1",
-    "focr_top1_combine", "focr_selftest", "focr_trace_set",
+    "focr_top1_combine", "focr_selftest", "focr_trace_set", "focr_rms_norm", "focr_rope_apply",
+    "focr_attention_decode",
 ]
 
 
@@ -93,6 +94,9 @@ lib.focr_lmhead_top1.argtypes = [vp, vp, sz, vp, vp, vp, i32, vp]
 lib.focr_top1_combine.argtypes = [vp, vp, sz, sz, vp]
 lib.focr_selftest.argtypes = [C.c_char_p, sz, C.POINTER(i32)]
 lib.focr_trace_set.argtypes = [vp, vp, sz]
+lib.focr_rms_norm.argtypes = [vp, sz, sz, vp, C.c_float, vp, i32, vp]
+lib.focr_rope_apply.argtypes = [vp, sz, sz, sz, vp, vp, i32, vp]
+lib.focr_attention_decode.argtypes = [vp, vp, vp, sz, sz, vp, vp, sz, sz, sz, sz, vp, i32, vp]
 
 
 def check(rc: int) -> None:

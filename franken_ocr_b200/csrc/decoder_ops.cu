@@ -1,0 +1,284 @@
+// Decoder pieces beside the MoE layer (the config-3 decoder): row RMSNorm,
+// NEOX RoPE application, and the R-SWA decode attention over a layer's
+// reference + ring KV blocks.
+//
+//  * focr_rms_norm       -- nn.rs:240-252 (rms_norm -> a third-party kernel,
+//    ft_kernel_cpu::rms_norm_forward_f32, whose order the oracle defines:
+//    32 lane-striped partial sums over 4-element chunks + xor butterfly);
+//    bit-identical to the oracle.
+//  * focr_rope_apply     -- decoder.rs:229-272 apply_rope with the host-built
+//    RopeTable (decoder.rs:171-213); bit-identical.
+//  * focr_attention_decode -- rswa.rs:855-944 decode attention (q_len 1, no
+//    mask, scale 1/sqrt(head_dim)) over reference ++ ring rows.  Scores are
+//    the reference's sequential dot in the same order; the softmax and the
+//    probs.V sum are two parallel passes (max, exp, tree sums) instead of the
+//    per-key online fold, so results match the fold to rounding (the
+//    reference's own batched-GEMV lever, rswa.rs:995-1050, does the same).
+#include <string>
+
+#include "common.cuh"
+
+namespace focr {
+
+// One warp per row.
+__global__ void rms_norm_kernel(const float *__restrict__ x, int rows, int cols,
+                                const float *__restrict__ w, float eps, float *__restrict__ y) {
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const float *xr = x + (size_t)row * cols;
+    float s = 0.0f;
+    for (int c = lane; 4 * c < cols; c += 32)
+        for (int k = 4 * c; k < 4 * c + 4 && k < cols; k++) s = __fadd_rn(s, __fmul_rn(xr[k], xr[k]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+    const float ms = __fdiv_rn(s, (float)cols);
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+    float *yr = y + (size_t)row * cols;
+    for (int k = lane; k < cols; k += 32) {
+        const float v = __fmul_rn(xr[k], r);
+        yr[k] = w ? __fmul_rn(v, w[k]) : v;
+    }
+}
+
+// One thread per (row, head, i < half).
+__global__ void rope_kernel(float *__restrict__ x, int seq, int cols, int head_dim,
+                            const float *__restrict__ cos_t, const float *__restrict__ sin_t) {
+    const int half = head_dim / 2, heads = cols / head_dim;
+    const long n = (long)seq * heads * half;
+    for (long g = blockIdx.x * (long)blockDim.x + threadIdx.x; g < n; g += (long)gridDim.x * blockDim.x) {
+        const int i = (int)(g % half);
+        const int h = (int)((g / half) % heads);
+        const int t = (int)(g / ((long)half * heads));
+        float *row = x + (size_t)t * cols + (size_t)h * head_dim;
+        const float a = row[i], b = row[half + i];
+        const float c = cos_t[(size_t)t * head_dim + i], s = sin_t[(size_t)t * head_dim + i];
+        row[i] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+        row[half + i] = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
+    }
+}
+
+constexpr int ATT_THREADS = 256;
+constexpr int ATT_MAX_KEYS = 16384;
+
+// One CTA per head.  Shared memory: q [head_dim], probabilities [total],
+// per-warp reduction scratch, partial outputs [ATT_THREADS].
+__global__ void __launch_bounds__(ATT_THREADS) attention_decode_kernel(
+    const float *__restrict__ q, const float *__restrict__ ref_k, const float *__restrict__ ref_v,
+    int prefill_len, int ref_stride, const float *__restrict__ ring_k,
+    const float *__restrict__ ring_v, int ring_len, int ring_stride, int head_dim,
+    float *__restrict__ out) {
+    extern __shared__ float att_sm[];
+    const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int total = prefill_len + ring_len;
+    float *sq = att_sm;                       // [head_dim]
+    float *sp = sq + head_dim;                // [total]
+    float *red = sp + total;                  // [ATT_THREADS / 32]
+    float *po = red + ATT_THREADS / 32;       // [ATT_THREADS]
+    for (int i = tid; i < head_dim; i += ATT_THREADS) sq[i] = q[(size_t)h * head_dim + i];
+    __syncthreads();
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)head_dim));
+    // scores: the reference's dot, d = 0 .. head_dim - 1 in order
+    float m = -INFINITY;
+    for (int r = tid; r < total; r += ATT_THREADS) {
+        const float *kr = r < prefill_len
+                              ? ref_k + ((size_t)h * ref_stride + r) * head_dim
+                              : ring_k + ((size_t)h * ring_stride + (r - prefill_len)) * head_dim;
+        float d = 0.0f;
+        for (int i = 0; i < head_dim; i += 4) {
+            const float4 k4 = *reinterpret_cast<const float4 *>(kr + i);
+            d = __fadd_rn(d, __fmul_rn(sq[i], k4.x));
+            d = __fadd_rn(d, __fmul_rn(sq[i + 1], k4.y));
+            d = __fadd_rn(d, __fmul_rn(sq[i + 2], k4.z));
+            d = __fadd_rn(d, __fmul_rn(sq[i + 3], k4.w));
+        }
+        const float sc = __fmul_rn(d, scale);
+        sp[r] = sc;
+        m = fmaxf(m, sc);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    m = red[0];
+    for (int w = 1; w < ATT_THREADS / 32; w++) m = fmaxf(m, red[w]);
+    __syncthreads();
+    // probabilities (unnormalised) and their sum
+    float den = 0.0f;
+    for (int r = tid; r < total; r += ATT_THREADS) {
+        const float p = dexpf(__fsub_rn(sp[r], m));
+        sp[r] = p;
+        den = __fadd_rn(den, p);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) den = __fadd_rn(den, __shfl_xor_sync(0xffffffffu, den, o));
+    if (lane == 0) red[warp] = den;
+    __syncthreads();
+    den = red[0];
+    for (int w = 1; w < ATT_THREADS / 32; w++) den = __fadd_rn(den, red[w]);
+    // probs . V: thread (g, d) sums keys r = g, g + G, ... for dimension d
+    const int G = ATT_THREADS / head_dim;
+    const int d = tid % head_dim, g = tid / head_dim;
+    float acc = 0.0f;
+    if (g < G)
+        for (int r = g; r < total; r += G) {
+            const float *vr = r < prefill_len
+                                  ? ref_v + ((size_t)h * ref_stride + r) * head_dim
+                                  : ring_v + ((size_t)h * ring_stride + (r - prefill_len)) * head_dim;
+            acc = __fadd_rn(acc, __fmul_rn(sp[r], vr[d]));
+        }
+    po[tid] = acc;
+    __syncthreads();
+    if (tid < head_dim) {
+        float a = 0.0f;
+        for (int gg = 0; gg < G; gg++) a = __fadd_rn(a, po[gg * head_dim + tid]);
+        const float inv = den > 0.0f ? __fdiv_rn(1.0f, den) : 0.0f;
+        out[(size_t)h * head_dim + tid] = __fmul_rn(a, inv);
+    }
+}
+
+}  // namespace focr
+
+using namespace focr;
+
+namespace {
+
+// Stage host buffers on the device for the duration of one call.
+struct Staged {
+    DevBuf buf;
+    const void *src;
+    size_t bytes;
+};
+
+int to_dev(Staged &s, const void *host, size_t bytes, cudaStream_t st) {
+    s.src = host;
+    s.bytes = bytes;
+    if (!host || !bytes) return FOCR_OK;
+    FOCR_CUDA_TRY(s.buf.alloc(bytes, st));
+    FOCR_CUDA_TRY(cudaMemcpyAsync(s.buf.p, host, bytes, cudaMemcpyHostToDevice, st));
+    return FOCR_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int focr_rms_norm(const float *x, size_t rows, size_t cols, const float *weight, float eps,
+                  float *y, int mem, void *stream) {
+    if (rows == 0 || cols == 0) return FOCR_OK;
+    if (!x || !y) return fail(FOCR_E_ARG, "rms_norm: null pointer");
+    if (rows > (size_t)INT32_MAX || cols > (size_t)INT32_MAX)
+        return fail(FOCR_E_UNSUPPORTED, "rms_norm: dimension exceeds int32 range");
+    cudaStream_t st = (cudaStream_t)stream;
+    const int blocks = (int)((rows + 7) / 8);
+    if (mem == FOCR_MEM_DEVICE) {
+        rms_norm_kernel<<<blocks, 256, 0, st>>>(x, (int)rows, (int)cols, weight, eps, y);
+        FOCR_CUDA_TRY(cudaGetLastError());
+        return FOCR_OK;
+    }
+    if (mem != FOCR_MEM_HOST) return fail(FOCR_E_ARG, "bad mem kind");
+    Staged sx, sw;
+    DevBuf dy;
+    int rc = to_dev(sx, x, rows * cols * 4, st);
+    if (!rc) rc = to_dev(sw, weight, weight ? cols * 4 : 0, st);
+    if (rc) return rc;
+    FOCR_CUDA_TRY(dy.alloc(rows * cols * 4, st));
+    rms_norm_kernel<<<blocks, 256, 0, st>>>((const float *)sx.buf.p, (int)rows, (int)cols,
+                                            (const float *)sw.buf.p, eps, (float *)dy.p);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    FOCR_CUDA_TRY(cudaMemcpyAsync(y, dy.p, rows * cols * 4, cudaMemcpyDeviceToHost, st));
+    FOCR_CUDA_TRY(cudaStreamSynchronize(st));
+    return FOCR_OK;
+}
+
+int focr_rope_apply(float *x, size_t seq, size_t cols, size_t head_dim, const float *cos_t,
+                    const float *sin_t, int mem, void *stream) {
+    if (seq == 0 || cols == 0) return FOCR_OK;
+    if (!x || !cos_t || !sin_t) return fail(FOCR_E_ARG, "apply_rope: null pointer");
+    if (head_dim == 0 || head_dim % 2 || cols % head_dim)
+        return fail(FOCR_E_SHAPE, "apply_rope: cols " + std::to_string(cols) +
+                                      " not a multiple of head_dim " + std::to_string(head_dim));
+    if (seq * cols > (size_t)INT32_MAX) return fail(FOCR_E_UNSUPPORTED, "apply_rope: too large");
+    cudaStream_t st = (cudaStream_t)stream;
+    const long n = (long)seq * (cols / 2);
+    const int blocks = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+    if (mem == FOCR_MEM_DEVICE) {
+        rope_kernel<<<blocks, 256, 0, st>>>(x, (int)seq, (int)cols, (int)head_dim, cos_t, sin_t);
+        FOCR_CUDA_TRY(cudaGetLastError());
+        return FOCR_OK;
+    }
+    if (mem != FOCR_MEM_HOST) return fail(FOCR_E_ARG, "bad mem kind");
+    Staged sx, sc, ss;
+    int rc = to_dev(sx, x, seq * cols * 4, st);
+    if (!rc) rc = to_dev(sc, cos_t, seq * head_dim * 4, st);
+    if (!rc) rc = to_dev(ss, sin_t, seq * head_dim * 4, st);
+    if (rc) return rc;
+    rope_kernel<<<blocks, 256, 0, st>>>((float *)sx.buf.p, (int)seq, (int)cols, (int)head_dim,
+                                        (const float *)sc.buf.p, (const float *)ss.buf.p);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    FOCR_CUDA_TRY(cudaMemcpyAsync(x, sx.buf.p, seq * cols * 4, cudaMemcpyDeviceToHost, st));
+    FOCR_CUDA_TRY(cudaStreamSynchronize(st));
+    return FOCR_OK;
+}
+
+int focr_attention_decode(const float *q, const float *ref_k, const float *ref_v,
+                          size_t prefill_len, size_t ref_stride, const float *ring_k,
+                          const float *ring_v, size_t ring_len, size_t ring_stride, size_t heads,
+                          size_t head_dim, float *out, int mem, void *stream) {
+    if (heads == 0) return FOCR_OK;
+    if (prefill_len + ring_len == 0)
+        return fail(FOCR_E_ARG, "rswa: empty attention key set (prefill_len=0, ring_len=0)");
+    if (!q || !out || (prefill_len && (!ref_k || !ref_v)) || (ring_len && (!ring_k || !ring_v)))
+        return fail(FOCR_E_ARG, "attention_decode: null pointer");
+    if (head_dim == 0 || head_dim % 4 || head_dim > ATT_THREADS || ATT_THREADS % head_dim)
+        return fail(FOCR_E_UNSUPPORTED, "attention_decode: head_dim must divide 256 and be a multiple of 4");
+    if (prefill_len > ref_stride || ring_len > ring_stride)
+        return fail(FOCR_E_SHAPE, "attention_decode: rows exceed the cache stride");
+    if (prefill_len + ring_len > (size_t)ATT_MAX_KEYS || heads > 65535)
+        return fail(FOCR_E_UNSUPPORTED, "attention_decode: more than 16384 keys or 65535 heads");
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t total = prefill_len + ring_len;
+    const size_t smem = (head_dim + total + ATT_THREADS / 32 + ATT_THREADS) * sizeof(float);
+    static bool attr = false;
+    if (!attr) {
+        FOCR_CUDA_TRY(cudaFuncSetAttribute(attention_decode_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)((head_dim > 256 ? head_dim : 256) + ATT_MAX_KEYS +
+                                                 ATT_THREADS / 32 + ATT_THREADS) *
+                                               4));
+        attr = true;
+    }
+    const float *dq = q, *drk = ref_k, *drv = ref_v, *dgk = ring_k, *dgv = ring_v;
+    float *dout = out;
+    Staged sq, srk, srv, sgk, sgv;
+    DevBuf dob;
+    if (mem == FOCR_MEM_HOST) {
+        const size_t rb = heads * ref_stride * head_dim * 4, gb = heads * ring_stride * head_dim * 4;
+        int rc = to_dev(sq, q, heads * head_dim * 4, st);
+        if (!rc && prefill_len) rc = to_dev(srk, ref_k, rb, st);
+        if (!rc && prefill_len) rc = to_dev(srv, ref_v, rb, st);
+        if (!rc && ring_len) rc = to_dev(sgk, ring_k, gb, st);
+        if (!rc && ring_len) rc = to_dev(sgv, ring_v, gb, st);
+        if (rc) return rc;
+        FOCR_CUDA_TRY(dob.alloc(heads * head_dim * 4, st));
+        dq = (const float *)sq.buf.p;
+        drk = (const float *)srk.buf.p;
+        drv = (const float *)srv.buf.p;
+        dgk = (const float *)sgk.buf.p;
+        dgv = (const float *)sgv.buf.p;
+        dout = (float *)dob.p;
+    } else if (mem != FOCR_MEM_DEVICE) {
+        return fail(FOCR_E_ARG, "bad mem kind");
+    }
+    attention_decode_kernel<<<(unsigned)heads, ATT_THREADS, smem, st>>>(
+        dq, drk, drv, (int)prefill_len, (int)ref_stride, dgk, dgv, (int)ring_len, (int)ring_stride,
+        (int)head_dim, dout);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    if (mem == FOCR_MEM_HOST) {
+        FOCR_CUDA_TRY(cudaMemcpyAsync(out, dout, heads * head_dim * 4, cudaMemcpyDeviceToHost, st));
+        FOCR_CUDA_TRY(cudaStreamSynchronize(st));
+    }
+    return FOCR_OK;
+}
+
+}  // extern "C"

@@ -223,6 +223,32 @@ int focr_lmhead_top1(focr_lmhead *h, const float *x, size_t m, float *best_val,
 int focr_top1_combine(const float *vals, const int32_t *idx, size_t shards,
                       size_t m, uint32_t *token);
 
+/* ---- decoder pieces beside the MoE layer (config-3 decoder) ------------ */
+
+/* Row RMSNorm -- replaces nn::rms_norm (native_engine/nn.rs:240-252, which
+ * calls the third-party ft_kernel_cpu::rms_norm_forward_f32): y = (x * r) * w
+ * with r = 1 / sqrt(mean(x^2) + eps); weight may be NULL.  The sum of squares
+ * runs in the order oracle_rms_norm defines. */
+int focr_rms_norm(const float *x, size_t rows, size_t cols, const float *weight, float eps,
+                  float *y, int mem, void *stream);
+
+/* NEOX RoPE in place -- replaces apply_rope (native_engine/decoder.rs:229-272)
+ * for x [seq][cols], cols a multiple of head_dim, with the RopeTable cos/sin
+ * [seq][head_dim] built by the caller (decoder.rs:171-213). */
+int focr_rope_apply(float *x, size_t seq, size_t cols, size_t head_dim, const float *cos_t,
+                    const float *sin_t, int mem, void *stream);
+
+/* R-SWA decode attention (q_len 1, no mask, scale 1/sqrt(head_dim)) over the
+ * reference rows ++ ring rows of one layer -- replaces decode_attention
+ * (native_engine/rswa.rs:855-944).  q, out [heads][head_dim]; K/V head-major:
+ * head h's row r at base + (h * stride + r) * head_dim.  Scores match the
+ * reference's dot bit for bit; the softmax and probs.V run as parallel passes
+ * (not the per-key online fold), equal to it up to f32 rounding. */
+int focr_attention_decode(const float *q, const float *ref_k, const float *ref_v,
+                          size_t prefill_len, size_t ref_stride, const float *ring_k,
+                          const float *ring_v, size_t ring_len, size_t ring_stride, size_t heads,
+                          size_t head_dim, float *out, int mem, void *stream);
+
 /* ---- device event trace (GPU counterpart of FOCR_PROFILE_DECODE,
  * native_engine/decoder.rs:986-1024) ------------------------------------
  * Register a device buffer of `capacity` 16-byte events {u32 tag, u32 phase,

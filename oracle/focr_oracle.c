@@ -502,3 +502,120 @@ uint32_t oracle_argmax_row(const float *logits, size_t n) {
     }
     return best < 0 ? 0u : (uint32_t)best;
 }
+
+/* ===================================================================== */
+/* Decoder pieces beside the MoE layer (config 3)                         */
+/* ===================================================================== */
+
+/* nn.rs:240-252 rms_norm -> ft_kernel_cpu::rms_norm_forward_f32, a
+ * third-party kernel outside the reference (frankentorch, unpinned).  This
+ * project's definition, shaped for a warp per row: the sum of squares is
+ * taken as 32 partial sums, chunk c of 4 consecutive elements going to
+ * partial c % 32 (chunks in increasing order, elements of a chunk in order),
+ * combined by an xor butterfly over offsets 16, 8, 4, 2, 1 (the order the
+ * router logits use); ms = ss / cols; r = 1 / sqrt(ms + eps) (both correctly
+ * rounded); y = (x * r) * w, or x * r without a weight. */
+void oracle_rms_norm(const float *x, size_t rows, size_t cols, const float *w, float eps,
+                     float *y) {
+    for (size_t t = 0; t < rows; t++) {
+        const float *xr = x + t * cols;
+        float part[32];
+        for (int l = 0; l < 32; l++) part[l] = 0.0f;
+        for (size_t c = 0; 4 * c < cols; c++)
+            for (size_t k = 4 * c; k < 4 * c + 4 && k < cols; k++)
+                part[c % 32] = part[c % 32] + xr[k] * xr[k];
+        for (int o = 16; o > 0; o >>= 1) {
+            float nxt[32];
+            for (int l = 0; l < 32; l++) nxt[l] = part[l] + part[l ^ o];
+            for (int l = 0; l < 32; l++) part[l] = nxt[l];
+        }
+        float ms = part[0] / (float)cols;
+        float r = 1.0f / sqrtf(ms + eps);
+        for (size_t k = 0; k < cols; k++) {
+            float v = xr[k] * r;
+            y[t * cols + k] = w ? v * w[k] : v;
+        }
+    }
+}
+
+/* decoder.rs:171-213 RopeTable::build: inv_freq[i] = (f32)(1 / theta^(2i/hd))
+ * in f64, angle = (f32)pos * inv_freq[i], (sin, cos) = angle.sin_cos(), each
+ * duplicated into columns i and i + hd/2. */
+void oracle_rope_table(const size_t *pos, size_t seq, size_t head_dim, float theta, float *cos_t,
+                       float *sin_t) {
+    size_t half = head_dim / 2;
+    for (size_t p = 0; p < seq; p++) {
+        for (size_t i = 0; i < half; i++) {
+            double exponent = (double)(2 * i) / (double)head_dim;
+            float inv_freq = (float)(1.0 / pow((double)theta, exponent));
+            float angle = (float)pos[p] * inv_freq;
+            float s = sinf(angle), c = cosf(angle);
+            cos_t[p * head_dim + i] = c;
+            cos_t[p * head_dim + half + i] = c;
+            sin_t[p * head_dim + i] = s;
+            sin_t[p * head_dim + half + i] = s;
+        }
+    }
+}
+
+/* decoder.rs:229-272 apply_rope (NEOX rotate_half over each head's two
+ * halves): first half a*cos - b*sin, second half b*cos + a*sin. */
+void oracle_apply_rope(float *x, size_t seq, size_t cols, size_t head_dim, const float *cos_t,
+                       const float *sin_t) {
+    size_t half = head_dim / 2, heads = cols / head_dim;
+    for (size_t t = 0; t < seq; t++) {
+        float *row = x + t * cols;
+        for (size_t h = 0; h < heads; h++) {
+            size_t hb = h * head_dim;
+            for (size_t i = 0; i < half; i++) {
+                float a = row[hb + i], b = row[hb + half + i];
+                float c = cos_t[t * head_dim + i], s = sin_t[t * head_dim + i];
+                row[hb + i] = a * c - b * s;
+                row[hb + half + i] = b * c + a * s;
+            }
+        }
+    }
+}
+
+/* rswa.rs:894-944 decode_attention_scalar with fold (:1163-1182) and dot
+ * (:612-619): per head the online softmax over reference ++ ring rows,
+ * score = dot(q, k) * (1 / sqrt(head_dim)).  K/V are head-major:
+ * head h's row r at base + (h * stride + r) * head_dim. */
+int oracle_attention_decode(const float *q, const float *ref_k, const float *ref_v,
+                            size_t prefill_len, size_t ref_stride, const float *ring_k,
+                            const float *ring_v, size_t ring_len, size_t ring_stride,
+                            size_t heads, size_t head_dim, float *out) {
+    if (prefill_len + ring_len == 0) return -1;
+    float scale = 1.0f / sqrtf((float)head_dim);
+    float *acc = (float *)malloc(head_dim * sizeof(float));
+    for (size_t h = 0; h < heads; h++) {
+        const float *qh = q + h * head_dim;
+        float run_max = -INFINITY, run_den = 0.0f;
+        for (size_t i = 0; i < head_dim; i++) acc[i] = 0.0f;
+        for (int part = 0; part < 2; part++) {
+            size_t n = part ? ring_len : prefill_len;
+            const float *K = part ? ring_k : ref_k, *V = part ? ring_v : ref_v;
+            size_t stride = part ? ring_stride : ref_stride;
+            for (size_t r = 0; r < n; r++) {
+                const float *kr = K + (h * stride + r) * head_dim;
+                const float *vr = V + (h * stride + r) * head_dim;
+                float d = 0.0f;
+                for (size_t i = 0; i < head_dim; i++) d = d + qh[i] * kr[i];
+                float score = d * scale;
+                if (score > run_max) {
+                    float corr = isfinite(run_max) ? expf(run_max - score) : 0.0f;
+                    run_den = run_den * corr;
+                    for (size_t i = 0; i < head_dim; i++) acc[i] = acc[i] * corr;
+                    run_max = score;
+                }
+                float wgt = expf(score - run_max);
+                run_den = run_den + wgt;
+                for (size_t i = 0; i < head_dim; i++) acc[i] = acc[i] + wgt * vr[i];
+            }
+        }
+        float inv = run_den > 0.0f ? 1.0f / run_den : 0.0f;
+        for (size_t i = 0; i < head_dim; i++) out[h * head_dim + i] = acc[i] * inv;
+    }
+    free(acc);
+    return 0;
+}

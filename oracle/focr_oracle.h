@@ -95,6 +95,18 @@ int oracle_moe_prefill(const oracle_moe_layer *L, const float *x, size_t m,
 int oracle_moe_prefill_routed(const oracle_moe_layer *L, const float *x, size_t m,
                               const int32_t *idx, const float *w, float *y);
 
+/* ---- decoder pieces beside the MoE layer ------------------------------- */
+void oracle_rms_norm(const float *x, size_t rows, size_t cols, const float *w, float eps,
+                     float *y);
+void oracle_rope_table(const size_t *pos, size_t seq, size_t head_dim, float theta, float *cos_t,
+                       float *sin_t);
+void oracle_apply_rope(float *x, size_t seq, size_t cols, size_t head_dim, const float *cos_t,
+                       const float *sin_t);
+int oracle_attention_decode(const float *q, const float *ref_k, const float *ref_v,
+                            size_t prefill_len, size_t ref_stride, const float *ring_k,
+                            const float *ring_v, size_t ring_len, size_t ring_stride,
+                            size_t heads, size_t head_dim, float *out);
+
 /* ---- lm-head / sampler ------------------------------------------------- */
 void oracle_vocab_tile_ranges(size_t n, size_t tiles, size_t *starts, size_t *ends);
 uint32_t oracle_argmax_row(const float *logits, size_t n);

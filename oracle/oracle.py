@@ -71,6 +71,11 @@ lib.oracle_moe_prefill_routed.argtypes = lib.oracle_moe_decode_routed.argtypes
 lib.oracle_moe_prefill_routed.restype = C.c_int
 lib.oracle_cpu_moe_decode.argtypes = [C.POINTER(MoeLayerC), vp, sz, vp, vp, vp, C.c_int]
 lib.oracle_vocab_tile_ranges.argtypes = [sz, sz, vp, vp]
+lib.oracle_rms_norm.argtypes = [vp, sz, sz, vp, C.c_float, vp]
+lib.oracle_rope_table.argtypes = [vp, sz, sz, C.c_float, vp, vp]
+lib.oracle_apply_rope.argtypes = [vp, sz, sz, sz, vp, vp]
+lib.oracle_attention_decode.argtypes = [vp, vp, vp, sz, sz, vp, vp, sz, sz, sz, sz, vp]
+lib.oracle_attention_decode.restype = C.c_int
 lib.oracle_argmax_row.argtypes = [vp, sz]
 
 
@@ -269,3 +274,45 @@ def vocab_tile_ranges(n, tiles):
 def argmax_row(v):
     v = _c(v, np.float32)
     return int(lib.oracle_argmax_row(_p(v), v.size))
+
+
+def rms_norm(x, w=None, eps=1e-6):
+    """nn.rs:240 rms_norm in the order this project defines (see focr_oracle.c)."""
+    x = _c(x, np.float32)
+    rows, cols = x.shape
+    y = np.empty_like(x)
+    lib.oracle_rms_norm(_p(x), rows, cols, _p(_c(w, np.float32)) if w is not None else None,
+                        float(eps), _p(y))
+    return y
+
+
+def rope_table(positions, head_dim, theta=10000.0):
+    """decoder.rs:171 RopeTable::build -> (cos, sin), each [seq, head_dim]."""
+    pos = np.ascontiguousarray(np.asarray(positions, dtype=np.uintp))
+    seq = pos.size
+    cos_t = np.empty((seq, head_dim), np.float32)
+    sin_t = np.empty((seq, head_dim), np.float32)
+    lib.oracle_rope_table(pos.ctypes.data, seq, head_dim, float(theta), _p(cos_t), _p(sin_t))
+    return cos_t, sin_t
+
+
+def apply_rope(x, cos_t, sin_t, head_dim):
+    """decoder.rs:229 apply_rope, returning a rotated copy."""
+    y = np.array(_c(x, np.float32), copy=True)
+    seq, cols = y.shape
+    lib.oracle_apply_rope(_p(y), seq, cols, head_dim, _p(_c(cos_t, np.float32)),
+                          _p(_c(sin_t, np.float32)))
+    return y
+
+
+def attention_decode(q, ref_k, ref_v, prefill_len, ring_k, ring_v, ring_len):
+    """rswa.rs:894 decode_attention_scalar (online-softmax fold)."""
+    q = _c(q, np.float32)
+    heads, hd = q.shape
+    out = np.empty_like(q)
+    rc = lib.oracle_attention_decode(_p(q), _p(_c(ref_k, np.float32)), _p(_c(ref_v, np.float32)),
+                                     prefill_len, ref_k.shape[1], _p(_c(ring_k, np.float32)),
+                                     _p(_c(ring_v, np.float32)), ring_len, ring_k.shape[1],
+                                     heads, hd, _p(out))
+    assert rc == 0, rc
+    return out
