@@ -220,6 +220,8 @@ def run_ours(args, ws, rank, local):
             "config": {"workload": m1["workload"], "l2": m1["l2"], "cuda_graph": m1["cuda_graph"]},
             "roofline": m1["roofline"], "gpu_launches": args.steps}), flush=True)
         return
+    if args.workload == "config3":
+        return config3(args, dev)
     # ring of layers so that consecutive steps stream from HBM
     R = 2
     layers = [MoeLayer(synth.moe_layer(100 + r, shared_inter=SHARED), max_tokens=TOKENS)
@@ -545,6 +547,58 @@ def run_ep(args, ws, rank, local):
         L.close()
 
 
+def config3(args, dev, prefill=1024, n_tokens=256, seed=3):
+    """Config 3: the synthetic 12-layer int8 decoder; one step = a
+    1024-token prefill then a 256-token greedy decode (batch 1).  Timed on the
+    device with CUDA events; the metric is decode tokens/s (256 / decode
+    time), prefill tokens/s beside it."""
+    import torch
+
+    from franken_ocr_b200 import synth
+    from franken_ocr_b200.decoder import DecoderI8
+
+    W = synth.decoder_model(seed)
+    D = DecoderI8(W, max_prefill=prefill)
+    e = torch.from_numpy(synth.prompt_embeds(seed, prefill)).to(dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+
+    def run():
+        ev[0].record()
+        h = D.prefill(e)
+        ev[1].record()
+        toks = []
+        for i in range(n_tokens):
+            _, bi = D.lm_head_top1(h[-1:])
+            tok = int(bi.item())
+            toks.append(tok)
+            if i + 1 < n_tokens:
+                h = D.decode_step(D.embed[tok:tok + 1], prefill + i)
+        ev[2].record()
+        torch.cuda.synchronize()
+        return toks, ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+
+    for _ in range(max(1, args.warmup)):
+        toks0, _, _ = run()
+    pre, dec = [], []
+    for _ in range(args.steps):
+        toks, p_ms, d_ms = run()
+        assert toks == toks0, "greedy tokens changed between runs"
+        pre.append(p_ms)
+        dec.append(d_ms)
+    d_ms, p_ms = float(np.median(dec)), float(np.median(pre))
+    print(json.dumps({
+        "metric": "int8 decoder greedy decode tokens/s (config 3: 12 layers, batch 1)",
+        "value": n_tokens / (d_ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": p_ms + d_ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8 (i32 accumulate, f32 dequant)",
+        "data": "synthetic (random-init weights, N(0,1) prompt embeddings)",
+        "config": {"workload": "config3_decoder_prefill1024_greedy256", "layers": 12,
+                   "prefill_tokens": prefill, "decode_tokens": n_tokens},
+        "prefill_ms": p_ms, "prefill_tokens_per_s": prefill / (p_ms / 1e3),
+        "decode_ms_per_token": d_ms / n_tokens, "tokens_head": toks0[:16]}), flush=True)
+    D.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -553,8 +607,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-m1", action="store_true", help="skip the config-0 single-token line")
-    ap.add_argument("--workload", default="config2", choices=["config2", "config0", "config1"],
-                    help="config0: only the single-token layer; config1: the raw igemm sweep")
+    ap.add_argument("--workload", default="config2", choices=["config2", "config0", "config1", "config3"],
+                    help="config0: only the single-token layer; config1: the raw igemm sweep; "
+                         "config3: the 12-layer decoder")
     args = ap.parse_args()
     ws, rank, local = dist_init()
     if args.impl == "reference":

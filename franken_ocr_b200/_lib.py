@@ -30,7 +30,8 @@ EXPORTS = [
     "focr_moe_decode", "focr_moe_prefill", "focr_moe_forward_rows", "focr_moe_combine", "focr_ep_pack",
     "focr_lmhead_create", "focr_lmhead_destroy", "focr_lmhead_top1",
     "focr_top1_combine", "focr_selftest", "focr_trace_set", "focr_rms_norm", "focr_rope_apply",
-    "focr_attention_decode",
+    "focr_attention_decode", "focr_linear_i8", "focr_swiglu", "focr_add",
+    "focr_attention_prefill", "focr_rope_table",
 ]
 
 
@@ -97,6 +98,11 @@ lib.focr_trace_set.argtypes = [vp, vp, sz]
 lib.focr_rms_norm.argtypes = [vp, sz, sz, vp, C.c_float, vp, i32, vp]
 lib.focr_rope_apply.argtypes = [vp, sz, sz, sz, vp, vp, i32, vp]
 lib.focr_attention_decode.argtypes = [vp, vp, vp, sz, sz, vp, vp, sz, sz, sz, sz, vp, i32, vp]
+lib.focr_linear_i8.argtypes = [vp, sz, sz, vp, vp, sz, i32, vp, i32, vp]
+lib.focr_swiglu.argtypes = [vp, sz, sz, vp, i32, vp]
+lib.focr_add.argtypes = [vp, vp, sz, vp, i32, vp]
+lib.focr_attention_prefill.argtypes = [vp, vp, vp, sz, sz, sz, vp, i32, vp]
+lib.focr_rope_table.argtypes = [vp, sz, sz, C.c_float, vp, vp]
 
 
 def check(rc: int) -> None:

@@ -1,0 +1,348 @@
+// The remaining ops of the int8 decoder layer loop (decoder.rs:2412-2540
+// prefill_with_cache_i8, :2542-2640 decode_step_with_cache_i8), so that a
+// whole 12-layer decoder runs on the device:
+//
+//  * focr_linear_i8        -- a projection with per-row dynamic int8
+//    activations: nn::linear_int8_dynamic (nn.rs:151-173, ties-even,
+//    prefill) or gemv_i8 (decoder.rs:1607, half away, decode).  Rows are
+//    quantised once, the int32 contraction runs on the GEMV tier for <= 16
+//    rows and on the tcgen05 tier above, and the dequant is
+//    ((f32)acc * a_scale) * w_scale -- bit-identical to the oracle.
+//  * focr_swiglu           -- act = silu(g) * u over a [rows, 2*inter]
+//    gate|up output (decoder.rs:1711-1720, :2120-2135); bit-identical.
+//  * focr_add              -- the residual add (decoder.rs:529 add_residual).
+//  * focr_attention_prefill -- decoder.rs:568-654 causal prefill attention on
+//    token-major q/k/v.  Scores are the sequential dot of the oracle's order;
+//    the softmax is an online fold over 32-key tiles, so results agree with
+//    the oracle's two-pass softmax to rounding.
+#include <string>
+
+#include "common.cuh"
+#include "gemv.cuh"
+
+namespace focr {
+
+__global__ void dequant_rows_kernel(const int32_t *__restrict__ acc, const float *__restrict__ a_scale,
+                                    const float *__restrict__ w_scale, int M, int N,
+                                    float *__restrict__ y) {
+    const long n = (long)M * N;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+        const int r = (int)(i / N), o = (int)(i % N);
+        y[i] = __fmul_rn(__fmul_rn((float)acc[i], a_scale[r]), w_scale[o]);
+    }
+}
+
+__global__ void swiglu_kernel(const float *__restrict__ gu, int rows, int inter,
+                              float *__restrict__ act) {
+    const long n = (long)rows * inter;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+        const long r = i / inter, c = i % inter;
+        const float g = gu[r * 2 * inter + c], u = gu[r * 2 * inter + inter + c];
+        act[i] = __fmul_rn(silu_f(g), u);
+    }
+}
+
+__global__ void add_kernel(const float4 *__restrict__ a, const float4 *__restrict__ b, long n4,
+                           float4 *__restrict__ y) {
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
+        const float4 x = a[i], z = b[i];
+        y[i] = make_float4(__fadd_rn(x.x, z.x), __fadd_rn(x.y, z.y), __fadd_rn(x.z, z.z),
+                           __fadd_rn(x.w, z.w));
+    }
+}
+
+__global__ void add_tail_kernel(const float *a, const float *b, long n0, long n, float *y) {
+    for (long i = n0 + threadIdx.x; i < n; i += blockDim.x) y[i] = __fadd_rn(a[i], b[i]);
+}
+
+// Causal prefill attention, head_dim 128.  CTA = (32-query block, head);
+// 8 warps, 4 queries per warp.  Key/value tiles of 32 rows are staged in
+// shared memory (K rows padded to 129 floats: lane j reads row j
+// conflict-free).  Per tile a lane scores one key, the warp takes the tile
+// max, rescales its running (max, sum, acc) and adds p_j * v_j with lane l
+// owning dimensions 4l .. 4l+3.
+constexpr int PA_HD = 128, PA_Q = 32, PA_KT = 32, PA_THREADS = 256;
+constexpr size_t PA_SMEM = ((PA_KT + PA_Q) * PA_HD + PA_KT * (PA_HD + 1)) * sizeof(float);
+
+__global__ void __launch_bounds__(PA_THREADS) attention_prefill_kernel(
+    const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v, int seq,
+    int dim, float *__restrict__ out) {
+    extern __shared__ __align__(16) float pa_sm[];
+    float(*sv)[PA_HD] = reinterpret_cast<float(*)[PA_HD]>(pa_sm);
+    float(*sq)[PA_HD] = reinterpret_cast<float(*)[PA_HD]>(pa_sm + PA_KT * PA_HD);
+    float(*sk)[PA_HD + 1] = reinterpret_cast<float(*)[PA_HD + 1]>(pa_sm + (PA_KT + PA_Q) * PA_HD);
+    const int h = blockIdx.y, q0 = blockIdx.x * PA_Q, tid = threadIdx.x, lane = tid & 31,
+              warp = tid >> 5;
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)PA_HD));
+    for (int i = tid; i < PA_Q * PA_HD; i += PA_THREADS) {
+        const int r = i / PA_HD, c = i % PA_HD;
+        sq[r][c] = q0 + r < seq ? q[(size_t)(q0 + r) * dim + (size_t)h * PA_HD + c] : 0.0f;
+    }
+    float m[4], l[4], acc[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        m[j] = -INFINITY;
+        l[j] = 0.0f;
+#pragma unroll
+        for (int d = 0; d < 4; d++) acc[j][d] = 0.0f;
+    }
+    const int qlast = min(q0 + PA_Q, seq) - 1;
+    for (int k0 = 0; k0 <= qlast; k0 += PA_KT) {
+        __syncthreads();
+        for (int i = tid; i < PA_KT * PA_HD; i += PA_THREADS) {
+            const int r = i / PA_HD, c = i % PA_HD;
+            const bool in = k0 + r < seq;
+            const size_t off = (size_t)(k0 + r) * dim + (size_t)h * PA_HD + c;
+            sk[r][c] = in ? k[off] : 0.0f;
+            sv[r][c] = in ? v[off] : 0.0f;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int qi = warp * 4 + j, t = q0 + qi;
+            if (t >= seq || k0 > t) continue;  // warp-uniform
+            const int key = k0 + lane;
+            float s = -INFINITY;
+            if (key <= t) {
+                float d = 0.0f;
+#pragma unroll 8
+                for (int i = 0; i < PA_HD; i++) d = __fadd_rn(d, __fmul_rn(sq[qi][i], sk[lane][i]));
+                s = __fmul_rn(d, scale);
+            }
+            float tm = s;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, o));
+            const float mn = fmaxf(m[j], tm);
+            const float corr = m[j] == -INFINITY ? 0.0f : dexpf(__fsub_rn(m[j], mn));
+            const float p = key <= t ? dexpf(__fsub_rn(s, mn)) : 0.0f;
+            float ps = p;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ps = __fadd_rn(ps, __shfl_xor_sync(0xffffffffu, ps, o));
+            l[j] = __fadd_rn(__fmul_rn(l[j], corr), ps);
+            m[j] = mn;
+#pragma unroll
+            for (int d = 0; d < 4; d++) acc[j][d] = __fmul_rn(acc[j][d], corr);
+            const int nk = min(PA_KT, t - k0 + 1);
+            for (int kk = 0; kk < nk; kk++) {
+                const float pk = __shfl_sync(0xffffffffu, p, kk);
+                const float4 vv = *reinterpret_cast<const float4 *>(&sv[kk][4 * lane]);
+                acc[j][0] = __fadd_rn(acc[j][0], __fmul_rn(pk, vv.x));
+                acc[j][1] = __fadd_rn(acc[j][1], __fmul_rn(pk, vv.y));
+                acc[j][2] = __fadd_rn(acc[j][2], __fmul_rn(pk, vv.z));
+                acc[j][3] = __fadd_rn(acc[j][3], __fmul_rn(pk, vv.w));
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const int t = q0 + warp * 4 + j;
+        if (t >= seq) continue;
+        const float inv = l[j] > 0.0f ? __fdiv_rn(1.0f, l[j]) : 0.0f;
+        float4 o4 = make_float4(__fmul_rn(acc[j][0], inv), __fmul_rn(acc[j][1], inv),
+                                __fmul_rn(acc[j][2], inv), __fmul_rn(acc[j][3], inv));
+        *reinterpret_cast<float4 *>(out + (size_t)t * dim + (size_t)h * PA_HD + 4 * lane) = o4;
+    }
+}
+
+static unsigned grid_for(long n) {
+    const long b = (n + 255) / 256;
+    return (unsigned)(b < 148 * 16 ? (b > 0 ? b : 1) : 148 * 16);
+}
+
+// y[M, N] = dequant(Q(x) . w^T); device pointers.
+int linear_i8_dev(const float *x, size_t M, size_t K, const int8_t *w, const float *ws, size_t N,
+                  bool te, float *y, cudaStream_t st) {
+    DevBuf bq, bas;
+    FOCR_CUDA_TRY(bq.alloc(M * K, st));
+    FOCR_CUDA_TRY(bas.alloc(M * 4, st));
+    int rc = launch_quantize_rows(x, M, K, te, (int8_t *)bq.p, (float *)bas.p, st);
+    if (rc) return rc;
+    if (M <= 16) return launch_gemv_dequant((const int8_t *)bq.p, (const float *)bas.p, w, ws, M, K, N, y, st);
+    DevBuf bacc;
+    FOCR_CUDA_TRY(bacc.alloc(M * N * 4, st));
+    FOCR_CUDA_TRY(cudaMemsetAsync(bacc.p, 0, M * N * 4, st));
+    rc = launch_igemm(bq.p, false, w, M, K, N, (int32_t *)bacc.p, st);
+    if (rc) return rc;
+    dequant_rows_kernel<<<grid_for((long)(M * N)), 256, 0, st>>>(
+        (const int32_t *)bacc.p, (const float *)bas.p, ws, (int)M, (int)N, y);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    return FOCR_OK;
+}
+
+}  // namespace focr
+
+using namespace focr;
+
+namespace {
+
+struct Staged {
+    DevBuf buf;
+};
+
+int stage_in(Staged &s, const void *host, size_t bytes, cudaStream_t st) {
+    FOCR_CUDA_TRY(s.buf.alloc(bytes, st));
+    if (host && bytes)
+        FOCR_CUDA_TRY(cudaMemcpyAsync(s.buf.p, host, bytes, cudaMemcpyHostToDevice, st));
+    return FOCR_OK;
+}
+
+int finish_out(void *host, const Staged &s, size_t bytes, cudaStream_t st) {
+    if (bytes) FOCR_CUDA_TRY(cudaMemcpyAsync(host, s.buf.p, bytes, cudaMemcpyDeviceToHost, st));
+    FOCR_CUDA_TRY(cudaStreamSynchronize(st));
+    return FOCR_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int focr_linear_i8(const float *x, size_t m, size_t k, const int8_t *w, const float *w_scale,
+                   size_t n, int ties_even, float *y, int mem, void *stream) {
+    if (m == 0 || n == 0) return FOCR_OK;
+    if (!x || !w || !w_scale || !y) return fail(FOCR_E_ARG, "linear_i8: null pointer");
+    if (m > (size_t)INT32_MAX || n > (size_t)INT32_MAX || k > (size_t)INT32_MAX)
+        return fail(FOCR_E_UNSUPPORTED, "linear_i8: dimension exceeds int32 range");
+    cudaStream_t st = (cudaStream_t)stream;
+    if (mem == FOCR_MEM_DEVICE) return linear_i8_dev(x, m, k, w, w_scale, n, ties_even != 0, y, st);
+    if (mem != FOCR_MEM_HOST) return fail(FOCR_E_ARG, "bad mem kind");
+    Staged sx, sw, ss;
+    int rc = stage_in(sx, x, m * k * 4, st);
+    if (!rc) rc = stage_in(sw, w, n * k, st);
+    if (!rc) rc = stage_in(ss, w_scale, n * 4, st);
+    if (rc) return rc;
+    DevBuf dy;
+    FOCR_CUDA_TRY(dy.alloc(m * n * 4, st));
+    rc = linear_i8_dev((const float *)sx.buf.p, m, k, (const int8_t *)sw.buf.p,
+                       (const float *)ss.buf.p, n, ties_even != 0, (float *)dy.p, st);
+    if (rc) return rc;
+    FOCR_CUDA_TRY(cudaMemcpyAsync(y, dy.p, m * n * 4, cudaMemcpyDeviceToHost, st));
+    FOCR_CUDA_TRY(cudaStreamSynchronize(st));
+    return FOCR_OK;
+}
+
+int focr_swiglu(const float *gate_up, size_t rows, size_t inter, float *act, int mem,
+                void *stream) {
+    if (rows == 0 || inter == 0) return FOCR_OK;
+    if (!gate_up || !act) return fail(FOCR_E_ARG, "swiglu: null pointer");
+    cudaStream_t st = (cudaStream_t)stream;
+    const long n = (long)(rows * inter);
+    if (mem == FOCR_MEM_DEVICE) {
+        swiglu_kernel<<<grid_for(n), 256, 0, st>>>(gate_up, (int)rows, (int)inter, act);
+        FOCR_CUDA_TRY(cudaGetLastError());
+        return FOCR_OK;
+    }
+    if (mem != FOCR_MEM_HOST) return fail(FOCR_E_ARG, "bad mem kind");
+    Staged sg, sa;
+    int rc = stage_in(sg, gate_up, rows * inter * 8, st);
+    if (!rc) rc = stage_in(sa, nullptr, rows * inter * 4, st);
+    if (rc) return rc;
+    swiglu_kernel<<<grid_for(n), 256, 0, st>>>((const float *)sg.buf.p, (int)rows, (int)inter,
+                                               (float *)sa.buf.p);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    return finish_out(act, sa, rows * inter * 4, st);
+}
+
+int focr_add(const float *a, const float *b, size_t n, float *y, int mem, void *stream) {
+    if (n == 0) return FOCR_OK;
+    if (!a || !b || !y) return fail(FOCR_E_ARG, "add: null pointer");
+    cudaStream_t st = (cudaStream_t)stream;
+    const float *da = a, *db = b;
+    float *dy = y;
+    Staged sa, sb, sy;
+    if (mem == FOCR_MEM_HOST) {
+        int rc = stage_in(sa, a, n * 4, st);
+        if (!rc) rc = stage_in(sb, b, n * 4, st);
+        if (!rc) rc = stage_in(sy, nullptr, n * 4, st);
+        if (rc) return rc;
+        da = (const float *)sa.buf.p;
+        db = (const float *)sb.buf.p;
+        dy = (float *)sy.buf.p;
+    } else if (mem != FOCR_MEM_DEVICE) {
+        return fail(FOCR_E_ARG, "bad mem kind");
+    }
+    const bool al = ((uintptr_t)da | (uintptr_t)db | (uintptr_t)dy) % 16 == 0;
+    const long n4 = al ? (long)(n / 4) : 0;
+    if (n4)
+        add_kernel<<<grid_for(n4), 256, 0, st>>>((const float4 *)da, (const float4 *)db, n4,
+                                                 (float4 *)dy);
+    if ((long)n > 4 * n4) add_tail_kernel<<<1, 256, 0, st>>>(da, db, 4 * n4, (long)n, dy);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    if (mem == FOCR_MEM_HOST) return finish_out(y, sy, n * 4, st);
+    return FOCR_OK;
+}
+
+int focr_attention_prefill(const float *q, const float *k, const float *v, size_t seq,
+                           size_t heads, size_t head_dim, float *out, int mem, void *stream) {
+    if (seq == 0 || heads == 0) return FOCR_OK;
+    if (!q || !k || !v || !out) return fail(FOCR_E_ARG, "attention_prefill: null pointer");
+    if (head_dim != PA_HD)
+        return fail(FOCR_E_UNSUPPORTED, "attention_prefill: head_dim must be 128, got " +
+                                            std::to_string(head_dim));
+    if (seq > (size_t)INT32_MAX / PA_Q || heads > 65535 || seq * heads * head_dim > (size_t)INT32_MAX * 4)
+        return fail(FOCR_E_UNSUPPORTED, "attention_prefill: too large");
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t bytes = seq * heads * head_dim * 4;
+    const float *dq = q, *dk = k, *dv = v;
+    float *dout = out;
+    Staged sq, sk, sv, so;
+    if (mem == FOCR_MEM_HOST) {
+        int rc = stage_in(sq, q, bytes, st);
+        if (!rc) rc = stage_in(sk, k, bytes, st);
+        if (!rc) rc = stage_in(sv, v, bytes, st);
+        if (!rc) rc = stage_in(so, nullptr, bytes, st);
+        if (rc) return rc;
+        dq = (const float *)sq.buf.p;
+        dk = (const float *)sk.buf.p;
+        dv = (const float *)sv.buf.p;
+        dout = (float *)so.buf.p;
+    } else if (mem != FOCR_MEM_DEVICE) {
+        return fail(FOCR_E_ARG, "bad mem kind");
+    } else if (((uintptr_t)out) % 16) {
+        return fail(FOCR_E_ARG, "attention_prefill: out must be 16-byte aligned");
+    }
+    dim3 grid((unsigned)((seq + PA_Q - 1) / PA_Q), (unsigned)heads);
+    static bool attr = false;
+    if (!attr) {
+        FOCR_CUDA_TRY(cudaFuncSetAttribute(attention_prefill_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)PA_SMEM));
+        attr = true;
+    }
+    attention_prefill_kernel<<<grid, PA_THREADS, PA_SMEM, st>>>(dq, dk, dv, (int)seq,
+                                                          (int)(heads * head_dim), dout);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    if (mem == FOCR_MEM_HOST) return finish_out(out, so, bytes, st);
+    return FOCR_OK;
+}
+
+}  // extern "C"
+
+extern "C" {
+
+/* RopeTable::build (native_engine/decoder.rs:171-213) on the host:
+ * inv_freq[i] = (f32)(1 / theta^(2i / head_dim)) in f64, angle =
+ * (f32)pos * inv_freq[i] in f32, (sin, cos) from the C library's sinf /
+ * cosf -- the functions Rust's f32::sin_cos calls on Linux -- duplicated into
+ * columns i and i + head_dim / 2. */
+int focr_rope_table(const size_t *positions, size_t n, size_t head_dim, float theta,
+                    float *cos_t, float *sin_t) {
+    if (n == 0) return FOCR_OK;
+    if (!positions || !cos_t || !sin_t) return fail(FOCR_E_ARG, "rope_table: null pointer");
+    if (head_dim == 0 || head_dim % 2) return fail(FOCR_E_SHAPE, "rope_table: head_dim must be even");
+    const size_t half = head_dim / 2;
+    for (size_t p = 0; p < n; p++) {
+        for (size_t i = 0; i < half; i++) {
+            const double e = (double)(2 * i) / (double)head_dim;
+            const float inv = (float)(1.0 / pow((double)theta, e));
+            const float a = (float)positions[p] * inv;
+            const float s = sinf(a), c = cosf(a);
+            cos_t[p * head_dim + i] = c;
+            cos_t[p * head_dim + half + i] = c;
+            sin_t[p * head_dim + i] = s;
+            sin_t[p * head_dim + half + i] = s;
+        }
+    }
+    return FOCR_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,276 @@
+"""The int8 decoder on the GPU: prefill, R-SWA decode steps and greedy decode.
+
+Mirrors the reference's int8 decode engine:
+
+* :class:`DecoderWeightsHost` -- ``DecoderWeightCacheI8`` (decoder.rs:2001-2117):
+  per layer the two RMSNorm weights, int8 q/k/v/o projections, and either
+  the dense SwiGLU MLP (layer 0) or a MoE layer; the final norm, the int8
+  lm-head and the f32 token-embedding table;
+* :meth:`DecoderI8.prefill` -- ``prefill_with_cache_i8`` (decoder.rs:2412-2540,
+  monolithic schedule): ties-even int8 projections, RoPE at positions
+  ``0..seq``, causal attention, MoE prefill, and the prefill K/V recorded as
+  each layer's permanent reference block (``RingCache::record_prefill``,
+  rswa.rs:389);
+* :meth:`DecoderI8.decode_step` -- ``decode_step_with_cache_i8``
+  (decoder.rs:2542-2640): half-away int8 GEMVs (q/k/v as one fused GEMV,
+  byte-identical per row), RoPE at the true position, the ring write
+  (``write_decode_step``, rswa.rs:451-500: append until 128 rows, then
+  overwrite the oldest slot) and decode attention over reference ++ ring;
+* :meth:`DecoderI8.lm_head_top1` -- ``lm_head_cached_i8`` (decoder.rs:2275)
+  + ``sampler::argmax_row`` (sampler.rs:168);
+* :meth:`DecoderI8.generate` -- the greedy loop of ``generate_cached_i8``
+  (native_engine/mod.rs:1860-1898): token ``i`` is decoded at position
+  ``prefill_len + i - 1``.  There is no EOS stop: a fixed number of tokens is
+  produced, as the benchmark configuration asks.
+
+Every op is a call into ``libfocr_cuda.so`` on torch's current stream; torch
+only allocates device memory and copies rows (embedding lookup, ring writes,
+reference-block layout).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from ._lib import MEM_DEVICE, check, lib
+from .synth import MoeWeightsHost
+
+HEAD_DIM = 128
+RING_WINDOW = 128
+ROPE_THETA = 10000.0
+RMS_NORM_EPS = 1e-6
+
+
+@dataclass
+class LayerWeightsHost:
+    """One decoder layer: norms f32 ``[hidden]``; projections int8 ``[out, in]``
+    with per-row f32 scales; ``dense`` = dict of gate/up/down ``_w``/``_s``
+    (layer 0) or ``moe`` (layers >= 1)."""
+    input_ln: np.ndarray
+    post_ln: np.ndarray
+    proj: dict = field(default_factory=dict)  # q_w q_s k_w k_s v_w v_s o_w o_s
+    dense: dict | None = None
+    moe: MoeWeightsHost | None = None
+
+
+@dataclass
+class DecoderWeightsHost:
+    hidden: int
+    heads: int
+    vocab: int
+    layers: list
+    final_norm: np.ndarray
+    lm_w: np.ndarray
+    lm_s: np.ndarray
+    embed: np.ndarray  # [vocab, hidden] f32
+    norm_topk_prob: bool = False  # moe.rs:73
+    routed_scaling_factor: float = 1.0  # moe.rs:70
+
+
+def rope_table(positions, head_dim: int = HEAD_DIM, theta: float = ROPE_THETA):
+    """``RopeTable::build`` (decoder.rs:171-213) -> (cos, sin), each
+    ``[len(positions), head_dim]`` f32, built by ``focr_rope_table``."""
+    pos = np.ascontiguousarray(positions, dtype=np.uint64)
+    n = pos.size
+    c = np.empty((n, head_dim), np.float32)
+    s = np.empty((n, head_dim), np.float32)
+    check(lib.focr_rope_table(pos.ctypes.data, n, head_dim, float(theta), c.ctypes.data,
+                              s.ctypes.data))
+    return c, s
+
+
+def _p(t):
+    return t.data_ptr()
+
+
+class DecoderI8:
+    """Device-resident int8 decoder (weights uploaded once) with one R-SWA
+    cache per layer: reference block ``[heads, max_prefill, head_dim]`` and
+    ring ``[heads, 128, head_dim]`` for K and V."""
+
+    def __init__(self, W: DecoderWeightsHost, max_prefill: int, device: str = "cuda"):
+        import torch
+
+        from .lmhead import LmHeadShard
+        from .moe import MoeLayer
+
+        self.W = W
+        self.hidden, self.heads, self.vocab = W.hidden, W.heads, W.vocab
+        self.dim = W.heads * HEAD_DIM
+        self.max_prefill = max_prefill
+        self.dev = torch.device(device)
+        self._torch = torch
+
+        def up(a):
+            return torch.from_numpy(np.ascontiguousarray(a)).to(self.dev)
+
+        self.layers = []
+        for L in W.layers:
+            d = {"input_ln": up(L.input_ln), "post_ln": up(L.post_ln)}
+            for r in ("q", "k", "v", "o"):
+                d[r + "_w"], d[r + "_s"] = up(L.proj[r + "_w"]), up(L.proj[r + "_s"])
+            # fused q|k|v rows for the decode GEMV (fuse_qkv, decoder.rs:1951):
+            # each output row is an independent dot, so byte-identical
+            d["qkv_w"] = torch.cat([d["q_w"], d["k_w"], d["v_w"]]).contiguous()
+            d["qkv_s"] = torch.cat([d["q_s"], d["k_s"], d["v_s"]]).contiguous()
+            if L.dense is not None:
+                d["inter"] = L.dense["gate_w"].shape[0]
+                d["gu_w"] = up(np.concatenate([L.dense["gate_w"], L.dense["up_w"]]))
+                d["gu_s"] = up(np.concatenate([L.dense["gate_s"], L.dense["up_s"]]))
+                d["down_w"], d["down_s"] = up(L.dense["down_w"]), up(L.dense["down_s"])
+            else:
+                d["moe"] = MoeLayer(L.moe, max_tokens=max_prefill,
+                                    norm_topk_prob=W.norm_topk_prob,
+                                    routed_scaling_factor=W.routed_scaling_factor)
+            z = dict(dtype=torch.float32, device=self.dev)
+            d["ref_k"] = torch.zeros((self.heads, max_prefill, HEAD_DIM), **z)
+            d["ref_v"] = torch.zeros((self.heads, max_prefill, HEAD_DIM), **z)
+            d["ring_k"] = torch.zeros((self.heads, RING_WINDOW, HEAD_DIM), **z)
+            d["ring_v"] = torch.zeros((self.heads, RING_WINDOW, HEAD_DIM), **z)
+            self.layers.append(d)
+        self.final_norm = up(W.final_norm)
+        self.head = LmHeadShard(W.lm_w, W.lm_s, row_begin=0, max_tokens=1)
+        self.embed = up(W.embed)
+        self.prefill_len = None
+        self.ring_len = 0
+        self.ring_pos = 0
+
+    def close(self):
+        for d in self.layers:
+            if "moe" in d:
+                d["moe"].close()
+        self.head.close()
+
+    # -- device ops ---------------------------------------------------------------
+    def _stream(self):
+        return self._torch.cuda.current_stream().cuda_stream
+
+    def _empty(self, *shape):
+        return self._torch.empty(shape, dtype=self._torch.float32, device=self.dev)
+
+    def _norm(self, x, w):
+        y = self._empty(*x.shape)
+        check(lib.focr_rms_norm(_p(x), x.shape[0], x.shape[1], _p(w), RMS_NORM_EPS, _p(y),
+                                MEM_DEVICE, self._stream()))
+        return y
+
+    def _linear(self, x, w, s, te: bool):
+        y = self._empty(x.shape[0], w.shape[0])
+        check(lib.focr_linear_i8(_p(x), x.shape[0], x.shape[1], _p(w), _p(s), w.shape[0],
+                                 int(te), _p(y), MEM_DEVICE, self._stream()))
+        return y
+
+    def _add(self, a, b):
+        y = self._empty(*a.shape)
+        check(lib.focr_add(_p(a), _p(b), a.numel(), _p(y), MEM_DEVICE, self._stream()))
+        return y
+
+    def _rope(self, x, cos_t, sin_t, cols=None):
+        check(lib.focr_rope_apply(_p(x), x.shape[0], cols or x.shape[1], HEAD_DIM, _p(cos_t),
+                                  _p(sin_t), MEM_DEVICE, self._stream()))
+
+    def _dense(self, d, x, te: bool):
+        gu = self._linear(x, d["gu_w"], d["gu_s"], te)
+        act = self._empty(x.shape[0], d["inter"])
+        check(lib.focr_swiglu(_p(gu), x.shape[0], d["inter"], _p(act), MEM_DEVICE,
+                              self._stream()))
+        return self._linear(act, d["down_w"], d["down_s"], te)
+
+    # -- reference entry points -----------------------------------------------------
+    def prefill(self, embeds):
+        """``prefill_with_cache_i8``: ``embeds`` ``[seq, hidden]`` (device f32)
+        -> final hidden states ``[seq, hidden]``; resets every layer's cache."""
+        torch = self._torch
+        seq = embeds.shape[0]
+        if not 0 < seq <= self.max_prefill:
+            raise ValueError(f"prefill seq {seq} outside (0, {self.max_prefill}]")
+        c, s = rope_table(np.arange(seq))
+        cos_t, sin_t = torch.from_numpy(c).to(self.dev), torch.from_numpy(s).to(self.dev)
+        x = embeds.contiguous()
+        for d in self.layers:
+            normed = self._norm(x, d["input_ln"])
+            q = self._linear(normed, d["q_w"], d["q_s"], True)
+            k = self._linear(normed, d["k_w"], d["k_s"], True)
+            v = self._linear(normed, d["v_w"], d["v_s"], True)
+            self._rope(q, cos_t, sin_t)
+            self._rope(k, cos_t, sin_t)
+            d["ref_k"][:, :seq].copy_(k.view(seq, self.heads, HEAD_DIM).transpose(0, 1))
+            d["ref_v"][:, :seq].copy_(v.view(seq, self.heads, HEAD_DIM).transpose(0, 1))
+            ctx = self._empty(seq, self.dim)
+            check(lib.focr_attention_prefill(_p(q), _p(k), _p(v), seq, self.heads, HEAD_DIM,
+                                             _p(ctx), MEM_DEVICE, self._stream()))
+            h = self._add(x, self._linear(ctx, d["o_w"], d["o_s"], True))
+            normed2 = self._norm(h, d["post_ln"])
+            if "moe" in d:
+                mlp, _, _ = d["moe"].prefill(normed2)
+            else:
+                mlp = self._dense(d, normed2, True)
+            x = self._add(h, mlp)
+        self.prefill_len = seq
+        self.ring_len = 0
+        self.ring_pos = 0
+        return x
+
+    def _ring_slot(self) -> int:
+        """``RingCache::write_decode_step`` slot rule (rswa.rs:467-493)."""
+        if self.ring_len < RING_WINDOW:
+            slot = self.ring_len
+            self.ring_len += 1
+            self.ring_pos = self.ring_len % RING_WINDOW
+        else:
+            slot = self.ring_pos
+            self.ring_pos = (self.ring_pos + 1) % RING_WINDOW
+        return slot
+
+    def decode_step(self, token_embed, position: int):
+        """``decode_step_with_cache_i8``: ``token_embed`` ``[1, hidden]`` ->
+        hidden ``[1, hidden]``; writes this step's K/V into every ring."""
+        torch = self._torch
+        if self.prefill_len is None:
+            raise RuntimeError("rswa: write_decode_step before record_prefill")
+        c, s = rope_table([position])
+        cos_t, sin_t = torch.from_numpy(c).to(self.dev), torch.from_numpy(s).to(self.dev)
+        slot = self._ring_slot()
+        D = self.dim
+        x = token_embed.contiguous()
+        for d in self.layers:
+            normed = self._norm(x, d["input_ln"])
+            qkv = self._linear(normed, d["qkv_w"], d["qkv_s"], False)
+            self._rope(qkv, cos_t, sin_t, cols=2 * D)  # q and k: one row, 2 * heads heads
+            d["ring_k"][:, slot].copy_(qkv[0, D:2 * D].view(self.heads, HEAD_DIM))
+            d["ring_v"][:, slot].copy_(qkv[0, 2 * D:].view(self.heads, HEAD_DIM))
+            ctx = self._empty(1, D)
+            check(lib.focr_attention_decode(
+                _p(qkv), _p(d["ref_k"]), _p(d["ref_v"]), self.prefill_len, self.max_prefill,
+                _p(d["ring_k"]), _p(d["ring_v"]), self.ring_len, RING_WINDOW, self.heads,
+                HEAD_DIM, _p(ctx), MEM_DEVICE, self._stream()))
+            h = self._add(x, self._linear(ctx, d["o_w"], d["o_s"], False))
+            normed2 = self._norm(h, d["post_ln"])
+            if "moe" in d:
+                mlp, _, _ = d["moe"].decode(normed2)
+            else:
+                mlp = self._dense(d, normed2, False)
+            x = self._add(h, mlp)
+        return x
+
+    def lm_head_top1(self, hidden_row):
+        """``lm_head_cached_i8`` + ``argmax_row`` on a ``[1, hidden]`` row ->
+        (best logit, token id) as device tensors."""
+        normed = self._norm(hidden_row, self.final_norm)
+        bv, bi, _ = self.head.top1(normed)
+        return bv, bi
+
+    def generate(self, embeds, n_tokens: int) -> np.ndarray:
+        """Greedy decode of ``n_tokens`` after prefilling ``embeds``."""
+        h = self.prefill(embeds)
+        seq = embeds.shape[0]
+        out = np.empty(n_tokens, np.int64)
+        for i in range(n_tokens):
+            _, bi = self.lm_head_top1(h[-1:])
+            tok = int(bi.item())
+            out[i] = tok
+            if i + 1 == n_tokens:
+                break
+            h = self.decode_step(self.embed[tok:tok + 1], seq + i)
+        return out

@@ -25,7 +25,9 @@ VOCAB = 129280
 WEIGHT_STD = 0.02
 
 _ROLE = {"router": 1, "gate": 2, "up": 3, "down": 4, "sh_gate": 5, "sh_up": 6, "sh_down": 7,
-         "x": 8, "route": 9, "lm_head": 10}
+         "x": 8, "route": 9, "lm_head": 10, "q": 11, "k": 12, "v": 13, "o": 14,
+         "dense_gate": 15, "dense_up": 16, "dense_down": 17, "norm": 18, "embed": 19,
+         "prompt": 20}
 
 
 def rng(seed: int, role: str, idx: int = 0) -> np.random.Generator:
@@ -128,3 +130,52 @@ def lm_head(seed: int, rows: int, hidden: int = HIDDEN, row_begin: int = 0,
         s[lo - row_begin:hi - row_begin] = ss
         r = hi
     return q, s
+
+
+DENSE_INTER = 6848
+N_LAYERS = 12
+HEADS = 10
+
+
+def decoder_model(seed: int, layers: int = N_LAYERS, hidden: int = HIDDEN, heads: int = HEADS,
+                  n_experts: int = N_EXPERTS, topk: int = TOPK, inter: int = INTER,
+                  shared_inter: int = SHARED_INTER, dense_inter: int = DENSE_INTER,
+                  vocab: int = VOCAB, first_dense: int = 1):
+    """A synthetic int8 decoder with the reference's layout (decoder.rs:2001-2117):
+    layers ``[0, first_dense)`` dense SwiGLU, the rest MoE (``n_experts``
+    routed top-``topk`` plus one shared expert of ``shared_inter`` = the two
+    shared experts of 896 fused), heads x 128 attention, RMSNorm weights
+    1 + N(0, 0.05), projections N(0, 0.02) quantised per row, f32 embeddings
+    N(0, 1).  Layer ``l``'s arrays are drawn from seed ``seed * 1000 + l``."""
+    from .decoder import HEAD_DIM, DecoderWeightsHost, LayerWeightsHost
+
+    D = heads * HEAD_DIM
+    Ls = []
+    for li in range(layers):
+        ls = seed * 1000 + li
+        L = LayerWeightsHost(
+            input_ln=(1.0 + normal(ls, "norm", 0, (hidden,), 0.05)).astype(np.float32),
+            post_ln=(1.0 + normal(ls, "norm", 1, (hidden,), 0.05)).astype(np.float32))
+        for r, shp in (("q", (D, hidden)), ("k", (D, hidden)), ("v", (D, hidden)),
+                       ("o", (hidden, D))):
+            L.proj[r + "_w"], L.proj[r + "_s"] = quantize_int8_f32(normal(ls, r, 0, shp, WEIGHT_STD))
+        if li < first_dense:
+            L.dense = {}
+            for r, shp in (("gate", (dense_inter, hidden)), ("up", (dense_inter, hidden)),
+                           ("down", (hidden, dense_inter))):
+                L.dense[r + "_w"], L.dense[r + "_s"] = quantize_int8_f32(
+                    normal(ls, "dense_" + r, 0, shp, WEIGHT_STD))
+        else:
+            L.moe = moe_layer(ls, hidden=hidden, inter=inter, n_experts=n_experts, topk=topk,
+                              shared_inter=shared_inter)
+        Ls.append(L)
+    lm_w, lm_s = lm_head(seed, vocab, hidden=hidden, block=min(16160, vocab))
+    return DecoderWeightsHost(
+        hidden=hidden, heads=heads, vocab=vocab, layers=Ls,
+        final_norm=(1.0 + normal(seed, "norm", 2, (hidden,), 0.05)).astype(np.float32),
+        lm_w=lm_w, lm_s=lm_s, embed=normal(seed, "embed", 0, (vocab, hidden), 1.0))
+
+
+def prompt_embeds(seed: int, seq: int, hidden: int = HIDDEN) -> np.ndarray:
+    """Prefill input embeddings N(0, 1) ``[seq, hidden]``."""
+    return normal(seed, "prompt", 0, (seq, hidden), 1.0)

@@ -249,6 +249,37 @@ int focr_attention_decode(const float *q, const float *ref_k, const float *ref_v
                           const float *ring_v, size_t ring_len, size_t ring_stride, size_t heads,
                           size_t head_dim, float *out, int mem, void *stream);
 
+/* Projection with per-row dynamic int8 activations, y[m][n] =
+ * ((f32)(Q(x[r]) . w[o]) * a_scale[r]) * w_scale[o].  ties_even = 1 is
+ * nn::linear_int8_dynamic (native_engine/nn.rs:151-173, the prefill
+ * projections of decoder.rs:2514-2529); 0 is gemv_i8 (decoder.rs:1607, half
+ * away from zero, the decode projections of decoder.rs:2560-2620). */
+int focr_linear_i8(const float *x, size_t m, size_t k, const int8_t *w, const float *w_scale,
+                   size_t n, int ties_even, float *y, int mem, void *stream);
+
+/* act[r][i] = silu(gate_up[r][i]) * gate_up[r][inter + i] -- the SwiGLU
+ * step of expert_gemv_i8 / expert_mlp_i8 (decoder.rs:1711-1720, :2120-2135)
+ * over a fused [rows][2 * inter] gate|up projection. */
+int focr_swiglu(const float *gate_up, size_t rows, size_t inter, float *act, int mem,
+                void *stream);
+
+/* y = a + b elementwise -- add_residual (native_engine/decoder.rs:529). */
+int focr_add(const float *a, const float *b, size_t n, float *y, int mem, void *stream);
+
+/* Causal prefill attention on token-major q/k/v [seq][heads * head_dim]
+ * (head_dim 128), scale 1/sqrt(head_dim) -- replaces prefill_attention
+ * (native_engine/decoder.rs:568-654, which calls the third-party nn::sdpa).
+ * Scores are sequential dots in dimension order; the softmax is an online
+ * fold, equal to a two-pass softmax up to f32 rounding. */
+int focr_attention_prefill(const float *q, const float *k, const float *v, size_t seq,
+                           size_t heads, size_t head_dim, float *out, int mem, void *stream);
+
+/* RopeTable::build (native_engine/decoder.rs:171-213), on the host: cos/sin
+ * [n][head_dim] for the given absolute positions, with the C library's
+ * sinf/cosf as the reference's f32::sin_cos. */
+int focr_rope_table(const size_t *positions, size_t n, size_t head_dim, float theta,
+                    float *cos_t, float *sin_t);
+
 /* ---- device event trace (GPU counterpart of FOCR_PROFILE_DECODE,
  * native_engine/decoder.rs:986-1024) ------------------------------------
  * Register a device buffer of `capacity` 16-byte events {u32 tag, u32 phase,

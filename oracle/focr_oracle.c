@@ -619,3 +619,72 @@ int oracle_attention_decode(const float *q, const float *ref_k, const float *ref
     free(acc);
     return 0;
 }
+
+/* ---- config-3 decoder pieces ------------------------------------------- */
+
+/* nn::linear_int8_dynamic (nn.rs:151-173; te = 1, ties-even per-row
+ * activation scale) and decoder.rs:1607 gemv_i8 (te = 0, half away), applied
+ * row by row: y[r, o] = ((f32)(Q(x[r]) . w[o]) * a_scale[r]) * ws[o]. */
+void oracle_linear_i8(const float *x, size_t m, size_t k, const int8_t *w, const float *ws,
+                      size_t n, int te, float *y) {
+    int8_t *xq = (int8_t *)malloc(k ? k : 1);
+    for (size_t r = 0; r < m; r++) {
+        float s = te ? oracle_quantize_row_i8_te(x + r * k, k, xq)
+                     : oracle_quantize_row_i8(x + r * k, k, xq);
+        oracle_gemv_i8_prequant(xq, s, w, ws, n, k, y + r * n);
+    }
+    free(xq);
+}
+
+/* The dense SwiGLU MLP of layer 0: decode_mlp_i8's Dense arm
+ * (decoder.rs:2205-2213 -> expert_gemv_i8 :1711, te = 0) and prefill_mlp_i8's
+ * (decoder.rs:2185-2189 -> expert_mlp_i8 :2120, te = 1), row by row. */
+void oracle_swiglu_mlp_i8(const float *x, size_t m, size_t hidden, size_t inter,
+                          const int8_t *gate_w, const float *gate_s, const int8_t *up_w,
+                          const float *up_s, const int8_t *down_w, const float *down_s, int te,
+                          float *y) {
+    for (size_t r = 0; r < m; r++)
+        expert_i8_q(x + r * hidden, hidden, inter, gate_w, gate_s, up_w, up_s, down_w, down_s,
+                    te, y + r * hidden);
+}
+
+/* decoder.rs:568-654 prefill_attention: causal softmax attention over
+ * token-major q/k/v [seq, heads*head_dim].  The reference runs it through the
+ * external ft-kernel-cpu sdpa, whose summation order is not in the tree; this
+ * restatement fixes one: score_j = (sum_d q[d]*k_j[d], d ascending) * scale,
+ * scale = 1/sqrt(head_dim); p_j = expf(score_j - max) / sum (j ascending);
+ * out[d] = sum_j p_j * v_j[d] (j ascending). */
+int oracle_attention_prefill(const float *q, const float *k, const float *v, size_t seq,
+                             size_t heads, size_t head_dim, float *out) {
+    if (seq == 0) return 0;
+    const size_t dim = heads * head_dim;
+    const float scale = 1.0f / sqrtf((float)head_dim);
+    float *p = (float *)malloc(seq * sizeof(float));
+    for (size_t h = 0; h < heads; h++) {
+        for (size_t t = 0; t < seq; t++) {
+            const float *qt = q + t * dim + h * head_dim;
+            float mx = -INFINITY;
+            for (size_t j = 0; j <= t; j++) {
+                const float *kj = k + j * dim + h * head_dim;
+                float d = 0.0f;
+                for (size_t i = 0; i < head_dim; i++) d = d + qt[i] * kj[i];
+                p[j] = d * scale;
+                if (p[j] > mx) mx = p[j];
+            }
+            float den = 0.0f;
+            for (size_t j = 0; j <= t; j++) {
+                p[j] = expf(p[j] - mx);
+                den = den + p[j];
+            }
+            for (size_t j = 0; j <= t; j++) p[j] = p[j] / den;
+            float *o = out + t * dim + h * head_dim;
+            for (size_t i = 0; i < head_dim; i++) {
+                float acc = 0.0f;
+                for (size_t j = 0; j <= t; j++) acc = acc + p[j] * v[j * dim + h * head_dim + i];
+                o[i] = acc;
+            }
+        }
+    }
+    free(p);
+    return 0;
+}

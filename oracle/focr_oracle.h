@@ -107,6 +107,15 @@ int oracle_attention_decode(const float *q, const float *ref_k, const float *ref
                             const float *ring_v, size_t ring_len, size_t ring_stride,
                             size_t heads, size_t head_dim, float *out);
 
+void oracle_linear_i8(const float *x, size_t m, size_t k, const int8_t *w, const float *ws,
+                      size_t n, int te, float *y);
+void oracle_swiglu_mlp_i8(const float *x, size_t m, size_t hidden, size_t inter,
+                          const int8_t *gate_w, const float *gate_s, const int8_t *up_w,
+                          const float *up_s, const int8_t *down_w, const float *down_s, int te,
+                          float *y);
+int oracle_attention_prefill(const float *q, const float *k, const float *v, size_t seq,
+                             size_t heads, size_t head_dim, float *out);
+
 /* ---- lm-head / sampler ------------------------------------------------- */
 void oracle_vocab_tile_ranges(size_t n, size_t tiles, size_t *starts, size_t *ends);
 uint32_t oracle_argmax_row(const float *logits, size_t n);

@@ -77,6 +77,10 @@ lib.oracle_apply_rope.argtypes = [vp, sz, sz, sz, vp, vp]
 lib.oracle_attention_decode.argtypes = [vp, vp, vp, sz, sz, vp, vp, sz, sz, sz, sz, vp]
 lib.oracle_attention_decode.restype = C.c_int
 lib.oracle_argmax_row.argtypes = [vp, sz]
+lib.oracle_linear_i8.argtypes = [vp, sz, sz, vp, vp, sz, C.c_int, vp]
+lib.oracle_swiglu_mlp_i8.argtypes = [vp, sz, sz, sz, vp, vp, vp, vp, vp, vp, C.c_int, vp]
+lib.oracle_attention_prefill.argtypes = [vp, vp, vp, sz, sz, sz, vp]
+lib.oracle_attention_prefill.restype = C.c_int
 
 
 def _p(a):
@@ -316,3 +320,130 @@ def attention_decode(q, ref_k, ref_v, prefill_len, ring_k, ring_v, ring_len):
                                      heads, hd, _p(out))
     assert rc == 0, rc
     return out
+
+
+def linear_i8(x, w, ws, ties_even):
+    """nn::linear_int8_dynamic (ties_even) / gemv_i8 (half away), row by row."""
+    x, w, ws = _c(x, np.float32), _c(w, np.int8), _c(ws, np.float32)
+    m, k = x.shape
+    n = w.shape[0]
+    y = np.empty((m, n), np.float32)
+    lib.oracle_linear_i8(_p(x), m, k, _p(w), _p(ws), n, int(ties_even), _p(y))
+    return y
+
+
+def swiglu_mlp_i8(x, d, ties_even):
+    """The dense layer-0 MLP (decoder.rs:1711 / :2120) with d = gate/up/down _w/_s."""
+    x = _c(x, np.float32)
+    m, H = x.shape
+    I = d["gate_w"].shape[0]
+    a = {k: _c(v, np.int8 if k.endswith("_w") else np.float32) for k, v in d.items()}
+    y = np.empty((m, H), np.float32)
+    lib.oracle_swiglu_mlp_i8(_p(x), m, H, I, _p(a["gate_w"]), _p(a["gate_s"]), _p(a["up_w"]),
+                             _p(a["up_s"]), _p(a["down_w"]), _p(a["down_s"]), int(ties_even),
+                             _p(y))
+    return y
+
+
+def attention_prefill(q, k, v, heads, head_dim=128):
+    q, k, v = _c(q, np.float32), _c(k, np.float32), _c(v, np.float32)
+    out = np.empty_like(q)
+    rc = lib.oracle_attention_prefill(_p(q), _p(k), _p(v), q.shape[0], heads, head_dim, _p(out))
+    assert rc == 0, rc
+    return out
+
+
+class DecoderOracle:
+    """CPU restatement of the int8 decoder loop over a synth.decoder_model:
+    prefill_with_cache_i8 (decoder.rs:2412-2540), decode_step_with_cache_i8
+    (:2542-2640), lm_head_cached_i8 (:2275) + argmax_row, and the greedy loop
+    of generate_cached_i8 (native_engine/mod.rs:1860-1898), with the RingCache
+    slot rule of rswa.rs:451-500."""
+
+    HD, WINDOW, EPS = 128, 128, 1e-6
+
+    def __init__(self, W):
+        self.W = W
+        self.D = W.heads * self.HD
+        self.moe = [MoeOracle(L.moe, norm_topk_prob=W.norm_topk_prob,
+                              scaling=W.routed_scaling_factor) if L.moe is not None else None
+                    for L in W.layers]
+
+    def _heads(self, t):  # [seq, D] -> [heads, seq, HD]
+        return np.ascontiguousarray(t.reshape(t.shape[0], self.W.heads, self.HD).transpose(1, 0, 2))
+
+    def prefill(self, x):
+        x = _c(x, np.float32)
+        seq = x.shape[0]
+        cos_t, sin_t = rope_table(np.arange(seq), self.HD)
+        self.ref, self.ring = [], []
+        for li, L in enumerate(self.W.layers):
+            P = L.proj
+            n = rms_norm(x, L.input_ln, self.EPS)
+            q = apply_rope(linear_i8(n, P["q_w"], P["q_s"], True), cos_t, sin_t, self.HD)
+            k = apply_rope(linear_i8(n, P["k_w"], P["k_s"], True), cos_t, sin_t, self.HD)
+            v = linear_i8(n, P["v_w"], P["v_s"], True)
+            self.ref.append((self._heads(k), self._heads(v)))
+            z = np.zeros((self.W.heads, self.WINDOW, self.HD), np.float32)
+            self.ring.append((z, z.copy()))
+            ctx = attention_prefill(q, k, v, self.W.heads, self.HD)
+            h = x + linear_i8(ctx, P["o_w"], P["o_s"], True)
+            n2 = rms_norm(h, L.post_ln, self.EPS)
+            if L.moe is not None:
+                rc, mlp, _, _ = self.moe[li].prefill(n2)
+                assert rc == 0, rc
+            else:
+                mlp = swiglu_mlp_i8(n2, L.dense, True)
+            x = h + mlp
+        self.prefill_len, self.ring_len, self.ring_pos = seq, 0, 0
+        return x
+
+    def decode_step(self, x, position):
+        x = _c(x, np.float32).reshape(1, -1)
+        cos_t, sin_t = rope_table([position], self.HD)
+        if self.ring_len < self.WINDOW:
+            slot = self.ring_len
+            self.ring_len += 1
+            self.ring_pos = self.ring_len % self.WINDOW
+        else:
+            slot = self.ring_pos
+            self.ring_pos = (self.ring_pos + 1) % self.WINDOW
+        for li, L in enumerate(self.W.layers):
+            P = L.proj
+            n = rms_norm(x, L.input_ln, self.EPS)
+            q = apply_rope(linear_i8(n, P["q_w"], P["q_s"], False), cos_t, sin_t, self.HD)
+            k = apply_rope(linear_i8(n, P["k_w"], P["k_s"], False), cos_t, sin_t, self.HD)
+            v = linear_i8(n, P["v_w"], P["v_s"], False)
+            rk, rv = self.ring[li]
+            rk[:, slot] = k.reshape(self.W.heads, self.HD)
+            rv[:, slot] = v.reshape(self.W.heads, self.HD)
+            fk, fv = self.ref[li]
+            ctx = attention_decode(q.reshape(self.W.heads, self.HD), fk, fv, self.prefill_len,
+                                   rk, rv, self.ring_len)
+            h = x + linear_i8(ctx.reshape(1, -1), P["o_w"], P["o_s"], False)
+            n2 = rms_norm(h, L.post_ln, self.EPS)
+            if L.moe is not None:
+                rc, mlp, _, _ = self.moe[li].decode(n2)
+                assert rc == 0, rc
+            else:
+                mlp = swiglu_mlp_i8(n2, L.dense, False)
+            x = h + mlp
+        return x
+
+    def lm_head(self, row):
+        n = rms_norm(_c(row, np.float32).reshape(1, -1), self.W.final_norm, self.EPS)
+        return linear_i8(n, self.W.lm_w, self.W.lm_s, False)[0]
+
+    def generate(self, embeds, n_tokens, hiddens=None):
+        h = self.prefill(embeds)
+        seq = embeds.shape[0]
+        out = []
+        for i in range(n_tokens):
+            if hiddens is not None:
+                hiddens.append(h[-1].copy())
+            tok = argmax_row(self.lm_head(h[-1]))
+            out.append(tok)
+            if i + 1 == n_tokens:
+                break
+            h = self.decode_step(self.W.embed[tok], seq + i)
+        return np.array(out, np.int64)
