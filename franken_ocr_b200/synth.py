@@ -39,6 +39,22 @@ def normal(seed: int, role: str, idx: int, shape, std: float) -> np.ndarray:
         np.float32)
 
 
+def _parallel(fn, n: int) -> None:
+    """fn(0..n-1) on a thread pool: numpy's generators and ufuncs release the
+    GIL on large arrays, and every index draws from its own stream, so the
+    result does not depend on scheduling."""
+    import os
+    from concurrent.futures import ThreadPoolExecutor
+
+    workers = min(n, os.cpu_count() or 1, 32)
+    if workers <= 1:
+        for i in range(n):
+            fn(i)
+        return
+    with ThreadPoolExecutor(workers) as ex:
+        list(ex.map(fn, range(n)))
+
+
 @dataclass
 class MoeWeightsHost:
     hidden: int
@@ -73,8 +89,11 @@ def moe_layer(seed: int, hidden: int = HIDDEN, inter: int = INTER, n_experts: in
         else:
             q = np.empty((E,) + shp, dtype=np.int8)
             s = np.empty((E, shp[0]), dtype=np.float32)
-            for e in range(E):
+
+            def one(e, role=role, shp=shp, q=q, s=s):
                 q[e], s[e] = quantize_int8_f32(normal(seed, role, expert_begin + e, shp, WEIGHT_STD))
+
+            _parallel(one, E)
             W.arrays[role + "_w"] = q
             W.arrays[role + "_s"] = s
     if shared_inter:
