@@ -12,9 +12,9 @@
 //    gate|up output (decoder.rs:1711-1720, :2120-2135); bit-identical.
 //  * focr_add              -- the residual add (decoder.rs:529 add_residual).
 //  * focr_attention_prefill -- decoder.rs:568-654 causal prefill attention on
-//    token-major q/k/v.  Scores are the sequential dot of the oracle's order;
-//    the softmax is an online fold over 32-key tiles, so results agree with
-//    the oracle's two-pass softmax to rounding.
+//    token-major q/k/v in the evaluation order the oracle fixes for the
+//    reference's third-party sdpa (sequential dots, max, exp, key-order sum,
+//    divide, key-order probs.V); bit-identical to it up to exp.
 #include <string>
 
 #include "common.cuh"
@@ -55,93 +55,70 @@ __global__ void add_tail_kernel(const float *a, const float *b, long n0, long n,
     for (long i = n0 + threadIdx.x; i < n; i += blockDim.x) y[i] = __fadd_rn(a[i], b[i]);
 }
 
-// Causal prefill attention, head_dim 128.  CTA = (32-query block, head);
-// 8 warps, 4 queries per warp.  Key/value tiles of 32 rows are staged in
-// shared memory (K rows padded to 129 floats: lane j reads row j
-// conflict-free).  Per tile a lane scores one key, the warp takes the tile
-// max, rescales its running (max, sum, acc) and adds p_j * v_j with lane l
-// owning dimensions 4l .. 4l+3.
-constexpr int PA_HD = 128, PA_Q = 32, PA_KT = 32, PA_THREADS = 256;
-constexpr size_t PA_SMEM = ((PA_KT + PA_Q) * PA_HD + PA_KT * (PA_HD + 1)) * sizeof(float);
+// Causal prefill attention, head_dim 128, bit-identical to the two-pass
+// softmax the oracle restates: a warp per (query, head).  Lanes score keys
+// j = lane, lane + 32, ... with the sequential dot; the warp takes the max;
+// p_j = exp(s_j - max) in parallel; lane 0 sums p_j in key order (the serial
+// chain the definition fixes); p_j /= sum in parallel; then lane l owns
+// dimensions l, l + 32, l + 64, l + 96 and sums p_j * v_j[d] in key order.
+// Each warp keeps its query's scores in its own shared-memory row of
+// PA_ROW floats; rows are padded so that a query of length seq fits.
+constexpr int PA_HD = 128, PA_WARPS = 8;
 
-__global__ void __launch_bounds__(PA_THREADS) attention_prefill_kernel(
+__global__ void __launch_bounds__(PA_WARPS * 32) attention_prefill_kernel(
     const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v, int seq,
-    int dim, float *__restrict__ out) {
+    int dim, int row, float *__restrict__ out) {
     extern __shared__ __align__(16) float pa_sm[];
-    float(*sv)[PA_HD] = reinterpret_cast<float(*)[PA_HD]>(pa_sm);
-    float(*sq)[PA_HD] = reinterpret_cast<float(*)[PA_HD]>(pa_sm + PA_KT * PA_HD);
-    float(*sk)[PA_HD + 1] = reinterpret_cast<float(*)[PA_HD + 1]>(pa_sm + (PA_KT + PA_Q) * PA_HD);
-    const int h = blockIdx.y, q0 = blockIdx.x * PA_Q, tid = threadIdx.x, lane = tid & 31,
-              warp = tid >> 5;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int h = blockIdx.y;
+    const int t = blockIdx.x * PA_WARPS + warp;  // query
+    if (t >= seq) return;
+    float *sp = pa_sm + (size_t)warp * row;
+    float *sqv = pa_sm + (size_t)PA_WARPS * row + warp * PA_HD;
+    const float *qt = q + (size_t)t * dim + (size_t)h * PA_HD;
+    for (int i = lane; i < PA_HD; i += 32) sqv[i] = qt[i];
+    __syncwarp();
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)PA_HD));
-    for (int i = tid; i < PA_Q * PA_HD; i += PA_THREADS) {
-        const int r = i / PA_HD, c = i % PA_HD;
-        sq[r][c] = q0 + r < seq ? q[(size_t)(q0 + r) * dim + (size_t)h * PA_HD + c] : 0.0f;
-    }
-    float m[4], l[4], acc[4][4];
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-        m[j] = -INFINITY;
-        l[j] = 0.0f;
-#pragma unroll
-        for (int d = 0; d < 4; d++) acc[j][d] = 0.0f;
-    }
-    const int qlast = min(q0 + PA_Q, seq) - 1;
-    for (int k0 = 0; k0 <= qlast; k0 += PA_KT) {
-        __syncthreads();
-        for (int i = tid; i < PA_KT * PA_HD; i += PA_THREADS) {
-            const int r = i / PA_HD, c = i % PA_HD;
-            const bool in = k0 + r < seq;
-            const size_t off = (size_t)(k0 + r) * dim + (size_t)h * PA_HD + c;
-            sk[r][c] = in ? k[off] : 0.0f;
-            sv[r][c] = in ? v[off] : 0.0f;
+    float mx = -INFINITY;
+    for (int j = lane; j <= t; j += 32) {
+        const float *kj = k + (size_t)j * dim + (size_t)h * PA_HD;
+        float d = 0.0f;
+        for (int i = 0; i < PA_HD; i += 4) {
+            const float4 k4 = *reinterpret_cast<const float4 *>(kj + i);
+            d = __fadd_rn(d, __fmul_rn(sqv[i], k4.x));
+            d = __fadd_rn(d, __fmul_rn(sqv[i + 1], k4.y));
+            d = __fadd_rn(d, __fmul_rn(sqv[i + 2], k4.z));
+            d = __fadd_rn(d, __fmul_rn(sqv[i + 3], k4.w));
         }
-        __syncthreads();
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int qi = warp * 4 + j, t = q0 + qi;
-            if (t >= seq || k0 > t) continue;  // warp-uniform
-            const int key = k0 + lane;
-            float s = -INFINITY;
-            if (key <= t) {
-                float d = 0.0f;
-#pragma unroll 8
-                for (int i = 0; i < PA_HD; i++) d = __fadd_rn(d, __fmul_rn(sq[qi][i], sk[lane][i]));
-                s = __fmul_rn(d, scale);
-            }
-            float tm = s;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, o));
-            const float mn = fmaxf(m[j], tm);
-            const float corr = m[j] == -INFINITY ? 0.0f : dexpf(__fsub_rn(m[j], mn));
-            const float p = key <= t ? dexpf(__fsub_rn(s, mn)) : 0.0f;
-            float ps = p;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) ps = __fadd_rn(ps, __shfl_xor_sync(0xffffffffu, ps, o));
-            l[j] = __fadd_rn(__fmul_rn(l[j], corr), ps);
-            m[j] = mn;
-#pragma unroll
-            for (int d = 0; d < 4; d++) acc[j][d] = __fmul_rn(acc[j][d], corr);
-            const int nk = min(PA_KT, t - k0 + 1);
-            for (int kk = 0; kk < nk; kk++) {
-                const float pk = __shfl_sync(0xffffffffu, p, kk);
-                const float4 vv = *reinterpret_cast<const float4 *>(&sv[kk][4 * lane]);
-                acc[j][0] = __fadd_rn(acc[j][0], __fmul_rn(pk, vv.x));
-                acc[j][1] = __fadd_rn(acc[j][1], __fmul_rn(pk, vv.y));
-                acc[j][2] = __fadd_rn(acc[j][2], __fmul_rn(pk, vv.z));
-                acc[j][3] = __fadd_rn(acc[j][3], __fmul_rn(pk, vv.w));
-            }
-        }
+        const float sc = __fmul_rn(d, scale);
+        sp[j] = sc;
+        mx = sc > mx ? sc : mx;
     }
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-        const int t = q0 + warp * 4 + j;
-        if (t >= seq) continue;
-        const float inv = l[j] > 0.0f ? __fdiv_rn(1.0f, l[j]) : 0.0f;
-        float4 o4 = make_float4(__fmul_rn(acc[j][0], inv), __fmul_rn(acc[j][1], inv),
-                                __fmul_rn(acc[j][2], inv), __fmul_rn(acc[j][3], inv));
-        *reinterpret_cast<float4 *>(out + (size_t)t * dim + (size_t)h * PA_HD + 4 * lane) = o4;
+    for (int o = 16; o > 0; o >>= 1) {
+        const float other = __shfl_xor_sync(0xffffffffu, mx, o);
+        mx = other > mx ? other : mx;
     }
+    for (int j = lane; j <= t; j += 32) sp[j] = dexpf(__fsub_rn(sp[j], mx));
+    __syncwarp();
+    float den = 0.0f;
+    if (lane == 0)
+        for (int j = 0; j <= t; j++) den = __fadd_rn(den, sp[j]);
+    den = __shfl_sync(0xffffffffu, den, 0);
+    __syncwarp();
+    for (int j = lane; j <= t; j += 32) sp[j] = __fdiv_rn(sp[j], den);
+    __syncwarp();
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const float *vh = v + (size_t)h * PA_HD + lane;
+    for (int j = 0; j <= t; j++) {
+        const float p = sp[j];
+        const float *vj = vh + (size_t)j * dim;
+#pragma unroll
+        for (int c = 0; c < 4; c++) acc[c] = __fadd_rn(acc[c], __fmul_rn(p, vj[32 * c]));
+    }
+    float *o = out + (size_t)t * dim + (size_t)h * PA_HD + lane;
+#pragma unroll
+    for (int c = 0; c < 4; c++) o[32 * c] = acc[c];
 }
 
 static unsigned grid_for(long n) {
@@ -278,7 +255,7 @@ int focr_attention_prefill(const float *q, const float *k, const float *v, size_
     if (head_dim != PA_HD)
         return fail(FOCR_E_UNSUPPORTED, "attention_prefill: head_dim must be 128, got " +
                                             std::to_string(head_dim));
-    if (seq > (size_t)INT32_MAX / PA_Q || heads > 65535 || seq * heads * head_dim > (size_t)INT32_MAX * 4)
+    if (seq > (size_t)INT32_MAX / 8 || heads > 65535 || seq * heads * head_dim > (size_t)INT32_MAX * 4)
         return fail(FOCR_E_UNSUPPORTED, "attention_prefill: too large");
     cudaStream_t st = (cudaStream_t)stream;
     const size_t bytes = seq * heads * head_dim * 4;
@@ -297,19 +274,23 @@ int focr_attention_prefill(const float *q, const float *k, const float *v, size_
         dout = (float *)so.buf.p;
     } else if (mem != FOCR_MEM_DEVICE) {
         return fail(FOCR_E_ARG, "bad mem kind");
-    } else if (((uintptr_t)out) % 16) {
-        return fail(FOCR_E_ARG, "attention_prefill: out must be 16-byte aligned");
+    } else if (((uintptr_t)k) % 16) {
+        return fail(FOCR_E_ARG, "attention_prefill: k must be 16-byte aligned");
     }
-    dim3 grid((unsigned)((seq + PA_Q - 1) / PA_Q), (unsigned)heads);
+    const int rowf = (int)((seq + 3) / 4 * 4);
+    const size_t smem = ((size_t)PA_WARPS * rowf + PA_WARPS * PA_HD) * sizeof(float);
+    if (smem > 220 * 1024)
+        return fail(FOCR_E_UNSUPPORTED, "attention_prefill: seq above 6880 tokens");
     static bool attr = false;
     if (!attr) {
         FOCR_CUDA_TRY(cudaFuncSetAttribute(attention_prefill_kernel,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)PA_SMEM));
+                                           220 * 1024));
         attr = true;
     }
-    attention_prefill_kernel<<<grid, PA_THREADS, PA_SMEM, st>>>(dq, dk, dv, (int)seq,
-                                                          (int)(heads * head_dim), dout);
+    dim3 grid((unsigned)((seq + PA_WARPS - 1) / PA_WARPS), (unsigned)heads);
+    attention_prefill_kernel<<<grid, PA_WARPS * 32, smem, st>>>(dq, dk, dv, (int)seq,
+                                                                (int)(heads * head_dim), rowf, dout);
     FOCR_CUDA_TRY(cudaGetLastError());
     if (mem == FOCR_MEM_HOST) return finish_out(out, so, bytes, st);
     return FOCR_OK;

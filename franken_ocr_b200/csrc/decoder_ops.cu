@@ -61,25 +61,35 @@ __global__ void rope_kernel(float *__restrict__ x, int seq, int cols, int head_d
 constexpr int ATT_THREADS = 256;
 constexpr int ATT_MAX_KEYS = 16384;
 
-// One CTA per head.  Shared memory: q [head_dim], probabilities [total],
-// per-warp reduction scratch, partial outputs [ATT_THREADS].
+// One CTA per head; bit-identical to the reference's per-key online fold
+// (rswa.rs:894-944 with fold at :1163-1182):
+//   1. every key's score (the reference's sequential dot) in parallel;
+//   2. the running max as a prefix scan (m_r = s_r > m_{r-1} ? s_r : m_{r-1},
+//      which skips NaN as the reference's `score > run_max` does);
+//   3. per key, in parallel, the fold's two exponentials: the correction
+//      c_r = exp(m_{r-1} - s_r) (0 while m_{r-1} is -inf, exactly 1 when the
+//      max did not move -- multiplying by 1 is exact, so it stands in for the
+//      skipped branch) and the weight w_r = exp(s_r - m_r);
+//   4. the serial part, den = den * c_r + w_r and acc[d] = acc[d] * c_r +
+//      w_r * v_r[d] in key order, with thread d owning dimension d.
+// Shared memory: q [head_dim] | scores/max [total] | corr [total] | w [total]
+// | chunk maxima [ATT_THREADS].
 __global__ void __launch_bounds__(ATT_THREADS) attention_decode_kernel(
     const float *__restrict__ q, const float *__restrict__ ref_k, const float *__restrict__ ref_v,
     int prefill_len, int ref_stride, const float *__restrict__ ring_k,
     const float *__restrict__ ring_v, int ring_len, int ring_stride, int head_dim,
     float *__restrict__ out) {
     extern __shared__ float att_sm[];
-    const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int h = blockIdx.x, tid = threadIdx.x;
     const int total = prefill_len + ring_len;
-    float *sq = att_sm;                       // [head_dim]
-    float *sp = sq + head_dim;                // [total]
-    float *red = sp + total;                  // [ATT_THREADS / 32]
-    float *po = red + ATT_THREADS / 32;       // [ATT_THREADS]
+    float *sq = att_sm;            // [head_dim]
+    float *ss = sq + head_dim;     // [total] scores
+    float *sc = ss + total;        // [total] corrections
+    float *sw = sc + total;        // [total] weights
+    float *cm = sw + total;        // [ATT_THREADS] chunk maxima
     for (int i = tid; i < head_dim; i += ATT_THREADS) sq[i] = q[(size_t)h * head_dim + i];
     __syncthreads();
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)head_dim));
-    // scores: the reference's dot, d = 0 .. head_dim - 1 in order
-    float m = -INFINITY;
     for (int r = tid; r < total; r += ATT_THREADS) {
         const float *kr = r < prefill_len
                               ? ref_k + ((size_t)h * ref_stride + r) * head_dim
@@ -92,48 +102,55 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_decode_kernel(
             d = __fadd_rn(d, __fmul_rn(sq[i + 2], k4.z));
             d = __fadd_rn(d, __fmul_rn(sq[i + 3], k4.w));
         }
-        const float sc = __fmul_rn(d, scale);
-        sp[r] = sc;
-        m = fmaxf(m, sc);
+        ss[r] = __fmul_rn(d, scale);
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) red[warp] = m;
     __syncthreads();
-    m = red[0];
-    for (int w = 1; w < ATT_THREADS / 32; w++) m = fmaxf(m, red[w]);
+    // prefix max: contiguous chunks per thread, then the chunk maxima in order
+    const int per = (total + ATT_THREADS - 1) / ATT_THREADS;
+    const int c0 = tid * per, c1 = min(c0 + per, total);
+    float m = -INFINITY;
+    for (int r = c0; r < c1; r++) m = ss[r] > m ? ss[r] : m;
+    cm[tid] = m;
     __syncthreads();
-    // probabilities (unnormalised) and their sum
-    float den = 0.0f;
-    for (int r = tid; r < total; r += ATT_THREADS) {
-        const float p = dexpf(__fsub_rn(sp[r], m));
-        sp[r] = p;
-        den = __fadd_rn(den, p);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) den = __fadd_rn(den, __shfl_xor_sync(0xffffffffu, den, o));
-    if (lane == 0) red[warp] = den;
-    __syncthreads();
-    den = red[0];
-    for (int w = 1; w < ATT_THREADS / 32; w++) den = __fadd_rn(den, red[w]);
-    // probs . V: thread (g, d) sums keys r = g, g + G, ... for dimension d
-    const int G = ATT_THREADS / head_dim;
-    const int d = tid % head_dim, g = tid / head_dim;
-    float acc = 0.0f;
-    if (g < G)
-        for (int r = g; r < total; r += G) {
-            const float *vr = r < prefill_len
-                                  ? ref_v + ((size_t)h * ref_stride + r) * head_dim
-                                  : ring_v + ((size_t)h * ring_stride + (r - prefill_len)) * head_dim;
-            acc = __fadd_rn(acc, __fmul_rn(sp[r], vr[d]));
+    if (tid == 0) {
+        float run = -INFINITY;
+        for (int t = 0; t < ATT_THREADS; t++) {
+            const float v = cm[t];
+            cm[t] = run;  // max before chunk t
+            run = v > run ? v : run;
         }
-    po[tid] = acc;
+    }
     __syncthreads();
+    m = cm[tid];
+    for (int r = c0; r < c1; r++) {
+        const float s = ss[r];
+        float c = 1.0f;
+        if (s > m) {
+            c = m == -INFINITY ? 0.0f : dexpf(__fsub_rn(m, s));
+            m = s;
+        }
+        sc[r] = c;
+        sw[r] = dexpf(__fsub_rn(s, m));
+    }
+    __syncthreads();
+    float den = 0.0f;
     if (tid < head_dim) {
-        float a = 0.0f;
-        for (int gg = 0; gg < G; gg++) a = __fadd_rn(a, po[gg * head_dim + tid]);
+        float acc = 0.0f;
+        int r = 0;
+        for (; r < prefill_len; r++) {
+            const float c = sc[r], w = sw[r];
+            const float v = ref_v[((size_t)h * ref_stride + r) * head_dim + tid];
+            acc = __fadd_rn(__fmul_rn(acc, c), __fmul_rn(w, v));
+            den = __fadd_rn(__fmul_rn(den, c), w);
+        }
+        for (; r < total; r++) {
+            const float c = sc[r], w = sw[r];
+            const float v = ring_v[((size_t)h * ring_stride + (r - prefill_len)) * head_dim + tid];
+            acc = __fadd_rn(__fmul_rn(acc, c), __fmul_rn(w, v));
+            den = __fadd_rn(__fmul_rn(den, c), w);
+        }
         const float inv = den > 0.0f ? __fdiv_rn(1.0f, den) : 0.0f;
-        out[(size_t)h * head_dim + tid] = __fmul_rn(a, inv);
+        out[(size_t)h * head_dim + tid] = __fmul_rn(acc, inv);
     }
 }
 
@@ -238,14 +255,12 @@ int focr_attention_decode(const float *q, const float *ref_k, const float *ref_v
         return fail(FOCR_E_UNSUPPORTED, "attention_decode: more than 16384 keys or 65535 heads");
     cudaStream_t st = (cudaStream_t)stream;
     const size_t total = prefill_len + ring_len;
-    const size_t smem = (head_dim + total + ATT_THREADS / 32 + ATT_THREADS) * sizeof(float);
+    const size_t smem = (head_dim + 3 * total + ATT_THREADS) * sizeof(float);
     static bool attr = false;
     if (!attr) {
         FOCR_CUDA_TRY(cudaFuncSetAttribute(attention_decode_kernel,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)((head_dim > 256 ? head_dim : 256) + ATT_MAX_KEYS +
-                                                 ATT_THREADS / 32 + ATT_THREADS) *
-                                               4));
+                                           (int)((256 + 3 * ATT_MAX_KEYS + ATT_THREADS) * 4)));
         attr = true;
     }
     const float *dq = q, *drk = ref_k, *drv = ref_v, *dgk = ring_k, *dgv = ring_v;

@@ -1,8 +1,8 @@
 """GPU parity of the config-3 decoder: the new ops against the oracle
-(bit-exact for the int8 projections, SwiGLU and residual add; within 1e-5
-for causal prefill attention, whose softmax is an online fold on the device
-and a two-pass sum in the oracle), then whole decoders: prefill, R-SWA decode
-steps through a ring wrap, and identical greedy tokens."""
+(bit-exact for the int8 projections, SwiGLU and residual add; causal prefill
+attention in the oracle's evaluation order, bit-exact except where libm's expf
+and the device's exp round differently), then whole decoders: prefill, R-SWA
+decode steps through a ring wrap, and identical greedy tokens."""
 import numpy as np
 import pytest
 
@@ -69,7 +69,9 @@ def test_attention_prefill_close(cuda, oracle, seq):
     check(lib.focr_attention_prefill(q.ctypes.data, k.ctypes.data, v.ctypes.data, seq, heads,
                                      128, out.ctypes.data, 0, None))
     want = oracle.attention_prefill(q, k, v, heads)
-    assert rel_err(out, want) < 1e-5, rel_err(out, want)
+    from tests.test_gpu_moe import assert_close_rel
+
+    assert_close_rel(out, want, f"prefill attention seq={seq}", min_exact=0.9)
     assert np.array_equal(out[0], v[0])
 
 
