@@ -121,6 +121,59 @@ __global__ void __launch_bounds__(PA_WARPS * 32) attention_prefill_kernel(
     for (int c = 0; c < 4; c++) o[32 * c] = acc[c];
 }
 
+// One decode step's device-side bookkeeping (decode_step_with_cache_i8 +
+// RingCache::write_decode_step, rswa.rs:467-493, + the greedy loop's
+// position rule, native_engine/mod.rs:1895): record the previous step's
+// argmax token, advance the position and the ring cursor, and gather the
+// token's embedding row.
+__global__ void decode_prologue_kernel(int *__restrict__ st, const int *__restrict__ token,
+                                       const float *__restrict__ embed, int vocab, int hidden,
+                                       int ring_window, int *__restrict__ tokens_out,
+                                       int max_tokens, float *__restrict__ x) {
+    __shared__ int tok;
+    if (threadIdx.x == 0) {
+        int t = *token;
+        if (t < 0 || t >= vocab) {
+            st[FOCR_STATE_ERROR] = 1;
+            t = 0;
+        }
+        tok = t;
+        const int n = st[FOCR_STATE_STEP];
+        if (tokens_out && n < max_tokens) tokens_out[n] = t;
+        st[FOCR_STATE_STEP] = n + 1;
+        st[FOCR_STATE_POS] = st[FOCR_STATE_NEXT_POS];
+        st[FOCR_STATE_NEXT_POS] = st[FOCR_STATE_POS] + 1;
+        const int len = st[FOCR_STATE_RING_LEN];
+        if (len < ring_window) {
+            st[FOCR_STATE_SLOT] = len;
+            st[FOCR_STATE_RING_LEN] = len + 1;
+            st[FOCR_STATE_RING_POS] = (len + 1) % ring_window;
+        } else {
+            const int pos = st[FOCR_STATE_RING_POS];
+            st[FOCR_STATE_SLOT] = pos;
+            st[FOCR_STATE_RING_POS] = (pos + 1) % ring_window;
+        }
+    }
+    __syncthreads();
+    const float *row = embed + (size_t)tok * hidden;
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x) x[i] = row[i];
+}
+
+// ring_k/v[h][slot][:] = k/v[h][:] with slot from the step state.
+__global__ void ring_write_kernel(const float *__restrict__ k, const float *__restrict__ v,
+                                  int heads, int head_dim, float *__restrict__ ring_k,
+                                  float *__restrict__ ring_v, int ring_stride,
+                                  const int *__restrict__ st) {
+    const int slot = st[FOCR_STATE_SLOT];
+    const int n = heads * head_dim;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const int h = i / head_dim, d = i % head_dim;
+        const size_t dst = ((size_t)h * ring_stride + slot) * head_dim + d;
+        ring_k[dst] = k[i];
+        ring_v[dst] = v[i];
+    }
+}
+
 static unsigned grid_for(long n) {
     const long b = (n + 255) / 256;
     return (unsigned)(b < 148 * 16 ? (b > 0 ? b : 1) : 148 * 16);
@@ -323,6 +376,31 @@ int focr_rope_table(const size_t *positions, size_t n, size_t head_dim, float th
             sin_t[p * head_dim + half + i] = s;
         }
     }
+    return FOCR_OK;
+}
+
+
+int focr_decode_prologue(int32_t *state, const int32_t *token, const float *embed, size_t vocab,
+                         size_t hidden, size_t ring_window, int32_t *tokens_out,
+                         size_t max_tokens, float *x, void *stream) {
+    if (!state || !token || !embed || !x) return fail(FOCR_E_ARG, "decode_prologue: null pointer");
+    if (ring_window == 0 || vocab > (size_t)INT32_MAX || hidden > (size_t)INT32_MAX)
+        return fail(FOCR_E_SHAPE, "decode_prologue: bad sizes");
+    decode_prologue_kernel<<<1, 256, 0, (cudaStream_t)stream>>>(
+        state, token, embed, (int)vocab, (int)hidden, (int)ring_window, tokens_out,
+        (int)max_tokens, x);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    return FOCR_OK;
+}
+
+int focr_ring_write(const float *k, const float *v, size_t heads, size_t head_dim, float *ring_k,
+                    float *ring_v, size_t ring_stride, const int32_t *state, void *stream) {
+    if (!k || !v || !ring_k || !ring_v || !state) return fail(FOCR_E_ARG, "ring_write: null pointer");
+    const long n = (long)(heads * head_dim);
+    if (n == 0) return FOCR_OK;
+    ring_write_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+        k, v, (int)heads, (int)head_dim, ring_k, ring_v, (int)ring_stride, state);
+    FOCR_CUDA_TRY(cudaGetLastError());
     return FOCR_OK;
 }
 

@@ -42,9 +42,16 @@ __global__ void rms_norm_kernel(const float *__restrict__ x, int rows, int cols,
 }
 
 // One thread per (row, head, i < half).
+// With pos_dev set (one row), the table row is the decode position read
+// from device memory, so a captured decode step replays at any position.
 __global__ void rope_kernel(float *__restrict__ x, int seq, int cols, int head_dim,
-                            const float *__restrict__ cos_t, const float *__restrict__ sin_t) {
+                            const float *__restrict__ cos_t, const float *__restrict__ sin_t,
+                            const int *__restrict__ pos_dev = nullptr) {
     const int half = head_dim / 2, heads = cols / head_dim;
+    if (pos_dev) {
+        cos_t += (size_t)(*pos_dev) * head_dim;
+        sin_t += (size_t)(*pos_dev) * head_dim;
+    }
     const long n = (long)seq * heads * half;
     for (long g = blockIdx.x * (long)blockDim.x + threadIdx.x; g < n; g += (long)gridDim.x * blockDim.x) {
         const int i = (int)(g % half);
@@ -78,9 +85,10 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_decode_kernel(
     const float *__restrict__ q, const float *__restrict__ ref_k, const float *__restrict__ ref_v,
     int prefill_len, int ref_stride, const float *__restrict__ ring_k,
     const float *__restrict__ ring_v, int ring_len, int ring_stride, int head_dim,
-    float *__restrict__ out) {
+    float *__restrict__ out, const int *__restrict__ ring_len_dev = nullptr) {
     extern __shared__ float att_sm[];
     const int h = blockIdx.x, tid = threadIdx.x;
+    if (ring_len_dev) ring_len = *ring_len_dev;
     const int total = prefill_len + ring_len;
     float *sq = att_sm;            // [head_dim]
     float *ss = sq + head_dim;     // [total] scores
@@ -293,6 +301,48 @@ int focr_attention_decode(const float *q, const float *ref_k, const float *ref_v
         FOCR_CUDA_TRY(cudaMemcpyAsync(out, dout, heads * head_dim * 4, cudaMemcpyDeviceToHost, st));
         FOCR_CUDA_TRY(cudaStreamSynchronize(st));
     }
+    return FOCR_OK;
+}
+
+
+/* ---- device-state decode step (capturable in a CUDA graph) ------------- */
+
+int focr_rope_apply_at(float *x, size_t cols, size_t head_dim, const float *cos_table,
+                       const float *sin_table, const int32_t *state, void *stream) {
+    if (!x || !cos_table || !sin_table || !state) return fail(FOCR_E_ARG, "rope_apply_at: null pointer");
+    if (head_dim == 0 || head_dim % 2 || cols % head_dim || cols > (size_t)INT32_MAX)
+        return fail(FOCR_E_SHAPE, "rope_apply_at: cols not a multiple of head_dim");
+    const long n = (long)(cols / 2);
+    rope_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+        x, 1, (int)cols, (int)head_dim, cos_table, sin_table, state + FOCR_STATE_POS);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    return FOCR_OK;
+}
+
+int focr_attention_decode_at(const float *q, const float *ref_k, const float *ref_v,
+                             size_t prefill_len, size_t ref_stride, const float *ring_k,
+                             const float *ring_v, size_t ring_stride, size_t heads,
+                             size_t head_dim, const int32_t *state, float *out, void *stream) {
+    if (heads == 0) return FOCR_OK;
+    if (!q || !out || !state || !ring_k || !ring_v || (prefill_len && (!ref_k || !ref_v)))
+        return fail(FOCR_E_ARG, "attention_decode_at: null pointer");
+    if (head_dim == 0 || head_dim % 4 || head_dim > ATT_THREADS)
+        return fail(FOCR_E_UNSUPPORTED, "attention_decode_at: head_dim must be a multiple of 4 <= 256");
+    if (prefill_len > ref_stride || prefill_len + ring_stride > (size_t)ATT_MAX_KEYS || heads > 65535)
+        return fail(FOCR_E_UNSUPPORTED, "attention_decode_at: more than 16384 keys or 65535 heads");
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t smem = (head_dim + 3 * (prefill_len + ring_stride) + ATT_THREADS) * sizeof(float);
+    static bool attr = false;
+    if (!attr) {
+        FOCR_CUDA_TRY(cudaFuncSetAttribute(attention_decode_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)((256 + 3 * ATT_MAX_KEYS + ATT_THREADS) * 4)));
+        attr = true;
+    }
+    attention_decode_kernel<<<(unsigned)heads, ATT_THREADS, smem, st>>>(
+        q, ref_k, ref_v, (int)prefill_len, (int)ref_stride, ring_k, ring_v, 0, (int)ring_stride,
+        (int)head_dim, out, state + FOCR_STATE_RING_LEN);
+    FOCR_CUDA_TRY(cudaGetLastError());
     return FOCR_OK;
 }
 

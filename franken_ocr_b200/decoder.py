@@ -274,3 +274,93 @@ class DecoderI8:
                 break
             h = self.decode_step(self.embed[tok:tok + 1], seq + i)
         return out
+
+    # -- graph-replayed greedy decode ---------------------------------------------
+    def _step_dev(self):
+        """One decode step driven by the device state: prologue (record the
+        previous token, advance position and ring cursor, gather the
+        embedding), every layer, final norm and lm-head argmax into
+        ``self._tok``.  Capturable: no host-varying argument."""
+        from ._lib import STATE_WORDS  # noqa: F401  (layout documented there)
+
+        st = self._stream()
+        D = self.dim
+        check(lib.focr_decode_prologue(_p(self._state), _p(self._tok), _p(self.embed), self.vocab,
+                                       self.hidden, RING_WINDOW, _p(self._tokens),
+                                       self._tokens.numel(), _p(self._x), st))
+        x = self._x
+        for d in self.layers:
+            normed = self._norm(x, d["input_ln"])
+            qkv = self._linear(normed, d["qkv_w"], d["qkv_s"], False)
+            check(lib.focr_rope_apply_at(_p(qkv), 2 * D, HEAD_DIM, _p(self._cos), _p(self._sin),
+                                         _p(self._state), st))
+            k = qkv[0, D:2 * D]
+            v = qkv[0, 2 * D:]
+            check(lib.focr_ring_write(_p(k), _p(v), self.heads, HEAD_DIM, _p(d["ring_k"]),
+                                      _p(d["ring_v"]), RING_WINDOW, _p(self._state), st))
+            ctx = self._empty(1, D)
+            check(lib.focr_attention_decode_at(
+                _p(qkv), _p(d["ref_k"]), _p(d["ref_v"]), self.prefill_len, self.max_prefill,
+                _p(d["ring_k"]), _p(d["ring_v"]), RING_WINDOW, self.heads, HEAD_DIM,
+                _p(self._state), _p(ctx), st))
+            h = self._add(x, self._linear(ctx, d["o_w"], d["o_s"], False))
+            normed2 = self._norm(h, d["post_ln"])
+            if "moe" in d:
+                mlp, _, _ = d["moe"].decode(normed2)
+            else:
+                mlp = self._dense(d, normed2, False)
+            x = self._add(h, mlp)
+        self._head_top1(x)
+
+    def _head_top1(self, row):
+        normed = self._norm(row, self.final_norm)
+        check(lib.focr_lmhead_top1(self.head._h, _p(normed), 1, _p(self._bv), _p(self._tok), None,
+                                   MEM_DEVICE, self._stream()))
+
+    def generate_graph(self, embeds, n_tokens: int, use_graph: bool = True) -> np.ndarray:
+        """:meth:`generate` with the decode loop on the device: the step is
+        captured once in a CUDA graph and replayed per token; tokens are
+        recorded on the device and read back once at the end."""
+        torch = self._torch
+        from ._lib import STATE_NEXT_POS, STATE_WORDS
+
+        seq = embeds.shape[0]
+        key = (seq, n_tokens)
+        if getattr(self, "_graph_key", None) != key:
+            # buffers the captured step points at: fixed for a (seq, n_tokens)
+            c, s = rope_table(np.arange(seq + n_tokens))
+            self._cos, self._sin = torch.from_numpy(c).to(self.dev), torch.from_numpy(s).to(self.dev)
+            self._state = torch.zeros(STATE_WORDS, dtype=torch.int32, device=self.dev)
+            self._tok = torch.zeros(1, dtype=torch.int32, device=self.dev)
+            self._bv = torch.zeros(1, dtype=torch.float32, device=self.dev)
+            self._x = self._empty(1, self.hidden)
+            self._tokens = torch.zeros(n_tokens, dtype=torch.int32, device=self.dev)
+            self._graph, self._graph_key = None, key
+        st0 = np.zeros(STATE_WORDS, np.int32)
+        st0[STATE_NEXT_POS] = seq
+        self._state.copy_(torch.from_numpy(st0))
+        h = self.prefill(embeds)
+        self._head_top1(h[-1:])
+        steps = n_tokens - 1
+        if steps > 0:
+            self._step_dev()  # eager: first step, and one-time kernel attributes
+        if steps > 1:
+            if use_graph:
+                g = self._graph
+                if g is None:
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g):
+                        self._step_dev()
+                    self._graph = g
+                for _ in range(steps - 1):
+                    g.replay()
+            else:
+                for _ in range(steps - 1):
+                    self._step_dev()
+        self._tokens[n_tokens - 1:].copy_(self._tok)
+        out = self._tokens.cpu().numpy().astype(np.int64)
+        st = self._state.cpu().numpy()
+        if st[6]:
+            raise RuntimeError("decode: token id outside the embedding table")
+        self.ring_len, self.ring_pos = int(st[1]), int(st[2])
+        return out

@@ -280,6 +280,45 @@ int focr_attention_prefill(const float *q, const float *k, const float *v, size_
 int focr_rope_table(const size_t *positions, size_t n, size_t head_dim, float theta,
                     float *cos_t, float *sin_t);
 
+/* ---- device-state decode step ------------------------------------------
+ * The calls below read a step's varying values (position, ring cursor) from
+ * an int32 state array in device memory instead of taking them as
+ * arguments, so that a whole decode step -- prologue, every layer, lm-head
+ * -- can be captured once in a CUDA graph and replayed per token.  All
+ * pointers are device memory; work is enqueued on `stream`. */
+#define FOCR_STATE_POS 0      /* position of the current step */
+#define FOCR_STATE_RING_LEN 1 /* RingCache::ring_len after this step's write */
+#define FOCR_STATE_RING_POS 2 /* RingCache::ring_pos after this step's write */
+#define FOCR_STATE_SLOT 3     /* ring slot this step writes */
+#define FOCR_STATE_NEXT_POS 4 /* position of the next step */
+#define FOCR_STATE_STEP 5     /* tokens recorded so far */
+#define FOCR_STATE_ERROR 6    /* set to 1 when a token id is out of range */
+#define FOCR_STATE_WORDS 8
+
+/* Start a decode step: record *token (the previous argmax) in
+ * tokens_out[step] (when tokens_out is non-NULL and step < max_tokens),
+ * advance position and ring cursor (rswa.rs:467-493), and copy the token's
+ * embedding row (embed [vocab][hidden] f32) into x [hidden]. */
+int focr_decode_prologue(int32_t *state, const int32_t *token, const float *embed, size_t vocab,
+                         size_t hidden, size_t ring_window, int32_t *tokens_out,
+                         size_t max_tokens, float *x, void *stream);
+
+/* RoPE on one row x [cols] at the position state[FOCR_STATE_POS], reading
+ * row `position` of full cos/sin tables [positions][head_dim]. */
+int focr_rope_apply_at(float *x, size_t cols, size_t head_dim, const float *cos_table,
+                       const float *sin_table, const int32_t *state, void *stream);
+
+/* RingCache::write_decode_step's copy: k, v [heads][head_dim] into ring
+ * slot state[FOCR_STATE_SLOT] of ring_k/ring_v [heads][ring_stride][head_dim]. */
+int focr_ring_write(const float *k, const float *v, size_t heads, size_t head_dim, float *ring_k,
+                    float *ring_v, size_t ring_stride, const int32_t *state, void *stream);
+
+/* focr_attention_decode with ring_len = state[FOCR_STATE_RING_LEN]. */
+int focr_attention_decode_at(const float *q, const float *ref_k, const float *ref_v,
+                             size_t prefill_len, size_t ref_stride, const float *ring_k,
+                             const float *ring_v, size_t ring_stride, size_t heads,
+                             size_t head_dim, const int32_t *state, float *out, void *stream);
+
 /* ---- device event trace (GPU counterpart of FOCR_PROFILE_DECODE,
  * native_engine/decoder.rs:986-1024) ------------------------------------
  * Register a device buffer of `capacity` 16-byte events {u32 tag, u32 phase,

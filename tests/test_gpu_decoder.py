@@ -119,3 +119,26 @@ def test_full_dims_decoder_greedy_tokens(cuda, oracle):
     got, want, errs = _run_decoder(oracle, W, 64, 8, 12)
     assert np.array_equal(got, want)
     assert max(errs) < 1e-3, max(errs)
+
+
+def test_graph_greedy_decode_matches_oracle(cuda, oracle):
+    """The device-state decode step replayed from one CUDA graph gives the
+    oracle's tokens through a ring wrap, and equals the eager loop; a second
+    call reuses the captured graph."""
+    import torch
+
+    from franken_ocr_b200 import synth
+    from franken_ocr_b200.decoder import DecoderI8
+
+    W = synth.decoder_model(11, layers=3, n_experts=8, dense_inter=512, vocab=2048)
+    e = synth.prompt_embeds(11, 40, W.hidden)
+    want = oracle.DecoderOracle(W).generate(e, 140)
+    D = DecoderI8(W, max_prefill=40)
+    de = torch.from_numpy(e).cuda()
+    got = D.generate_graph(de, 140)
+    assert np.array_equal(got, want), np.nonzero(got != want)[0][:5]
+    assert (D.ring_len, D.ring_pos) == (128, 139 % 128)
+    assert np.array_equal(D.generate_graph(de, 140), want)
+    assert np.array_equal(D.generate_graph(de, 140, use_graph=False), want)
+    assert np.array_equal(D.generate(de, 140), want)
+    D.close()
