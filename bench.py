@@ -572,7 +572,7 @@ def config3(args, dev, prefill=1024, n_tokens=256, seed=3):
         ev[2].record()
         torch.cuda.synchronize()
         p_ms = ev[0].elapsed_time(ev[1])
-        return list(toks), p_ms, ev[1].elapsed_time(ev[2]) - p_ms
+        return [int(t) for t in toks], p_ms, ev[1].elapsed_time(ev[2]) - p_ms
 
     for _ in range(max(1, args.warmup)):
         toks0, _, _ = run()
