@@ -559,8 +559,8 @@ def cpu_baseline_config3(W, seed, prefill=32, steps=3):
 
     D = O.DecoderOracle(W)
     h = D.prefill(synth.prompt_embeds(seed, prefill))
-    t0 = time.perf_counter()
     tok = O.argmax_row(D.lm_head(h[-1]))
+    t0 = time.perf_counter()
     for i in range(steps):
         h = D.decode_step(W.embed[tok], prefill + i)
         tok = O.argmax_row(D.lm_head(h[-1]))
