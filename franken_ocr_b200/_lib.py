@@ -32,7 +32,7 @@ EXPORTS = [
     "focr_top1_combine", "focr_selftest", "focr_trace_set", "focr_rms_norm", "focr_rope_apply",
     "focr_attention_decode", "focr_linear_i8", "focr_swiglu", "focr_add",
     "focr_attention_prefill", "focr_rope_table", "focr_decode_prologue", "focr_rope_apply_at",
-    "focr_ring_write", "focr_attention_decode_at",
+    "focr_ring_write", "focr_attention_decode_at", "focr_add_rms_norm",
 ]
 
 
@@ -107,6 +107,7 @@ lib.focr_rope_table.argtypes = [vp, sz, sz, C.c_float, vp, vp]
 lib.focr_decode_prologue.argtypes = [vp, vp, vp, sz, sz, sz, vp, sz, vp, vp]
 lib.focr_rope_apply_at.argtypes = [vp, sz, sz, vp, vp, vp, vp]
 lib.focr_ring_write.argtypes = [vp, vp, sz, sz, vp, vp, sz, vp, vp]
+lib.focr_add_rms_norm.argtypes = [vp, vp, sz, sz, vp, C.c_float, vp, vp, vp]
 lib.focr_attention_decode_at.argtypes = [vp, vp, vp, sz, sz, vp, vp, sz, sz, sz, vp, vp, vp]
 STATE_POS, STATE_RING_LEN, STATE_RING_POS, STATE_SLOT, STATE_NEXT_POS, STATE_STEP = range(6)
 STATE_ERROR, STATE_WORDS = 6, 8

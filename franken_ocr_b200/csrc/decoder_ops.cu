@@ -20,13 +20,80 @@
 
 namespace focr {
 
-// One warp per row.
+// One warp per row.  The sum of squares runs in the oracle's order: lane l
+// accumulates the 4-element chunks l, l + 32, l + 64, ... (elements in order
+// within a chunk), then an xor butterfly.  Rows of up to 2048 floats with
+// 16-byte alignment are loaded once as float4s into registers, so the loads
+// are all in flight together.  With `add` set the row is first formed as
+// x + add (the residual add, decoder.rs:529) and written to h.
 __global__ void rms_norm_kernel(const float *__restrict__ x, int rows, int cols,
-                                const float *__restrict__ w, float eps, float *__restrict__ y) {
+                                const float *__restrict__ w, float eps, float *__restrict__ y,
+                                const float *__restrict__ add = nullptr,
+                                float *__restrict__ h = nullptr) {
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= rows) return;
     const float *xr = x + (size_t)row * cols;
+    float *yr = y + (size_t)row * cols;
+    const float *ar = add ? add + (size_t)row * cols : nullptr;
+    float *hr = h ? h + (size_t)row * cols : nullptr;
+    const bool vec = cols % 4 == 0 && cols <= 2048 &&
+                     (((uintptr_t)xr | (uintptr_t)yr | (uintptr_t)w | (uintptr_t)ar |
+                       (uintptr_t)hr) % 16) == 0;
+    if (vec) {
+        const int nc = cols / 4;
+        const float4 *x4 = reinterpret_cast<const float4 *>(xr);
+        float4 v[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            const int c = lane + 32 * i;
+            if (c < nc) {
+                v[i] = x4[c];
+                if (ar) {
+                    const float4 a = reinterpret_cast<const float4 *>(ar)[c];
+                    v[i] = make_float4(__fadd_rn(v[i].x, a.x), __fadd_rn(v[i].y, a.y),
+                                       __fadd_rn(v[i].z, a.z), __fadd_rn(v[i].w, a.w));
+                    reinterpret_cast<float4 *>(hr)[c] = v[i];
+                }
+            }
+        }
+        float s = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            if (lane + 32 * i < nc) {
+                s = __fadd_rn(s, __fmul_rn(v[i].x, v[i].x));
+                s = __fadd_rn(s, __fmul_rn(v[i].y, v[i].y));
+                s = __fadd_rn(s, __fmul_rn(v[i].z, v[i].z));
+                s = __fadd_rn(s, __fmul_rn(v[i].w, v[i].w));
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+        const float ms = __fdiv_rn(s, (float)cols);
+        const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+        const float4 *w4 = reinterpret_cast<const float4 *>(w);
+        float4 *y4 = reinterpret_cast<float4 *>(yr);
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            const int c = lane + 32 * i;
+            if (c < nc) {
+                float4 o = make_float4(__fmul_rn(v[i].x, r), __fmul_rn(v[i].y, r),
+                                       __fmul_rn(v[i].z, r), __fmul_rn(v[i].w, r));
+                if (w) {
+                    const float4 ww = w4[c];
+                    o = make_float4(__fmul_rn(o.x, ww.x), __fmul_rn(o.y, ww.y),
+                                    __fmul_rn(o.z, ww.z), __fmul_rn(o.w, ww.w));
+                }
+                y4[c] = o;
+            }
+        }
+        return;
+    }
+    if (ar) {
+        for (int k = lane; k < cols; k += 32) hr[k] = __fadd_rn(xr[k], ar[k]);
+        __syncwarp();
+        xr = hr;
+    }
     float s = 0.0f;
     for (int c = lane; 4 * c < cols; c += 32)
         for (int k = 4 * c; k < 4 * c + 4 && k < cols; k++) s = __fadd_rn(s, __fmul_rn(xr[k], xr[k]));
@@ -34,14 +101,12 @@ __global__ void rms_norm_kernel(const float *__restrict__ x, int rows, int cols,
     for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
     const float ms = __fdiv_rn(s, (float)cols);
     const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
-    float *yr = y + (size_t)row * cols;
     for (int k = lane; k < cols; k += 32) {
         const float v = __fmul_rn(xr[k], r);
         yr[k] = w ? __fmul_rn(v, w[k]) : v;
     }
 }
 
-// One thread per (row, head, i < half).
 // With pos_dev set (one row), the table row is the decode position read
 // from device memory, so a captured decode step replays at any position.
 __global__ void rope_kernel(float *__restrict__ x, int seq, int cols, int head_dim,
@@ -67,34 +132,66 @@ __global__ void rope_kernel(float *__restrict__ x, int seq, int cols, int head_d
 
 constexpr int ATT_THREADS = 256;
 constexpr int ATT_MAX_KEYS = 16384;
+constexpr int ATT_DG = 32;      // dimensions per CTA (one fold warp, a lane per dimension)
+constexpr int ATT_CH = 64;      // keys per staged V chunk
+constexpr int ATT_STAGES = 4;   // V chunks in flight
 
-// One CTA per head; bit-identical to the reference's per-key online fold
-// (rswa.rs:894-944 with fold at :1163-1182):
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Decode attention bit-identical to the reference's per-key online fold
+// (rswa.rs:894-944, fold at :1163-1182).  Grid = (heads, head_dim / 32):
+// every CTA of a head computes the same scores and exponentials, and folds
+// its own 32 dimensions:
 //   1. every key's score (the reference's sequential dot) in parallel;
 //   2. the running max as a prefix scan (m_r = s_r > m_{r-1} ? s_r : m_{r-1},
 //      which skips NaN as the reference's `score > run_max` does);
 //   3. per key, in parallel, the fold's two exponentials: the correction
-//      c_r = exp(m_{r-1} - s_r) (0 while m_{r-1} is -inf, exactly 1 when the
-//      max did not move -- multiplying by 1 is exact, so it stands in for the
-//      skipped branch) and the weight w_r = exp(s_r - m_r);
-//   4. the serial part, den = den * c_r + w_r and acc[d] = acc[d] * c_r +
-//      w_r * v_r[d] in key order, with thread d owning dimension d.
-// Shared memory: q [head_dim] | scores/max [total] | corr [total] | w [total]
-// | chunk maxima [ATT_THREADS].
+//      c_r = exp(m_{r-1} - s_r) (0 while m_{r-1} is -inf; exactly 1 when the
+//      max did not move, and then the multiply is skipped -- x * 1 == x, so
+//      that is the reference's untaken branch) and the weight
+//      w_r = exp(s_r - m_r);
+//   4. the serial recurrence den = den * c_r + w_r, acc[d] = acc[d] * c_r +
+//      w_r * v_r[d] in key order, one lane per dimension, fed from a ring of
+//      V chunks that all warps stage with cp.async.
+// Shared memory: q [head_dim] | corr [total] | scores, then weights [total] |
+// chunk maxima [ATT_THREADS] | V stages [ATT_STAGES][ATT_CH][ATT_DG].
 __global__ void __launch_bounds__(ATT_THREADS) attention_decode_kernel(
     const float *__restrict__ q, const float *__restrict__ ref_k, const float *__restrict__ ref_v,
     int prefill_len, int ref_stride, const float *__restrict__ ring_k,
     const float *__restrict__ ring_v, int ring_len, int ring_stride, int head_dim,
     float *__restrict__ out, const int *__restrict__ ring_len_dev = nullptr) {
-    extern __shared__ float att_sm[];
-    const int h = blockIdx.x, tid = threadIdx.x;
+    extern __shared__ __align__(16) float att_sm[];
+    const int h = blockIdx.x, g = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (ring_len_dev) ring_len = *ring_len_dev;
     const int total = prefill_len + ring_len;
-    float *sq = att_sm;            // [head_dim]
-    float *ss = sq + head_dim;     // [total] scores
-    float *sc = ss + total;        // [total] corrections
-    float *sw = sc + total;        // [total] weights
-    float *cm = sw + total;        // [ATT_THREADS] chunk maxima
+    float *sv = att_sm;                                   // [STAGES][CH][DG]
+    float *sq = sv + ATT_STAGES * ATT_CH * ATT_DG;        // [head_dim]
+    float *cm = sq + head_dim;                            // [ATT_THREADS]
+    float *sc = cm + ATT_THREADS;                         // [total]
+    float *sw = sc + total;                               // [total]
+    auto vrow = [&](int r) -> const float * {
+        return r < prefill_len ? ref_v + ((size_t)h * ref_stride + r) * head_dim
+                               : ring_v + ((size_t)h * ring_stride + (r - prefill_len)) * head_dim;
+    };
+    const int nch = (total + ATT_CH - 1) / ATT_CH;
+    // stage V chunk c into buffer c % STAGES: ATT_CH rows x 8 16-byte pieces
+    auto stage = [&](int c) {
+        float *dst = sv + (c % ATT_STAGES) * ATT_CH * ATT_DG;
+        for (int i = tid; i < ATT_CH * (ATT_DG / 4); i += ATT_THREADS) {
+            const int kr = i / (ATT_DG / 4), pc = i % (ATT_DG / 4), r = c * ATT_CH + kr;
+            if (r < total) cp_async16(dst + kr * ATT_DG + 4 * pc, vrow(r) + g * ATT_DG + 4 * pc);
+        }
+    };
+    for (int c = 0; c < ATT_STAGES - 1; c++) {
+        if (c < nch) stage(c);
+        cp_async_commit();
+    }
     for (int i = tid; i < head_dim; i += ATT_THREADS) sq[i] = q[(size_t)h * head_dim + i];
     __syncthreads();
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)head_dim));
@@ -110,14 +207,14 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_decode_kernel(
             d = __fadd_rn(d, __fmul_rn(sq[i + 2], k4.z));
             d = __fadd_rn(d, __fmul_rn(sq[i + 3], k4.w));
         }
-        ss[r] = __fmul_rn(d, scale);
+        sw[r] = __fmul_rn(d, scale);
     }
     __syncthreads();
     // prefix max: contiguous chunks per thread, then the chunk maxima in order
     const int per = (total + ATT_THREADS - 1) / ATT_THREADS;
-    const int c0 = tid * per, c1 = min(c0 + per, total);
+    const int c0 = min(tid * per, total), c1 = min(c0 + per, total);
     float m = -INFINITY;
-    for (int r = c0; r < c1; r++) m = ss[r] > m ? ss[r] : m;
+    for (int r = c0; r < c1; r++) m = sw[r] > m ? sw[r] : m;
     cm[tid] = m;
     __syncthreads();
     if (tid == 0) {
@@ -131,7 +228,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_decode_kernel(
     __syncthreads();
     m = cm[tid];
     for (int r = c0; r < c1; r++) {
-        const float s = ss[r];
+        const float s = sw[r];
         float c = 1.0f;
         if (s > m) {
             c = m == -INFINITY ? 0.0f : dexpf(__fsub_rn(m, s));
@@ -140,27 +237,42 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_decode_kernel(
         sc[r] = c;
         sw[r] = dexpf(__fsub_rn(s, m));
     }
-    __syncthreads();
-    float den = 0.0f;
-    if (tid < head_dim) {
-        float acc = 0.0f;
-        int r = 0;
-        for (; r < prefill_len; r++) {
-            const float c = sc[r], w = sw[r];
-            const float v = ref_v[((size_t)h * ref_stride + r) * head_dim + tid];
-            acc = __fadd_rn(__fmul_rn(acc, c), __fmul_rn(w, v));
-            den = __fadd_rn(__fmul_rn(den, c), w);
+    float acc = 0.0f, den = 0.0f;
+    for (int c = 0; c < nch; c++) {
+        if (c + ATT_STAGES - 1 < nch) stage(c + ATT_STAGES - 1);
+        cp_async_commit();
+        cp_async_wait<ATT_STAGES - 1>();
+        __syncthreads();
+        if (warp == 0) {
+            const float *buf = sv + (c % ATT_STAGES) * ATT_CH * ATT_DG + lane;
+            const int r0 = c * ATT_CH, r1 = min(r0 + ATT_CH, total);
+            for (int r = r0; r < r1; r++) {
+                const float cr = sc[r], w = sw[r];
+                const float wv = __fmul_rn(w, buf[(r - r0) * ATT_DG]);
+                if (cr == 1.0f) {
+                    acc = __fadd_rn(acc, wv);
+                    den = __fadd_rn(den, w);
+                } else {
+                    acc = __fadd_rn(__fmul_rn(acc, cr), wv);
+                    den = __fadd_rn(__fmul_rn(den, cr), w);
+                }
+            }
         }
-        for (; r < total; r++) {
-            const float c = sc[r], w = sw[r];
-            const float v = ring_v[((size_t)h * ring_stride + (r - prefill_len)) * head_dim + tid];
-            acc = __fadd_rn(__fmul_rn(acc, c), __fmul_rn(w, v));
-            den = __fadd_rn(__fmul_rn(den, c), w);
-        }
+        __syncthreads();
+    }
+    cp_async_wait<0>();
+    if (warp == 0) {
         const float inv = den > 0.0f ? __fdiv_rn(1.0f, den) : 0.0f;
-        out[(size_t)h * head_dim + tid] = __fmul_rn(acc, inv);
+        out[(size_t)h * head_dim + g * ATT_DG + lane] = __fmul_rn(acc, inv);
     }
 }
+
+static size_t att_smem(size_t head_dim, size_t total) {
+    return ((size_t)ATT_STAGES * ATT_CH * ATT_DG + head_dim + ATT_THREADS + 2 * total) *
+           sizeof(float);
+}
+static const size_t ATT_SMEM_MAX = ((size_t)ATT_STAGES * ATT_CH * ATT_DG + 256 + ATT_THREADS +
+                                    2 * (size_t)ATT_MAX_KEYS) * sizeof(float);
 
 }  // namespace focr
 
@@ -255,20 +367,20 @@ int focr_attention_decode(const float *q, const float *ref_k, const float *ref_v
         return fail(FOCR_E_ARG, "rswa: empty attention key set (prefill_len=0, ring_len=0)");
     if (!q || !out || (prefill_len && (!ref_k || !ref_v)) || (ring_len && (!ring_k || !ring_v)))
         return fail(FOCR_E_ARG, "attention_decode: null pointer");
-    if (head_dim == 0 || head_dim % 4 || head_dim > ATT_THREADS || ATT_THREADS % head_dim)
-        return fail(FOCR_E_UNSUPPORTED, "attention_decode: head_dim must divide 256 and be a multiple of 4");
+    if (head_dim == 0 || head_dim % ATT_DG || head_dim > 256)
+        return fail(FOCR_E_UNSUPPORTED, "attention_decode: head_dim must be a multiple of 32, at most 256");
     if (prefill_len > ref_stride || ring_len > ring_stride)
         return fail(FOCR_E_SHAPE, "attention_decode: rows exceed the cache stride");
     if (prefill_len + ring_len > (size_t)ATT_MAX_KEYS || heads > 65535)
         return fail(FOCR_E_UNSUPPORTED, "attention_decode: more than 16384 keys or 65535 heads");
     cudaStream_t st = (cudaStream_t)stream;
     const size_t total = prefill_len + ring_len;
-    const size_t smem = (head_dim + 3 * total + ATT_THREADS) * sizeof(float);
+    const size_t smem = att_smem(head_dim, total);
     static bool attr = false;
     if (!attr) {
         FOCR_CUDA_TRY(cudaFuncSetAttribute(attention_decode_kernel,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)((256 + 3 * ATT_MAX_KEYS + ATT_THREADS) * 4)));
+                                           (int)ATT_SMEM_MAX));
         attr = true;
     }
     const float *dq = q, *drk = ref_k, *drv = ref_v, *dgk = ring_k, *dgv = ring_v;
@@ -293,7 +405,8 @@ int focr_attention_decode(const float *q, const float *ref_k, const float *ref_v
     } else if (mem != FOCR_MEM_DEVICE) {
         return fail(FOCR_E_ARG, "bad mem kind");
     }
-    attention_decode_kernel<<<(unsigned)heads, ATT_THREADS, smem, st>>>(
+    attention_decode_kernel<<<dim3((unsigned)heads, (unsigned)(head_dim / ATT_DG)), ATT_THREADS,
+                              smem, st>>>(
         dq, drk, drv, (int)prefill_len, (int)ref_stride, dgk, dgv, (int)ring_len, (int)ring_stride,
         (int)head_dim, dout);
     FOCR_CUDA_TRY(cudaGetLastError());
@@ -326,22 +439,36 @@ int focr_attention_decode_at(const float *q, const float *ref_k, const float *re
     if (heads == 0) return FOCR_OK;
     if (!q || !out || !state || !ring_k || !ring_v || (prefill_len && (!ref_k || !ref_v)))
         return fail(FOCR_E_ARG, "attention_decode_at: null pointer");
-    if (head_dim == 0 || head_dim % 4 || head_dim > ATT_THREADS)
-        return fail(FOCR_E_UNSUPPORTED, "attention_decode_at: head_dim must be a multiple of 4 <= 256");
+    if (head_dim == 0 || head_dim % ATT_DG || head_dim > 256)
+        return fail(FOCR_E_UNSUPPORTED, "attention_decode_at: head_dim must be a multiple of 32, at most 256");
     if (prefill_len > ref_stride || prefill_len + ring_stride > (size_t)ATT_MAX_KEYS || heads > 65535)
         return fail(FOCR_E_UNSUPPORTED, "attention_decode_at: more than 16384 keys or 65535 heads");
     cudaStream_t st = (cudaStream_t)stream;
-    const size_t smem = (head_dim + 3 * (prefill_len + ring_stride) + ATT_THREADS) * sizeof(float);
+    const size_t smem = att_smem(head_dim, prefill_len + ring_stride);
     static bool attr = false;
     if (!attr) {
         FOCR_CUDA_TRY(cudaFuncSetAttribute(attention_decode_kernel,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)((256 + 3 * ATT_MAX_KEYS + ATT_THREADS) * 4)));
+                                           (int)ATT_SMEM_MAX));
         attr = true;
     }
-    attention_decode_kernel<<<(unsigned)heads, ATT_THREADS, smem, st>>>(
+    attention_decode_kernel<<<dim3((unsigned)heads, (unsigned)(head_dim / ATT_DG)), ATT_THREADS,
+                              smem, st>>>(
         q, ref_k, ref_v, (int)prefill_len, (int)ref_stride, ring_k, ring_v, 0, (int)ring_stride,
         (int)head_dim, out, state + FOCR_STATE_RING_LEN);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    return FOCR_OK;
+}
+
+
+int focr_add_rms_norm(const float *a, const float *b, size_t rows, size_t cols,
+                      const float *weight, float eps, float *h, float *y, void *stream) {
+    if (rows == 0 || cols == 0) return FOCR_OK;
+    if (!a || !b || !h || !y) return fail(FOCR_E_ARG, "add_rms_norm: null pointer");
+    if (rows > (size_t)INT32_MAX || cols > (size_t)INT32_MAX)
+        return fail(FOCR_E_UNSUPPORTED, "add_rms_norm: dimension exceeds int32 range");
+    rms_norm_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
+        a, (int)rows, (int)cols, weight, eps, y, b, h);
     FOCR_CUDA_TRY(cudaGetLastError());
     return FOCR_OK;
 }

@@ -161,6 +161,14 @@ class DecoderI8:
                                  int(te), _p(y), MEM_DEVICE, self._stream()))
         return y
 
+    def _add_norm(self, a, b, w):
+        """(a + b, rms_norm(a + b) * w) in one kernel."""
+        h = self._empty(*a.shape)
+        y = self._empty(*a.shape)
+        check(lib.focr_add_rms_norm(_p(a), _p(b), a.shape[0], a.shape[1], _p(w), RMS_NORM_EPS,
+                                    _p(h), _p(y), self._stream()))
+        return h, y
+
     def _add(self, a, b):
         y = self._empty(*a.shape)
         check(lib.focr_add(_p(a), _p(b), a.numel(), _p(y), MEM_DEVICE, self._stream()))
@@ -188,8 +196,12 @@ class DecoderI8:
         c, s = rope_table(np.arange(seq))
         cos_t, sin_t = torch.from_numpy(c).to(self.dev), torch.from_numpy(s).to(self.dev)
         x = embeds.contiguous()
+        mlp = None
         for d in self.layers:
-            normed = self._norm(x, d["input_ln"])
+            if mlp is None:
+                normed = self._norm(x, d["input_ln"])
+            else:  # x = h + mlp of the previous layer, fused with this norm
+                x, normed = self._add_norm(h, mlp, d["input_ln"])
             q = self._linear(normed, d["q_w"], d["q_s"], True)
             k = self._linear(normed, d["k_w"], d["k_s"], True)
             v = self._linear(normed, d["v_w"], d["v_s"], True)
@@ -200,13 +212,13 @@ class DecoderI8:
             ctx = self._empty(seq, self.dim)
             check(lib.focr_attention_prefill(_p(q), _p(k), _p(v), seq, self.heads, HEAD_DIM,
                                              _p(ctx), MEM_DEVICE, self._stream()))
-            h = self._add(x, self._linear(ctx, d["o_w"], d["o_s"], True))
-            normed2 = self._norm(h, d["post_ln"])
+            h, normed2 = self._add_norm(x, self._linear(ctx, d["o_w"], d["o_s"], True),
+                                        d["post_ln"])
             if "moe" in d:
                 mlp, _, _ = d["moe"].prefill(normed2)
             else:
                 mlp = self._dense(d, normed2, True)
-            x = self._add(h, mlp)
+        x = self._add(h, mlp)
         self.prefill_len = seq
         self.ring_len = 0
         self.ring_pos = 0
@@ -234,8 +246,12 @@ class DecoderI8:
         slot = self._ring_slot()
         D = self.dim
         x = token_embed.contiguous()
+        mlp = None
         for d in self.layers:
-            normed = self._norm(x, d["input_ln"])
+            if mlp is None:
+                normed = self._norm(x, d["input_ln"])
+            else:
+                x, normed = self._add_norm(h, mlp, d["input_ln"])
             qkv = self._linear(normed, d["qkv_w"], d["qkv_s"], False)
             self._rope(qkv, cos_t, sin_t, cols=2 * D)  # q and k: one row, 2 * heads heads
             d["ring_k"][:, slot].copy_(qkv[0, D:2 * D].view(self.heads, HEAD_DIM))
@@ -245,14 +261,13 @@ class DecoderI8:
                 _p(qkv), _p(d["ref_k"]), _p(d["ref_v"]), self.prefill_len, self.max_prefill,
                 _p(d["ring_k"]), _p(d["ring_v"]), self.ring_len, RING_WINDOW, self.heads,
                 HEAD_DIM, _p(ctx), MEM_DEVICE, self._stream()))
-            h = self._add(x, self._linear(ctx, d["o_w"], d["o_s"], False))
-            normed2 = self._norm(h, d["post_ln"])
+            h, normed2 = self._add_norm(x, self._linear(ctx, d["o_w"], d["o_s"], False),
+                                        d["post_ln"])
             if "moe" in d:
                 mlp, _, _ = d["moe"].decode(normed2)
             else:
                 mlp = self._dense(d, normed2, False)
-            x = self._add(h, mlp)
-        return x
+        return self._add(h, mlp)
 
     def lm_head_top1(self, hidden_row):
         """``lm_head_cached_i8`` + ``argmax_row`` on a ``[1, hidden]`` row ->
@@ -289,8 +304,12 @@ class DecoderI8:
                                        self.hidden, RING_WINDOW, _p(self._tokens),
                                        self._tokens.numel(), _p(self._x), st))
         x = self._x
+        mlp = None
         for d in self.layers:
-            normed = self._norm(x, d["input_ln"])
+            if mlp is None:
+                normed = self._norm(x, d["input_ln"])
+            else:
+                x, normed = self._add_norm(h, mlp, d["input_ln"])
             qkv = self._linear(normed, d["qkv_w"], d["qkv_s"], False)
             check(lib.focr_rope_apply_at(_p(qkv), 2 * D, HEAD_DIM, _p(self._cos), _p(self._sin),
                                          _p(self._state), st))
@@ -303,14 +322,15 @@ class DecoderI8:
                 _p(qkv), _p(d["ref_k"]), _p(d["ref_v"]), self.prefill_len, self.max_prefill,
                 _p(d["ring_k"]), _p(d["ring_v"]), RING_WINDOW, self.heads, HEAD_DIM,
                 _p(self._state), _p(ctx), st))
-            h = self._add(x, self._linear(ctx, d["o_w"], d["o_s"], False))
-            normed2 = self._norm(h, d["post_ln"])
+            h, normed2 = self._add_norm(x, self._linear(ctx, d["o_w"], d["o_s"], False),
+                                        d["post_ln"])
             if "moe" in d:
                 mlp, _, _ = d["moe"].decode(normed2)
             else:
                 mlp = self._dense(d, normed2, False)
-            x = self._add(h, mlp)
-        self._head_top1(x)
+        _, normed = self._add_norm(h, mlp, self.final_norm)
+        check(lib.focr_lmhead_top1(self.head._h, _p(normed), 1, _p(self._bv), _p(self._tok), None,
+                                   MEM_DEVICE, st))
 
     def _head_top1(self, row):
         normed = self._norm(row, self.final_norm)

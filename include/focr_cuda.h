@@ -232,6 +232,12 @@ int focr_top1_combine(const float *vals, const int32_t *idx, size_t shards,
 int focr_rms_norm(const float *x, size_t rows, size_t cols, const float *weight, float eps,
                   float *y, int mem, void *stream);
 
+/* h = a + b (add_residual, decoder.rs:529), then y = rms_norm(h) as
+ * focr_rms_norm -- the residual add fused into the norm that follows it in
+ * the layer loop (decoder.rs:2626-2636).  Device pointers. */
+int focr_add_rms_norm(const float *a, const float *b, size_t rows, size_t cols,
+                      const float *weight, float eps, float *h, float *y, void *stream);
+
 /* NEOX RoPE in place -- replaces apply_rope (native_engine/decoder.rs:229-272)
  * for x [seq][cols], cols a multiple of head_dim, with the RopeTable cos/sin
  * [seq][head_dim] built by the caller (decoder.rs:171-213). */
