@@ -214,12 +214,15 @@ int focr_gemv_i8(const float *x, size_t m, size_t k, const int8_t *w, const floa
         dws = (const float *)bs.p;
         dy = (float *)by.p;
     }
-    FOCR_CUDA_TRY(bq.alloc(m * k, st));
-    FOCR_CUDA_TRY(bas.alloc(m * 4, st));
-    int rc = launch_quantize_rows(dx, m, k, false, (int8_t *)bq.p, (float *)bas.p, st);
-    if (rc) return rc;
-    rc = launch_gemv_dequant((const int8_t *)bq.p, (const float *)bas.p, dw, dws, m, k, n, dy, st);
-    if (rc) return rc;
+    int rc = m == 1 ? launch_gemv_q1(dx, k, false, dw, dws, n, dy, st) : FOCR_E_UNSUPPORTED;
+    if (rc) {
+        FOCR_CUDA_TRY(bq.alloc(m * k, st));
+        FOCR_CUDA_TRY(bas.alloc(m * 4, st));
+        rc = launch_quantize_rows(dx, m, k, false, (int8_t *)bq.p, (float *)bas.p, st);
+        if (rc) return rc;
+        rc = launch_gemv_dequant((const int8_t *)bq.p, (const float *)bas.p, dw, dws, m, k, n, dy, st);
+        if (rc) return rc;
+    }
     if (mem == FOCR_MEM_HOST) {
         FOCR_CUDA_TRY(cudaMemcpyAsync(y, dy, m * n * 4, cudaMemcpyDeviceToHost, st));
         FOCR_CUDA_TRY(cudaStreamSynchronize(st));

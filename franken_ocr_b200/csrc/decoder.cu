@@ -182,6 +182,7 @@ static unsigned grid_for(long n) {
 // y[M, N] = dequant(Q(x) . w^T); device pointers.
 int linear_i8_dev(const float *x, size_t M, size_t K, const int8_t *w, const float *ws, size_t N,
                   bool te, float *y, cudaStream_t st) {
+    if (M == 1 && launch_gemv_q1(x, K, te, w, ws, N, y, st) == FOCR_OK) return FOCR_OK;
     DevBuf bq, bas;
     FOCR_CUDA_TRY(bq.alloc(M * K, st));
     FOCR_CUDA_TRY(bas.alloc(M * 4, st));

@@ -92,6 +92,86 @@ gemv_s4_kernel(const int8_t *__restrict__ A, const uint8_t *__restrict__ Bp,
     }
 }
 
+constexpr int GEMV_Q1_MAX_K = 16384;
+
+// launch_gemv_q1: every block quantises the row itself (amax, scale and
+// rounding exactly as quantize_rows_kernel) into shared memory, then streams
+// two weight rows per warp as gemv16_kernel<1>.
+__global__ void __launch_bounds__(GEMV_THREADS)
+gemv_q1_kernel(const float *__restrict__ x, int K, int te, const int8_t *__restrict__ B,
+               const float *__restrict__ w_scale, int N, float *__restrict__ y) {
+    __shared__ int4 sA[GEMV_Q1_MAX_K / 16];
+    __shared__ float red[GEMV_THREADS / 32];
+    __shared__ float s_sc, s_inv;
+    const int lane = threadIdx.x & 31;
+    const float4 *x4 = reinterpret_cast<const float4 *>(x);
+    float m = 0.0f;
+    for (int i = threadIdx.x; i < K / 4; i += blockDim.x) {
+        const float4 v = x4[i];
+        m = fmaxf(m, fabsf(v.x));
+        m = fmaxf(m, fabsf(v.y));
+        m = fmaxf(m, fabsf(v.z));
+        m = fmaxf(m, fabsf(v.w));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float a = 0.0f;
+        for (int w = 0; w < GEMV_THREADS / 32; w++) a = fmaxf(a, red[w]);
+        const float sc = a > 0.0f ? __fdiv_rn(a, 127.0f) : 1.0f;
+        s_sc = sc;
+        s_inv = __fdiv_rn(1.0f, sc);
+    }
+    __syncthreads();
+    const float inv = s_inv, as = s_sc;
+    int8_t *sq = reinterpret_cast<int8_t *>(sA);
+    for (int i = threadIdx.x; i < K / 4; i += blockDim.x) {
+        const float4 v = x4[i];
+        sq[4 * i] = (int8_t)quant_i8(v.x, inv, te != 0);
+        sq[4 * i + 1] = (int8_t)quant_i8(v.y, inv, te != 0);
+        sq[4 * i + 2] = (int8_t)quant_i8(v.z, inv, te != 0);
+        sq[4 * i + 3] = (int8_t)quant_i8(v.w, inv, te != 0);
+    }
+    __syncthreads();
+    const int K16 = K >> 4;
+    const int warp = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int nwarps = gridDim.x * (blockDim.x >> 5);
+    for (int n0 = warp * 2; n0 < N; n0 += nwarps * 2) {
+        const bool has1 = n0 + 1 < N;
+        const int4 *r0 = reinterpret_cast<const int4 *>(B + (size_t)n0 * K);
+        const int4 *r1 = has1 ? r0 + K16 : r0;
+        int acc0 = 0, acc1 = 0;
+        for (int c0 = lane; c0 < K16; c0 += 32 * GEMV_UNROLL) {
+            int4 b0[GEMV_UNROLL], b1[GEMV_UNROLL];
+#pragma unroll
+            for (int u = 0; u < GEMV_UNROLL; u++) {
+                const int c = c0 + 32 * u;
+                if (c < K16) {
+                    b0[u] = ld_stream16(r0 + c);
+                    b1[u] = ld_stream16(r1 + c);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < GEMV_UNROLL; u++) {
+                const int c = c0 + 32 * u;
+                if (c < K16) {
+                    const int4 a = sA[c];
+                    acc0 = dot16<false>(a, b0[u], acc0);
+                    acc1 = dot16<false>(a, b1[u], acc1);
+                }
+            }
+        }
+        const int s0 = warp_sum_i32(acc0);
+        const int s1 = warp_sum_i32(acc1);
+        if (lane == 0) {
+            y[n0] = __fmul_rn(__fmul_rn((float)s0, as), w_scale[n0]);
+            if (has1) y[n0 + 1] = __fmul_rn(__fmul_rn((float)s1, as), w_scale[n0 + 1]);
+        }
+    }
+}
+
 static int gemv_grid(size_t rows, int rows_per_block) {
     size_t blocks = (rows + rows_per_block - 1) / rows_per_block;
     size_t cap = (size_t)num_sms() * 8;
@@ -196,6 +276,18 @@ int launch_quantize_rows(const float *x, size_t M, size_t K, bool te, int8_t *xq
                          float *scales, cudaStream_t st) {
     if (M == 0) return FOCR_OK;
     quantize_rows_kernel<<<(unsigned)M, 256, 0, st>>>(x, (int)K, te ? 1 : 0, xq, scales);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    return FOCR_OK;
+}
+
+int launch_gemv_q1(const float *x, size_t K, bool te, const int8_t *B, const float *w_scale,
+                   size_t N, float *y, cudaStream_t st) {
+    if (N == 0) return FOCR_OK;
+    if (K == 0 || K % 16 || K > (size_t)GEMV_Q1_MAX_K || ((uintptr_t)x % 16) ||
+        ((uintptr_t)B % 16) || N > (size_t)INT32_MAX)
+        return FOCR_E_UNSUPPORTED;
+    gemv_q1_kernel<<<gemv_grid(N, (GEMV_THREADS / 32) * 2), GEMV_THREADS, 0, st>>>(
+        x, (int)K, te ? 1 : 0, B, w_scale, (int)N, y);
     FOCR_CUDA_TRY(cudaGetLastError());
     return FOCR_OK;
 }

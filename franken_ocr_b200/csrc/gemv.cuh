@@ -184,6 +184,12 @@ int launch_gemv_dequant(const int8_t *xq, const float *a_scale, const int8_t *B,
                         cudaStream_t st);
 int launch_quantize_rows(const float *x, size_t M, size_t K, bool te, int8_t *xq,
                          float *scales, cudaStream_t st);
+// One activation row, quantised inside the GEMV: y[n] = ((f32)(Q(x) . B[n])
+// * a_scale) * w_scale[n] -- the same values as launch_quantize_rows +
+// launch_gemv_dequant, in one launch.  Needs K % 16 == 0, K <= 16384 and
+// 16-byte aligned x and B; returns FOCR_E_UNSUPPORTED otherwise.
+int launch_gemv_q1(const float *x, size_t K, bool te, const int8_t *B, const float *w_scale,
+                   size_t N, float *y, cudaStream_t st);
 int launch_gemv_s4(const int8_t *A, const uint8_t *Bp, const float *scales, size_t group,
                    size_t M, size_t K, size_t N, float *out, const float *dequant_a,
                    cudaStream_t st);

@@ -126,8 +126,12 @@ int focr_lmhead_top1(focr_lmhead *h, const float *x, size_t m, float *best_val,
         dx = h->x;
     }
     float *dlog = (mem == FOCR_MEM_DEVICE && logits) ? logits : h->logits;
-    int rc = launch_quantize_rows(dx, m, h->hidden, false, h->xq, h->xs, st);
-    if (!rc) rc = launch_gemv_dequant(h->xq, h->xs, h->w, h->scales, m, h->hidden, h->rows, dlog, st);
+    int rc = FOCR_E_UNSUPPORTED;
+    if (m == 1) rc = launch_gemv_q1(dx, h->hidden, false, h->w, h->scales, h->rows, dlog, st);
+    if (rc) {
+        rc = launch_quantize_rows(dx, m, h->hidden, false, h->xq, h->xs, st);
+        if (!rc) rc = launch_gemv_dequant(h->xq, h->xs, h->w, h->scales, m, h->hidden, h->rows, dlog, st);
+    }
     if (rc) return rc;
     float *dbv = mem == FOCR_MEM_DEVICE ? best_val : h->bv;
     int32_t *dbi = mem == FOCR_MEM_DEVICE ? best_idx : h->bi;
