@@ -145,34 +145,77 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // Decode attention bit-identical to the reference's per-key online fold
-// (rswa.rs:894-944, fold at :1163-1182).  Grid = (heads, head_dim / 32):
-// every CTA of a head computes the same scores and exponentials, and folds
-// its own 32 dimensions:
-//   1. every key's score (the reference's sequential dot) in parallel;
-//   2. the running max as a prefix scan (m_r = s_r > m_{r-1} ? s_r : m_{r-1},
+// (rswa.rs:894-944, fold at :1163-1182), in two kernels.
+//
+// attention_scores_kernel -- grid (heads, key blocks of 32): the block's K
+// rows are staged in shared memory (row stride 129 floats: thread t reads row
+// t conflict-free) and thread t computes score_r = dot(q, k_r) * scale with
+// the reference's sequential dot (dimension order, one rounding per multiply
+// and per add).  Scores go to a scratch array [heads][keys].
+constexpr int ATT_SB = 32;  // keys per scores block
+
+__global__ void __launch_bounds__(128) attention_scores_kernel(
+    const float *__restrict__ q, const float *__restrict__ ref_k, int prefill_len, int ref_stride,
+    const float *__restrict__ ring_k, int ring_len, int ring_stride, int head_dim,
+    float *__restrict__ scores, int score_stride, const int *__restrict__ ring_len_dev) {
+    extern __shared__ __align__(16) float sc_sm[];
+    const int h = blockIdx.x, r0 = blockIdx.y * ATT_SB, tid = threadIdx.x;
+    if (ring_len_dev) ring_len = *ring_len_dev;
+    const int total = prefill_len + ring_len;
+    if (r0 >= total) return;
+    const int nk = min(ATT_SB, total - r0);
+    const int ld = head_dim + 1;
+    float *sq = sc_sm;           // [head_dim]
+    float *sk = sq + head_dim;   // [ATT_SB][head_dim + 1]
+    for (int i = tid; i < head_dim; i += blockDim.x) sq[i] = q[(size_t)h * head_dim + i];
+    const int per_row = head_dim / 4;
+    for (int i = tid; i < nk * per_row; i += blockDim.x) {
+        const int kr = i / per_row, c = i % per_row, r = r0 + kr;
+        const float *src = r < prefill_len
+                               ? ref_k + ((size_t)h * ref_stride + r) * head_dim
+                               : ring_k + ((size_t)h * ring_stride + (r - prefill_len)) * head_dim;
+        const float4 v = reinterpret_cast<const float4 *>(src)[c];
+        float *dst = sk + kr * ld + 4 * c;
+        dst[0] = v.x;
+        dst[1] = v.y;
+        dst[2] = v.z;
+        dst[3] = v.w;
+    }
+    __syncthreads();
+    if (tid < nk) {
+        const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)head_dim));
+        const float *kr = sk + tid * ld;
+        float d = 0.0f;
+#pragma unroll 16
+        for (int i = 0; i < head_dim; i++) d = __fadd_rn(d, __fmul_rn(sq[i], kr[i]));
+        scores[(size_t)h * score_stride + r0 + tid] = __fmul_rn(d, scale);
+    }
+}
+
+// attention_fold_kernel -- grid (heads, head_dim / 32); every CTA of a head
+// reads the head's scores and folds its own 32 dimensions:
+//   1. the running max as a prefix scan (m_r = s_r > m_{r-1} ? s_r : m_{r-1},
 //      which skips NaN as the reference's `score > run_max` does);
-//   3. per key, in parallel, the fold's two exponentials: the correction
+//   2. per key, in parallel, the fold's two exponentials: the correction
 //      c_r = exp(m_{r-1} - s_r) (0 while m_{r-1} is -inf; exactly 1 when the
 //      max did not move, and then the multiply is skipped -- x * 1 == x, so
 //      that is the reference's untaken branch) and the weight
 //      w_r = exp(s_r - m_r);
-//   4. the serial recurrence den = den * c_r + w_r, acc[d] = acc[d] * c_r +
+//   3. the serial recurrence den = den * c_r + w_r, acc[d] = acc[d] * c_r +
 //      w_r * v_r[d] in key order, one lane per dimension, fed from a ring of
 //      V chunks that all warps stage with cp.async.
-// Shared memory: q [head_dim] | corr [total] | scores, then weights [total] |
-// chunk maxima [ATT_THREADS] | V stages [ATT_STAGES][ATT_CH][ATT_DG].
-__global__ void __launch_bounds__(ATT_THREADS) attention_decode_kernel(
-    const float *__restrict__ q, const float *__restrict__ ref_k, const float *__restrict__ ref_v,
-    int prefill_len, int ref_stride, const float *__restrict__ ring_k,
-    const float *__restrict__ ring_v, int ring_len, int ring_stride, int head_dim,
-    float *__restrict__ out, const int *__restrict__ ring_len_dev = nullptr) {
+// Shared memory: V stages [ATT_STAGES][ATT_CH][ATT_DG] | chunk maxima
+// [ATT_THREADS] | corr [total] | weights [total].
+__global__ void __launch_bounds__(ATT_THREADS) attention_fold_kernel(
+    const float *__restrict__ scores, int score_stride, const float *__restrict__ ref_v,
+    int prefill_len, int ref_stride, const float *__restrict__ ring_v, int ring_len,
+    int ring_stride, int head_dim, float *__restrict__ out, const int *__restrict__ ring_len_dev) {
     extern __shared__ __align__(16) float att_sm[];
     const int h = blockIdx.x, g = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (ring_len_dev) ring_len = *ring_len_dev;
     const int total = prefill_len + ring_len;
     float *sv = att_sm;                                   // [STAGES][CH][DG]
-    float *sq = sv + ATT_STAGES * ATT_CH * ATT_DG;        // [head_dim]
-    float *cm = sq + head_dim;                            // [ATT_THREADS]
+    float *cm = sv + ATT_STAGES * ATT_CH * ATT_DG;        // [ATT_THREADS]
     float *sc = cm + ATT_THREADS;                         // [total]
     float *sw = sc + total;                               // [total]
     auto vrow = [&](int r) -> const float * {
@@ -180,7 +223,6 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_decode_kernel(
                                : ring_v + ((size_t)h * ring_stride + (r - prefill_len)) * head_dim;
     };
     const int nch = (total + ATT_CH - 1) / ATT_CH;
-    // stage V chunk c into buffer c % STAGES: ATT_CH rows x 8 16-byte pieces
     auto stage = [&](int c) {
         float *dst = sv + (c % ATT_STAGES) * ATT_CH * ATT_DG;
         for (int i = tid; i < ATT_CH * (ATT_DG / 4); i += ATT_THREADS) {
@@ -192,37 +234,36 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_decode_kernel(
         if (c < nch) stage(c);
         cp_async_commit();
     }
-    for (int i = tid; i < head_dim; i += ATT_THREADS) sq[i] = q[(size_t)h * head_dim + i];
+    const float *hs = scores + (size_t)h * score_stride;
+    for (int r = tid; r < total; r += ATT_THREADS) sw[r] = hs[r];
     __syncthreads();
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)head_dim));
-    for (int r = tid; r < total; r += ATT_THREADS) {
-        const float *kr = r < prefill_len
-                              ? ref_k + ((size_t)h * ref_stride + r) * head_dim
-                              : ring_k + ((size_t)h * ring_stride + (r - prefill_len)) * head_dim;
-        float d = 0.0f;
-        for (int i = 0; i < head_dim; i += 4) {
-            const float4 k4 = *reinterpret_cast<const float4 *>(kr + i);
-            d = __fadd_rn(d, __fmul_rn(sq[i], k4.x));
-            d = __fadd_rn(d, __fmul_rn(sq[i + 1], k4.y));
-            d = __fadd_rn(d, __fmul_rn(sq[i + 2], k4.z));
-            d = __fadd_rn(d, __fmul_rn(sq[i + 3], k4.w));
-        }
-        sw[r] = __fmul_rn(d, scale);
-    }
-    __syncthreads();
-    // prefix max: contiguous chunks per thread, then the chunk maxima in order
     const int per = (total + ATT_THREADS - 1) / ATT_THREADS;
     const int c0 = min(tid * per, total), c1 = min(c0 + per, total);
     float m = -INFINITY;
     for (int r = c0; r < c1; r++) m = sw[r] > m ? sw[r] : m;
     cm[tid] = m;
     __syncthreads();
-    if (tid == 0) {
+    if (warp == 0) {
+        // exclusive prefix max of the chunk maxima, 8 per lane, then a scan
+        float v[ATT_THREADS / 32];
         float run = -INFINITY;
-        for (int t = 0; t < ATT_THREADS; t++) {
-            const float v = cm[t];
-            cm[t] = run;  // max before chunk t
-            run = v > run ? v : run;
+#pragma unroll
+        for (int j = 0; j < ATT_THREADS / 32; j++) {
+            v[j] = cm[lane * (ATT_THREADS / 32) + j];
+            run = v[j] > run ? v[j] : run;
+        }
+        float incl = run;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float u = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl = u > incl ? u : incl;
+        }
+        float ex = __shfl_up_sync(0xffffffffu, incl, 1);
+        if (lane == 0) ex = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < ATT_THREADS / 32; j++) {
+            cm[lane * (ATT_THREADS / 32) + j] = ex;
+            ex = v[j] > ex ? v[j] : ex;
         }
     }
     __syncthreads();
@@ -246,6 +287,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_decode_kernel(
         if (warp == 0) {
             const float *buf = sv + (c % ATT_STAGES) * ATT_CH * ATT_DG + lane;
             const int r0 = c * ATT_CH, r1 = min(r0 + ATT_CH, total);
+#pragma unroll 8
             for (int r = r0; r < r1; r++) {
                 const float cr = sc[r], w = sw[r];
                 const float wv = __fmul_rn(w, buf[(r - r0) * ATT_DG]);
@@ -267,12 +309,46 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_decode_kernel(
     }
 }
 
-static size_t att_smem(size_t head_dim, size_t total) {
-    return ((size_t)ATT_STAGES * ATT_CH * ATT_DG + head_dim + ATT_THREADS + 2 * total) *
-           sizeof(float);
+// Scores then fold; `keys_cap` bounds the key count (prefill_len +
+// ring_len, or + ring_stride when ring_len comes from ring_len_dev).
+static int launch_attention(const float *q, const float *ref_k, const float *ref_v,
+                            int prefill_len, int ref_stride, const float *ring_k,
+                            const float *ring_v, int ring_len, int ring_stride, int heads,
+                            int head_dim, float *out, const int *ring_len_dev, int keys_cap,
+                            cudaStream_t st);
+
+static size_t att_smem(size_t total) {
+    return ((size_t)ATT_STAGES * ATT_CH * ATT_DG + ATT_THREADS + 2 * total) * sizeof(float);
 }
-static const size_t ATT_SMEM_MAX = ((size_t)ATT_STAGES * ATT_CH * ATT_DG + 256 + ATT_THREADS +
-                                    2 * (size_t)ATT_MAX_KEYS) * sizeof(float);
+static const size_t ATT_SMEM_MAX = att_smem(ATT_MAX_KEYS);
+
+static int launch_attention(const float *q, const float *ref_k, const float *ref_v,
+                            int prefill_len, int ref_stride, const float *ring_k,
+                            const float *ring_v, int ring_len, int ring_stride, int heads,
+                            int head_dim, float *out, const int *ring_len_dev, int keys_cap,
+                            cudaStream_t st) {
+    static bool attr = false;
+    if (!attr) {
+        FOCR_CUDA_TRY(cudaFuncSetAttribute(attention_fold_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)ATT_SMEM_MAX));
+        attr = true;
+    }
+    DevBuf scr;
+    FOCR_CUDA_TRY(scr.alloc((size_t)heads * keys_cap * sizeof(float), st));
+    const size_t ssm = ((size_t)head_dim + (size_t)ATT_SB * (head_dim + 1)) * sizeof(float);
+    attention_scores_kernel<<<dim3((unsigned)heads, (unsigned)((keys_cap + ATT_SB - 1) / ATT_SB)),
+                              128, ssm, st>>>(q, ref_k, prefill_len, ref_stride, ring_k, ring_len,
+                                              ring_stride, head_dim, (float *)scr.p, keys_cap,
+                                              ring_len_dev);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    attention_fold_kernel<<<dim3((unsigned)heads, (unsigned)(head_dim / ATT_DG)), ATT_THREADS,
+                            att_smem(keys_cap), st>>>(
+        (const float *)scr.p, keys_cap, ref_v, prefill_len, ref_stride, ring_v, ring_len,
+        ring_stride, head_dim, out, ring_len_dev);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    return FOCR_OK;
+}
 
 }  // namespace focr
 
@@ -375,14 +451,6 @@ int focr_attention_decode(const float *q, const float *ref_k, const float *ref_v
         return fail(FOCR_E_UNSUPPORTED, "attention_decode: more than 16384 keys or 65535 heads");
     cudaStream_t st = (cudaStream_t)stream;
     const size_t total = prefill_len + ring_len;
-    const size_t smem = att_smem(head_dim, total);
-    static bool attr = false;
-    if (!attr) {
-        FOCR_CUDA_TRY(cudaFuncSetAttribute(attention_decode_kernel,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)ATT_SMEM_MAX));
-        attr = true;
-    }
     const float *dq = q, *drk = ref_k, *drv = ref_v, *dgk = ring_k, *dgv = ring_v;
     float *dout = out;
     Staged sq, srk, srv, sgk, sgv;
@@ -405,11 +473,10 @@ int focr_attention_decode(const float *q, const float *ref_k, const float *ref_v
     } else if (mem != FOCR_MEM_DEVICE) {
         return fail(FOCR_E_ARG, "bad mem kind");
     }
-    attention_decode_kernel<<<dim3((unsigned)heads, (unsigned)(head_dim / ATT_DG)), ATT_THREADS,
-                              smem, st>>>(
-        dq, drk, drv, (int)prefill_len, (int)ref_stride, dgk, dgv, (int)ring_len, (int)ring_stride,
-        (int)head_dim, dout);
-    FOCR_CUDA_TRY(cudaGetLastError());
+    int rc = launch_attention(dq, drk, drv, (int)prefill_len, (int)ref_stride, dgk, dgv,
+                              (int)ring_len, (int)ring_stride, (int)heads, (int)head_dim, dout,
+                              nullptr, (int)total, st);
+    if (rc) return rc;
     if (mem == FOCR_MEM_HOST) {
         FOCR_CUDA_TRY(cudaMemcpyAsync(out, dout, heads * head_dim * 4, cudaMemcpyDeviceToHost, st));
         FOCR_CUDA_TRY(cudaStreamSynchronize(st));
@@ -444,33 +511,9 @@ int focr_attention_decode_at(const float *q, const float *ref_k, const float *re
     if (prefill_len > ref_stride || prefill_len + ring_stride > (size_t)ATT_MAX_KEYS || heads > 65535)
         return fail(FOCR_E_UNSUPPORTED, "attention_decode_at: more than 16384 keys or 65535 heads");
     cudaStream_t st = (cudaStream_t)stream;
-    const size_t smem = att_smem(head_dim, prefill_len + ring_stride);
-    static bool attr = false;
-    if (!attr) {
-        FOCR_CUDA_TRY(cudaFuncSetAttribute(attention_decode_kernel,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)ATT_SMEM_MAX));
-        attr = true;
-    }
-    attention_decode_kernel<<<dim3((unsigned)heads, (unsigned)(head_dim / ATT_DG)), ATT_THREADS,
-                              smem, st>>>(
-        q, ref_k, ref_v, (int)prefill_len, (int)ref_stride, ring_k, ring_v, 0, (int)ring_stride,
-        (int)head_dim, out, state + FOCR_STATE_RING_LEN);
-    FOCR_CUDA_TRY(cudaGetLastError());
-    return FOCR_OK;
-}
-
-
-int focr_add_rms_norm(const float *a, const float *b, size_t rows, size_t cols,
-                      const float *weight, float eps, float *h, float *y, void *stream) {
-    if (rows == 0 || cols == 0) return FOCR_OK;
-    if (!a || !b || !h || !y) return fail(FOCR_E_ARG, "add_rms_norm: null pointer");
-    if (rows > (size_t)INT32_MAX || cols > (size_t)INT32_MAX)
-        return fail(FOCR_E_UNSUPPORTED, "add_rms_norm: dimension exceeds int32 range");
-    rms_norm_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
-        a, (int)rows, (int)cols, weight, eps, y, b, h);
-    FOCR_CUDA_TRY(cudaGetLastError());
-    return FOCR_OK;
+    return launch_attention(q, ref_k, ref_v, (int)prefill_len, (int)ref_stride, ring_k, ring_v, 0,
+                            (int)ring_stride, (int)heads, (int)head_dim, out,
+                            state + FOCR_STATE_RING_LEN, (int)(prefill_len + ring_stride), st);
 }
 
 }  // extern "C"
