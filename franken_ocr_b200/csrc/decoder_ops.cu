@@ -516,4 +516,16 @@ int focr_attention_decode_at(const float *q, const float *ref_k, const float *re
                             state + FOCR_STATE_RING_LEN, (int)(prefill_len + ring_stride), st);
 }
 
+int focr_add_rms_norm(const float *a, const float *b, size_t rows, size_t cols,
+                      const float *weight, float eps, float *h, float *y, void *stream) {
+    if (rows == 0 || cols == 0) return FOCR_OK;
+    if (!a || !b || !h || !y) return fail(FOCR_E_ARG, "add_rms_norm: null pointer");
+    if (rows > (size_t)INT32_MAX || cols > (size_t)INT32_MAX)
+        return fail(FOCR_E_UNSUPPORTED, "add_rms_norm: dimension exceeds int32 range");
+    rms_norm_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
+        a, (int)rows, (int)cols, weight, eps, y, b, h);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    return FOCR_OK;
+}
+
 }  // extern "C"
