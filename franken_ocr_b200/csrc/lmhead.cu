@@ -21,49 +21,81 @@ struct focr_lmhead {
 
 namespace focr {
 
-// First maximum of one row (NaN skipped); -1 / NaN when the row is all-NaN.
-__global__ void argmax_rows_kernel(const float *__restrict__ logits, int n, int offset,
-                                   float *__restrict__ best_v, int32_t *__restrict__ best_i) {
-    const float *row = logits + (size_t)blockIdx.x * n;
+// First maximum (NaN skipped) -- sampler::argmax_row (sampler.rs:168-186).
+// The rule "greater value, or equal value at a lower index" is associative
+// and commutative, so the row is split: block (c, r) reduces columns
+// [c * span, (c + 1) * span) of row r to one (value, index) partial, and
+// argmax_combine_kernel reduces a row's partials.  Index -1 = all NaN.
+__device__ __forceinline__ void better(int &bi, float &bv, int oi, float ov) {
+    if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) {
+        bi = oi;
+        bv = ov;
+    }
+}
+
+__device__ __forceinline__ void block_best(int &bi, float &bv) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        better(bi, bv, __shfl_xor_sync(0xffffffffu, bi, o), __shfl_xor_sync(0xffffffffu, bv, o));
+    if ((threadIdx.x & 31) == 0) {
+        sv[threadIdx.x >> 5] = bv;
+        si[threadIdx.x >> 5] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0)
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++) better(bi, bv, si[w], sv[w]);
+}
+
+__global__ void argmax_part_kernel(const float *__restrict__ logits, int n, int span,
+                                   float *__restrict__ part_v, int *__restrict__ part_i) {
+    const float *row = logits + (size_t)blockIdx.y * n;
+    const int c0 = blockIdx.x * span, c1 = min(c0 + span, n);
     int bi = -1;
     float bv = 0.0f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    for (int i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
         const float v = row[i];
         if (v != v) continue;
         if (bi >= 0 && v <= bv) continue;
         bi = i;
         bv = v;
     }
-    __shared__ float sv[32];
-    __shared__ int si[32];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) {
-            bi = oi;
-            bv = ov;
-        }
-    }
-    if ((threadIdx.x & 31) == 0) {
-        sv[threadIdx.x >> 5] = bv;
-        si[threadIdx.x >> 5] = bi;
-    }
-    __syncthreads();
+    block_best(bi, bv);
     if (threadIdx.x == 0) {
-        int b = -1;
-        float v = 0.0f;
-        for (int w = 0; w < (int)(blockDim.x >> 5); w++) {
-            const int oi = si[w];
-            const float ov = sv[w];
-            if (oi >= 0 && (b < 0 || ov > v || (ov == v && oi < b))) {
-                b = oi;
-                v = ov;
-            }
-        }
-        best_i[blockIdx.x] = b < 0 ? -1 : b + offset;
-        best_v[blockIdx.x] = b < 0 ? NAN : v;
+        part_v[(size_t)blockIdx.y * gridDim.x + blockIdx.x] = bv;
+        part_i[(size_t)blockIdx.y * gridDim.x + blockIdx.x] = bi;
     }
+}
+
+__global__ void argmax_combine_kernel(const float *__restrict__ part_v,
+                                      const int *__restrict__ part_i, int parts, int offset,
+                                      float *__restrict__ best_v, int32_t *__restrict__ best_i) {
+    int bi = -1;
+    float bv = 0.0f;
+    for (int p = threadIdx.x; p < parts; p += blockDim.x)
+        better(bi, bv, part_i[(size_t)blockIdx.x * parts + p], part_v[(size_t)blockIdx.x * parts + p]);
+    block_best(bi, bv);
+    if (threadIdx.x == 0) {
+        best_i[blockIdx.x] = bi < 0 ? -1 : bi + offset;
+        best_v[blockIdx.x] = bi < 0 ? NAN : bv;
+    }
+}
+
+static int launch_argmax_rows(const float *logits, int m, int n, int offset, float *best_v,
+                              int32_t *best_i, cudaStream_t st) {
+    const int span = 1024;
+    const int parts = (n + span - 1) / span;
+    DevBuf pv, pi;
+    FOCR_CUDA_TRY(pv.alloc((size_t)m * parts * 4, st));
+    FOCR_CUDA_TRY(pi.alloc((size_t)m * parts * 4, st));
+    argmax_part_kernel<<<dim3((unsigned)parts, (unsigned)m), 256, 0, st>>>(
+        logits, n, span, (float *)pv.p, (int *)pi.p);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    argmax_combine_kernel<<<(unsigned)m, 256, 0, st>>>((const float *)pv.p, (const int *)pi.p, parts,
+                                                     offset, best_v, best_i);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    return FOCR_OK;
 }
 
 }  // namespace focr
@@ -135,8 +167,8 @@ int focr_lmhead_top1(focr_lmhead *h, const float *x, size_t m, float *best_val,
     if (rc) return rc;
     float *dbv = mem == FOCR_MEM_DEVICE ? best_val : h->bv;
     int32_t *dbi = mem == FOCR_MEM_DEVICE ? best_idx : h->bi;
-    argmax_rows_kernel<<<(unsigned)m, 1024, 0, st>>>(dlog, (int)h->rows, (int)h->row_begin, dbv, dbi);
-    FOCR_CUDA_TRY(cudaGetLastError());
+    rc = launch_argmax_rows(dlog, (int)m, (int)h->rows, (int)h->row_begin, dbv, dbi, st);
+    if (rc) return rc;
     if (mem == FOCR_MEM_HOST) {
         FOCR_CUDA_TRY(cudaMemcpyAsync(best_val, h->bv, m * 4, cudaMemcpyDeviceToHost, st));
         FOCR_CUDA_TRY(cudaMemcpyAsync(best_idx, h->bi, m * 4, cudaMemcpyDeviceToHost, st));
