@@ -89,7 +89,8 @@ class DecoderI8:
     cache per layer: reference block ``[heads, max_prefill, head_dim]`` and
     ring ``[heads, 128, head_dim]`` for K and V."""
 
-    def __init__(self, W: DecoderWeightsHost, max_prefill: int, device: str = "cuda"):
+    def __init__(self, W: DecoderWeightsHost, max_prefill: int, device: str = "cuda",
+                 max_batch: int = 1):
         import torch
 
         from .lmhead import LmHeadShard
@@ -120,7 +121,7 @@ class DecoderI8:
                 d["gu_s"] = up(np.concatenate([L.dense["gate_s"], L.dense["up_s"]]))
                 d["down_w"], d["down_s"] = up(L.dense["down_w"]), up(L.dense["down_s"])
             else:
-                d["moe"] = MoeLayer(L.moe, max_tokens=max_prefill,
+                d["moe"] = MoeLayer(L.moe, max_tokens=max(max_prefill, max_batch),
                                     norm_topk_prob=W.norm_topk_prob,
                                     routed_scaling_factor=W.routed_scaling_factor)
             z = dict(dtype=torch.float32, device=self.dev)
@@ -130,7 +131,7 @@ class DecoderI8:
             d["ring_v"] = torch.zeros((self.heads, RING_WINDOW, HEAD_DIM), **z)
             self.layers.append(d)
         self.final_norm = up(W.final_norm)
-        self.head = LmHeadShard(W.lm_w, W.lm_s, row_begin=0, max_tokens=1)
+        self.head = LmHeadShard(W.lm_w, W.lm_s, row_begin=0, max_tokens=max(1, max_batch))
         self.embed = up(W.embed)
         self.prefill_len = None
         self.ring_len = 0
