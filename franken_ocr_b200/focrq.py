@@ -32,6 +32,9 @@ reference's canonical names (decoder.rs:2057-2092): ``model.layers.{l}.mlp.gate
 ``QInt8PerChan`` record is used verbatim and a high-precision one is quantised
 per row at load time, the ``quant_oc_loaded`` rule (decoder.rs:1777-1786).
 ``QInt4PerGroup`` experts feed the int4 expert kernels directly.
+:func:`decoder_weights` assembles the whole int8 decoder (norms, attention
+projections, dense / MoE MLPs, final norm, lm-head, token embeddings) for the
+device decoder (DecoderWeightCacheI8::build, decoder.rs:2018-2117).
 """
 from __future__ import annotations
 
@@ -546,3 +549,96 @@ def write_moe_layer(wr: Writer, layer: int, W: MoeWeightsHost) -> None:
         for r in ("gate", "up", "down"):
             wr.add_qint8(f"{p}.shared_experts.{r}_proj.weight", W.arrays["sh_" + r + "_w"],
                          W.arrays["sh_" + r + "_s"])
+
+
+def decoder_tensor_names(n_layers: int, n_experts: int, first_dense: int = 1,
+                         shared: bool = True) -> list[str]:
+    """The census of the int8 decoder (DecoderWeightCacheI8::build,
+    decoder.rs:2018-2117)."""
+    names = ["model.embed_tokens.weight", "model.norm.weight", "lm_head.weight"]
+    for l in range(n_layers):
+        p = f"model.layers.{l}"
+        names += [f"{p}.input_layernorm.weight", f"{p}.post_attention_layernorm.weight"]
+        names += [f"{p}.self_attn.{r}_proj.weight" for r in ("q", "k", "v", "o")]
+        if l < first_dense:
+            names += [f"{p}.mlp.{r}_proj.weight" for r in ("gate", "up", "down")]
+        else:
+            names += moe_tensor_names(l, n_experts, shared)
+    return names
+
+
+def decoder_weights(w: Weights, n_layers: int | None = None, heads: int = 10, topk: int = 6):
+    """The whole int8 decoder as a ``DecoderWeightsHost`` for ``DecoderI8``:
+    per layer the two RMSNorm weights (high precision), the q/k/v/o
+    projections and the dense MLP through ``quant_oc_loaded``, MoE layers
+    through :func:`moe_layer_weights`; the final norm, the lm-head (int8) and
+    the token embeddings (widened to f32).  A layer is MoE when its router
+    ``mlp.gate.weight`` is present, dense otherwise; ``n_layers`` defaults to
+    the number of ``model.layers.{l}`` prefixes in the directory."""
+    from .decoder import DecoderWeightsHost, LayerWeightsHost
+
+    if n_layers is None:
+        ls = {int(nm.split(".")[2]) for nm in w.directory if nm.startswith("model.layers.")}
+        n_layers = max(ls) + 1 if ls else 0
+    if n_layers == 0:
+        raise FormatMismatch("no decoder layers in the weights directory")
+    embed = w.mat("model.embed_tokens.weight")
+    if embed.ndim != 2:
+        raise FormatMismatch("model.embed_tokens.weight must be [vocab, hidden]")
+    vocab, hidden = embed.shape
+    layers = []
+    for l in range(n_layers):
+        p = f"model.layers.{l}"
+        L = LayerWeightsHost(input_ln=w.mat(f"{p}.input_layernorm.weight").reshape(-1),
+                             post_ln=w.mat(f"{p}.post_attention_layernorm.weight").reshape(-1))
+        if L.input_ln.shape != (hidden,) or L.post_ln.shape != (hidden,):
+            raise FormatMismatch(f"{p}: layer norms must have {hidden} elements")
+        for r in ("q", "k", "v", "o"):
+            L.proj[r + "_w"], L.proj[r + "_s"] = w.int8_rows(f"{p}.self_attn.{r}_proj.weight")
+        D = heads * 128
+        want = {"q": (D, hidden), "k": (D, hidden), "v": (D, hidden), "o": (hidden, D)}
+        for r, shp in want.items():
+            if L.proj[r + "_w"].shape != shp:
+                raise FormatMismatch(f"{p}.self_attn.{r}_proj.weight: shape "
+                                     f"{list(L.proj[r + '_w'].shape)} != {list(shp)}")
+        if f"{p}.mlp.gate.weight" in w:
+            L.moe = moe_layer_weights(w, l, topk=topk)
+            if L.moe.hidden != hidden:
+                raise FormatMismatch(f"{p}: router hidden {L.moe.hidden} != {hidden}")
+        else:
+            L.dense = {}
+            for r in ("gate", "up", "down"):
+                L.dense[r + "_w"], L.dense[r + "_s"] = w.int8_rows(f"{p}.mlp.{r}_proj.weight")
+            I = L.dense["gate_w"].shape[0]
+            for r, shp in (("gate", (I, hidden)), ("up", (I, hidden)), ("down", (hidden, I))):
+                if L.dense[r + "_w"].shape != shp:
+                    raise FormatMismatch(f"{p}.mlp.{r}_proj.weight: shape "
+                                         f"{list(L.dense[r + '_w'].shape)} != {list(shp)}")
+        layers.append(L)
+    lm_w, lm_s = w.int8_rows("lm_head.weight")
+    if lm_w.shape != (vocab, hidden):
+        raise FormatMismatch(f"lm_head.weight: shape {list(lm_w.shape)} != {[vocab, hidden]}")
+    final = w.mat("model.norm.weight").reshape(-1)
+    return DecoderWeightsHost(hidden=hidden, heads=heads, vocab=vocab, layers=layers,
+                              final_norm=np.ascontiguousarray(final, dtype=np.float32),
+                              lm_w=lm_w, lm_s=lm_s,
+                              embed=np.ascontiguousarray(embed, dtype=np.float32))
+
+
+def write_decoder(wr: Writer, W) -> None:
+    """Store a ``DecoderWeightsHost`` under the canonical names (norms,
+    router and embeddings as F32; projections and experts as stored)."""
+    wr.add_f32("model.embed_tokens.weight", W.embed)
+    wr.add_f32("model.norm.weight", W.final_norm)
+    wr.add_qint8("lm_head.weight", W.lm_w, W.lm_s)
+    for l, L in enumerate(W.layers):
+        p = f"model.layers.{l}"
+        wr.add_f32(f"{p}.input_layernorm.weight", L.input_ln)
+        wr.add_f32(f"{p}.post_attention_layernorm.weight", L.post_ln)
+        for r in ("q", "k", "v", "o"):
+            wr.add_qint8(f"{p}.self_attn.{r}_proj.weight", L.proj[r + "_w"], L.proj[r + "_s"])
+        if L.moe is not None:
+            write_moe_layer(wr, l, L.moe)
+        else:
+            for r in ("gate", "up", "down"):
+                wr.add_qint8(f"{p}.mlp.{r}_proj.weight", L.dense[r + "_w"], L.dense[r + "_s"])

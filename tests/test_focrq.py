@@ -322,3 +322,42 @@ def test_lm_head_shard_rows():
     assert np.array_equal(q1, q[50:150]) and np.array_equal(s1, s[50:150])
     with pytest.raises(ValueError):
         focrq.lm_head_weights(w, 150, 100)
+
+
+def test_decoder_roundtrip_through_focrq():
+    """A whole synthetic decoder written under the canonical names reloads
+    into identical arrays (and into the oracle decoder's identical tokens)."""
+    from oracle import oracle as O
+
+    W = synth.decoder_model(9, layers=3, n_experts=4, topk=2, dense_inter=128, vocab=256,
+                            shared_inter=64)
+    wr = focrq.Writer()
+    focrq.write_decoder(wr, W)
+    w = Weights.from_bytes(wr.to_bytes())
+    w.census(focrq.decoder_tensor_names(3, 4))
+    R = focrq.decoder_weights(w, topk=2)
+    assert (R.hidden, R.heads, R.vocab, len(R.layers)) == (W.hidden, W.heads, W.vocab, 3)
+    for a, b in ((R.embed, W.embed), (R.final_norm, W.final_norm), (R.lm_w, W.lm_w),
+                 (R.lm_s, W.lm_s)):
+        assert np.array_equal(a, b)
+    for La, Lb in zip(R.layers, W.layers):
+        assert np.array_equal(La.input_ln, Lb.input_ln) and np.array_equal(La.post_ln, Lb.post_ln)
+        for k in Lb.proj:
+            assert np.array_equal(La.proj[k], Lb.proj[k]), k
+        if Lb.dense is not None:
+            for k in Lb.dense:
+                assert np.array_equal(La.dense[k], Lb.dense[k]), k
+        else:
+            for k in Lb.moe.arrays:
+                assert np.array_equal(La.moe.arrays[k], Lb.moe.arrays[k]), k
+    e = synth.prompt_embeds(9, 5, W.hidden)
+    assert np.array_equal(O.DecoderOracle(R).generate(e, 4), O.DecoderOracle(W).generate(e, 4))
+
+
+def test_decoder_weights_rejects_bad_shapes():
+    W = synth.decoder_model(9, layers=1, dense_inter=128, vocab=64)
+    W.layers[0].proj["o_w"] = W.layers[0].proj["o_w"][:, :640].copy()
+    wr = focrq.Writer()
+    focrq.write_decoder(wr, W)
+    with pytest.raises(FormatMismatch, match="o_proj"):
+        focrq.decoder_weights(Weights.from_bytes(wr.to_bytes()))
