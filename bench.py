@@ -570,6 +570,42 @@ def cpu_baseline_config3(W, seed, prefill=32, steps=3):
                       f"decoder (scalar C ops), 1 thread, {dt:.1f} s"}
 
 
+def config3_roofline(W, prefill, n_tokens, d_ms):
+    """(roofline dict, launches of our kernels in the decode loop) for config 3."""
+    # algorithmic bytes of one decode token: every int8 weight byte it reads
+    # (+ f32 scales): 6 routed experts + the shared expert per MoE layer, the
+    # dense layer-0 MLP, q/k/v/o per layer, the lm-head; reference+ring K/V
+    # (f32) read by attention
+    hbm_peak, peak_kind = peaks()
+    tok_bytes = 0
+    for L in W.layers:
+        for k in ("q", "k", "v", "o"):
+            tok_bytes += L.proj[k + "_w"].nbytes + L.proj[k + "_s"].nbytes
+        if L.dense is not None:
+            tok_bytes += sum(a.nbytes for a in L.dense.values())
+        else:
+            per_expert = sum(L.moe.arrays[k].nbytes for k in ("gate_w", "up_w", "down_w",
+                                                              "gate_s", "up_s", "down_s"))
+            tok_bytes += L.moe.topk * per_expert // L.moe.expert_count
+            tok_bytes += sum(L.moe.arrays[k].nbytes for k in L.moe.arrays if k.startswith("sh_"))
+            tok_bytes += L.moe.router.nbytes
+    tok_bytes += W.lm_w.nbytes + W.lm_s.nbytes
+    kv = 2 * len(W.layers) * W.heads * 128 * 4 * (prefill + min(n_tokens, 128) / 2)
+    tok_bytes += kv
+    achieved = tok_bytes / (d_ms / n_tokens / 1e3) / 1e9
+    roof = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+            "frac": achieved / hbm_peak, "traffic": None,
+            "note": f"{tok_bytes / 1e6:.0f} MB of weights + K/V per decode token; peak "
+                    f"{peak_kind}; the step is launch/latency bound, not bandwidth bound"}
+    # our kernels per decode token: per layer RMSNorm (or add+RMSNorm), q|k|v
+    # GEMV, RoPE, ring write, attention scores + fold, o GEMV, add+RMSNorm,
+    # then the fused MoE kernel or the dense MLP (gate|up GEMV, SwiGLU, down);
+    # plus prologue, final add+RMSNorm, lm-head GEMV and the two-stage argmax
+    per_tok = sum(9 if L.moe is not None else 11 for L in W.layers) + 5
+    launches = per_tok * (n_tokens - 1)
+    return roof, launches
+
+
 def config3(args, dev, prefill=1024, n_tokens=256, seed=3):
     """Config 3: the synthetic 12-layer int8 decoder; one step = a
     1024-token prefill then a 256-token greedy decode (batch 1), the decode
@@ -619,37 +655,7 @@ def config3(args, dev, prefill=1024, n_tokens=256, seed=3):
     e2e_ms = e2[0].elapsed_time(e2[1])
     d_ms, p_ms = float(np.median(dec)), float(np.median(pre))
     cpu = None if args.no_cpu else cpu_baseline_config3(W, seed)
-    # algorithmic bytes of one decode token: every int8 weight byte it reads
-    # (+ f32 scales): 6 routed experts + the shared expert per MoE layer, the
-    # dense layer-0 MLP, q/k/v/o per layer, the lm-head; reference+ring K/V
-    # (f32) read by attention
-    hbm_peak, peak_kind = peaks()
-    tok_bytes = 0
-    for L in W.layers:
-        for k in ("q", "k", "v", "o"):
-            tok_bytes += L.proj[k + "_w"].nbytes + L.proj[k + "_s"].nbytes
-        if L.dense is not None:
-            tok_bytes += sum(a.nbytes for a in L.dense.values())
-        else:
-            per_expert = sum(L.moe.arrays[k].nbytes for k in ("gate_w", "up_w", "down_w",
-                                                              "gate_s", "up_s", "down_s"))
-            tok_bytes += W.layers[1].moe.topk * per_expert // L.moe.expert_count
-            tok_bytes += sum(L.moe.arrays[k].nbytes for k in L.moe.arrays if k.startswith("sh_"))
-            tok_bytes += L.moe.router.nbytes
-    tok_bytes += W.lm_w.nbytes + W.lm_s.nbytes
-    kv = 2 * len(W.layers) * W.heads * 128 * 4 * (prefill + min(n_tokens, 128) / 2)
-    tok_bytes += kv
-    achieved = tok_bytes / (d_ms / n_tokens / 1e3) / 1e9
-    roof = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-            "frac": achieved / hbm_peak, "traffic": None,
-            "note": f"{tok_bytes / 1e6:.0f} MB of weights + K/V per decode token; peak "
-                    f"{peak_kind}; the step is launch/latency bound, not bandwidth bound"}
-    # our kernels per decode token: per layer RMSNorm (or add+RMSNorm), q|k|v
-    # GEMV, RoPE, ring write, attention scores + fold, o GEMV, add+RMSNorm,
-    # then the fused MoE kernel or the dense MLP (gate|up GEMV, SwiGLU, down);
-    # plus prologue, final add+RMSNorm, lm-head GEMV and the two-stage argmax
-    per_tok = sum(9 if L.moe is not None else 11 for L in W.layers) + 5
-    launches = per_tok * (n_tokens - 1)
+    roof, launches = config3_roofline(W, prefill, n_tokens, d_ms)
     print(json.dumps({
         "metric": "int8 decoder greedy decode tokens/s (config 3: 12 layers, batch 1)",
         "value": n_tokens / (d_ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
