@@ -222,6 +222,8 @@ def run_ours(args, ws, rank, local):
         return
     if args.workload == "config3":
         return config3(args, dev)
+    if args.workload == "config3_batch":
+        return config3_batch(args, dev)
     # ring of layers so that consecutive steps stream from HBM
     R = 2
     layers = [MoeLayer(synth.moe_layer(100 + r, shared_inter=SHARED), max_tokens=TOKENS)
@@ -606,6 +608,52 @@ def config3_roofline(W, prefill, n_tokens, d_ms):
     return roof, launches
 
 
+def config3_batch(args, dev, streams=16, batch=8, prefill=256, n_tokens=64, seed=3):
+    """Continuous batching on the config-3 decoder: `streams` prompts of
+    `prefill` tokens, `batch` active at a time, `n_tokens` greedy tokens each
+    (BatchScheduler + DecoderBatchStep + BatchedDecoderI8).  Timed on the
+    device from the first batched step to the last; the metric is aggregate
+    decode tokens/s."""
+    import torch
+
+    from franken_ocr_b200 import synth
+    from franken_ocr_b200.batch import BatchedDecoderI8, BatchScheduler, DecoderBatchStep, PageStream
+
+    W = synth.decoder_model(seed)
+    B = BatchedDecoderI8(W, n_streams=streams, max_prefill=prefill)
+    embeds = [torch.from_numpy(synth.prompt_embeds(seed + 100 + i, prefill)).to(dev)
+              for i in range(streams)]
+
+    def run():
+        ss = [PageStream(i, prefill, [], B.prefill_stream(i, embeds[i])) for i in range(streams)]
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        toks = BatchScheduler(batch, n_tokens).run(ss, DecoderBatchStep(B, eos_token_id=-1))
+        e1.record()
+        torch.cuda.synchronize()
+        return toks, e0.elapsed_time(e1)
+
+    for _ in range(max(1, args.warmup)):
+        toks0, _ = run()
+    ms = []
+    for _ in range(args.steps):
+        toks, t = run()
+        assert toks == toks0, "tokens changed between runs"
+        ms.append(t)
+    t = float(np.median(ms))
+    total = streams * n_tokens
+    print(json.dumps({
+        "metric": "int8 decoder continuous-batch decode tokens/s (config 3 decoder)",
+        "value": total / (t / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(1, args.warmup), "ms_per_step": t, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8 (i32 accumulate, f32 dequant)",
+        "data": "synthetic (random-init weights, N(0,1) prompt embeddings)",
+        "config": {"workload": "config3_continuous_batch", "streams": streams, "batch": batch,
+                   "prefill_tokens": prefill, "decode_tokens": n_tokens,
+                   "decode_loop": "eager host loop per batched step"}}), flush=True)
+    B.close()
+
+
 def config3(args, dev, prefill=1024, n_tokens=256, seed=3):
     """Config 3: the synthetic 12-layer int8 decoder; one step = a
     1024-token prefill then a 256-token greedy decode (batch 1), the decode
@@ -683,7 +731,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-m1", action="store_true", help="skip the config-0 single-token line")
-    ap.add_argument("--workload", default="config2", choices=["config2", "config0", "config1", "config3"],
+    ap.add_argument("--workload", default="config2", choices=["config2", "config0", "config1", "config3", "config3_batch"],
                     help="config0: only the single-token layer; config1: the raw igemm sweep; "
                          "config3: the 12-layer decoder")
     args = ap.parse_args()
