@@ -3,6 +3,9 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
+#include <set>
+#include <utility>
 #include <vector>
 
 #include "gemv.cuh"
@@ -34,6 +37,20 @@ int num_sms() {
         cached[dev] = v > 0 ? v : 1;
     }
     return cached[dev];
+}
+
+cudaError_t set_max_dynamic_smem(const void *func, int bytes) {
+    // the attribute is per device: remember (kernel, device) pairs already set
+    static std::mutex mu;
+    static std::set<std::pair<const void *, int>> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (done.count({func, dev})) return cudaSuccess;
+    const cudaError_t e =
+        cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) done.insert({func, dev});
+    return e;
 }
 
 bool checked_mul(size_t a, size_t b, size_t *out) {

@@ -22,6 +22,8 @@ void set_error(const std::string &msg);
 int fail(int code, const std::string &msg);
 int cuda_fail(cudaError_t e, const char *what);
 int num_sms();
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device).
+cudaError_t set_max_dynamic_smem(const void *func, int bytes);
 
 #define FOCR_CUDA_TRY(expr)                                  \
     do {                                                     \

@@ -335,13 +335,7 @@ int focr_attention_prefill(const float *q, const float *k, const float *v, size_
     const size_t smem = ((size_t)PA_WARPS * rowf + PA_WARPS * PA_HD) * sizeof(float);
     if (smem > 220 * 1024)
         return fail(FOCR_E_UNSUPPORTED, "attention_prefill: seq above 6880 tokens");
-    static bool attr = false;
-    if (!attr) {
-        FOCR_CUDA_TRY(cudaFuncSetAttribute(attention_prefill_kernel,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           220 * 1024));
-        attr = true;
-    }
+    FOCR_CUDA_TRY(set_max_dynamic_smem((const void *)attention_prefill_kernel, 220 * 1024));
     dim3 grid((unsigned)((seq + PA_WARPS - 1) / PA_WARPS), (unsigned)heads);
     attention_prefill_kernel<<<grid, PA_WARPS * 32, smem, st>>>(dq, dk, dv, (int)seq,
                                                                 (int)(heads * head_dim), rowf, dout);

@@ -333,13 +333,7 @@ static int launch_attention(const float *q, const float *ref_k, const float *ref
                             const float *ring_v, int ring_len, int ring_stride, int heads,
                             int head_dim, float *out, const int *ring_len_dev, int keys_cap,
                             cudaStream_t st) {
-    static bool attr = false;
-    if (!attr) {
-        FOCR_CUDA_TRY(cudaFuncSetAttribute(attention_fold_kernel,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)ATT_SMEM_MAX));
-        attr = true;
-    }
+    FOCR_CUDA_TRY(set_max_dynamic_smem((const void *)attention_fold_kernel, (int)ATT_SMEM_MAX));
     DevBuf scr;
     FOCR_CUDA_TRY(scr.alloc((size_t)heads * keys_cap * sizeof(float), st));
     const size_t ssm = ((size_t)head_dim + (size_t)ATT_SB * (head_dim + 1)) * sizeof(float);

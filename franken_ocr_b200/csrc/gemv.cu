@@ -203,25 +203,18 @@ static int launch_chunk(const int8_t *A, const int8_t *B, int M, int K, int N, i
     const bool fast = (K % 16 == 0) && ((uintptr_t)A % 16 == 0) && ((uintptr_t)B % 16 == 0);
     if (M > 65535 * 8) return fail(FOCR_E_UNSUPPORTED, "gemv: too many activation rows");
     size_t smem = (size_t)(M < 8 ? M : 8) * K;
-    static bool attr_done[2][2][4] = {};
     if (smem > 48 * 1024) {
-        // opt-in to large dynamic shared memory once per instantiation
-        int mi = M <= 1 ? 0 : M <= 2 ? 1 : M <= 4 ? 2 : 3;
-        if (!attr_done[fast][EPI][mi]) {
-#define FOCR_SET_ATTR(MT)                                                                   \
-    do {                                                                                    \
-        cudaFuncSetAttribute(gemv16_kernel<MT, AU8, EPI>,                                   \
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);      \
-        cudaFuncSetAttribute(gemv_any_kernel<MT, AU8, EPI>,                                 \
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);      \
+        // opt-in to large dynamic shared memory (once per kernel and device)
+#define FOCR_SET_ATTR(MT)                                                                      \
+    do {                                                                                       \
+        FOCR_CUDA_TRY(set_max_dynamic_smem((const void *)gemv16_kernel<MT, AU8, EPI>, 200 * 1024)); \
+        FOCR_CUDA_TRY(set_max_dynamic_smem((const void *)gemv_any_kernel<MT, AU8, EPI>, 200 * 1024)); \
     } while (0)
-            if (mi == 0) FOCR_SET_ATTR(1);
-            else if (mi == 1) FOCR_SET_ATTR(2);
-            else if (mi == 2) FOCR_SET_ATTR(4);
-            else FOCR_SET_ATTR(8);
+        if (M <= 1) FOCR_SET_ATTR(1);
+        else if (M <= 2) FOCR_SET_ATTR(2);
+        else if (M <= 4) FOCR_SET_ATTR(4);
+        else FOCR_SET_ATTR(8);
 #undef FOCR_SET_ATTR
-            attr_done[fast][EPI][mi] = true;
-        }
         if (smem > 200 * 1024) return fail(FOCR_E_UNSUPPORTED, "gemv: M*K too large for shared memory");
     }
     if (M <= 1) launch_rows<1, AU8, EPI>(A, B, M, K, N, out, y, as, ws, fast, st);
@@ -296,12 +289,7 @@ int launch_gemv_s4(const int8_t *A, const uint8_t *Bp, const float *scales, size
                    size_t M, size_t K, size_t N, float *out, const float *dequant_a,
                    cudaStream_t st) {
     if (M == 0 || N == 0) return FOCR_OK;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(gemv_s4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             200 * 1024);
-        attr = true;
-    }
+    FOCR_CUDA_TRY(set_max_dynamic_smem((const void *)gemv_s4_kernel, 200 * 1024));
     for (size_t m0 = 0; m0 < M; m0 += 8) {
         const int mc = (int)((M - m0) < 8 ? (M - m0) : 8);
         size_t smem = ((size_t)mc * K + 15) / 16 * 16;
