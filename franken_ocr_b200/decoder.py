@@ -297,8 +297,6 @@ class DecoderI8:
         previous token, advance position and ring cursor, gather the
         embedding), every layer, final norm and lm-head argmax into
         ``self._tok``.  Capturable: no host-varying argument."""
-        from ._lib import STATE_WORDS  # noqa: F401  (layout documented there)
-
         st = self._stream()
         D = self.dim
         check(lib.focr_decode_prologue(_p(self._state), _p(self._tok), _p(self.embed), self.vocab,

@@ -225,9 +225,14 @@ class Weights:
     # -- loading ---------------------------------------------------------------
     @classmethod
     def load(cls, path) -> "Weights":
+        """Map the file read-only (no copy of the payload) and index it."""
+        import mmap
+
         try:
             with open(path, "rb") as f:
-                blob = f.read()
+                size = os.fstat(f.fileno()).st_size
+                blob = (mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ) if size >= PREFIX_LEN
+                        else f.read())
         except OSError as e:
             raise ModelNotFound(f"cannot read weights at {os.fspath(path)}: {e}") from e
         return cls.from_bytes(blob)
