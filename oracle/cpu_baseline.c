@@ -185,3 +185,26 @@ int oracle_cpu_moe_decode(const oracle_moe_layer *L, const float *x, size_t m,
     free(part); free(sh); free(sg); free(su); free(xq); free(aq);
     return rc;
 }
+
+/* The decoder's projections on the dispatched tier: per-row dynamic
+ * quantisation (te: ties-even as linear_int8_dynamic, else decode's
+ * half-away gemv_i8), the VNNI igemm over 64-output-row blocks fanned over
+ * the pool (decoder.rs:1621-1640), dequant ((f32)acc * a_scale) * w_scale.
+ * Same values as oracle_linear_i8. */
+void oracle_cpu_linear_i8(const float *x, size_t m, size_t k, const int8_t *w, const float *ws,
+                          size_t n, int te, float *y, int threads) {
+    const size_t nx = (m * k) > 0 ? m * k : 1, ny = (m * n) > 0 ? m * n : 1;
+    int8_t *xq = (int8_t *)calloc(nx, 1);
+    float *as = (float *)malloc((m ? m : 1) * sizeof(float));
+    int32_t *acc = (int32_t *)calloc(ny, sizeof(int32_t));
+    for (size_t r = 0; r < m; r++)
+        as[r] = te ? oracle_quantize_row_i8_te(x + r * k, k, xq + r * k)
+                   : oracle_quantize_row_i8(x + r * k, k, xq + r * k);
+    oracle_cpu_igemm_s8s8_mt(xq, w, m, k, n, acc, threads);
+    for (size_t r = 0; r < m; r++)
+        for (size_t o = 0; o < n; o++) {
+            float t = (float)acc[r * n + o] * as[r];
+            y[r * n + o] = t * ws[o];
+        }
+    free(xq); free(as); free(acc);
+}

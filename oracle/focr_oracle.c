@@ -688,3 +688,8 @@ int oracle_attention_prefill(const float *q, const float *k, const float *v, siz
     free(p);
     return 0;
 }
+
+/* act[i] = silu(g[i]) * u[i] (decoder.rs:1716-1719) */
+void oracle_silu_mul(const float *g, const float *u, size_t n, float *act) {
+    for (size_t i = 0; i < n; i++) act[i] = oracle_silu(g[i]) * u[i];
+}

@@ -113,6 +113,7 @@ void oracle_swiglu_mlp_i8(const float *x, size_t m, size_t hidden, size_t inter,
                           const int8_t *gate_w, const float *gate_s, const int8_t *up_w,
                           const float *up_s, const int8_t *down_w, const float *down_s, int te,
                           float *y);
+void oracle_silu_mul(const float *g, const float *u, size_t n, float *act);
 int oracle_attention_prefill(const float *q, const float *k, const float *v, size_t seq,
                              size_t heads, size_t head_dim, float *out);
 
@@ -128,6 +129,8 @@ int oracle_cpu_moe_decode(const oracle_moe_layer *L, const float *x, size_t m,
                           const int32_t *idx, const float *w, float *y, int threads);
 void oracle_cpu_igemm_s8s8_mt(const int8_t *a, const int8_t *b, size_t m, size_t k,
                               size_t n, int32_t *out, int threads);
+void oracle_cpu_linear_i8(const float *x, size_t m, size_t k, const int8_t *w, const float *ws,
+                          size_t n, int te, float *y, int threads);
 
 #ifdef __cplusplus
 }

@@ -81,6 +81,8 @@ lib.oracle_linear_i8.argtypes = [vp, sz, sz, vp, vp, sz, C.c_int, vp]
 lib.oracle_swiglu_mlp_i8.argtypes = [vp, sz, sz, sz, vp, vp, vp, vp, vp, vp, C.c_int, vp]
 lib.oracle_attention_prefill.argtypes = [vp, vp, vp, sz, sz, sz, vp]
 lib.oracle_attention_prefill.restype = C.c_int
+lib.oracle_silu_mul.argtypes = [vp, vp, sz, vp]
+lib.oracle_cpu_linear_i8.argtypes = [vp, sz, sz, vp, vp, sz, C.c_int, vp, C.c_int]
 
 
 def _p(a):
@@ -322,13 +324,17 @@ def attention_decode(q, ref_k, ref_v, prefill_len, ring_k, ring_v, ring_len):
     return out
 
 
-def linear_i8(x, w, ws, ties_even):
-    """nn::linear_int8_dynamic (ties_even) / gemv_i8 (half away), row by row."""
+def linear_i8(x, w, ws, ties_even, threads=0):
+    """nn::linear_int8_dynamic (ties_even) / gemv_i8 (half away), row by row;
+    threads > 0 runs the restated dispatched tier (same values)."""
     x, w, ws = _c(x, np.float32), _c(w, np.int8), _c(ws, np.float32)
     m, k = x.shape
     n = w.shape[0]
     y = np.empty((m, n), np.float32)
-    lib.oracle_linear_i8(_p(x), m, k, _p(w), _p(ws), n, int(ties_even), _p(y))
+    if threads > 0:
+        lib.oracle_cpu_linear_i8(_p(x), m, k, _p(w), _p(ws), n, int(ties_even), _p(y), threads)
+    else:
+        lib.oracle_linear_i8(_p(x), m, k, _p(w), _p(ws), n, int(ties_even), _p(y))
     return y
 
 
@@ -362,8 +368,12 @@ class DecoderOracle:
 
     HD, WINDOW, EPS = 128, 128, 1e-6
 
-    def __init__(self, W):
+    def __init__(self, W, threads=0):
+        """threads > 0: decode steps run the projections, the dense MLP, the
+        MoE experts and the lm-head on the restated dispatched tier
+        (cpu_baseline.c, same values) -- the timed CPU baseline."""
         self.W = W
+        self.threads = threads
         self.D = W.heads * self.HD
         self.moe = [MoeOracle(L.moe, norm_topk_prob=W.norm_topk_prob,
                               scaling=W.routed_scaling_factor) if L.moe is not None else None
@@ -411,20 +421,34 @@ class DecoderOracle:
         for li, L in enumerate(self.W.layers):
             P = L.proj
             n = rms_norm(x, L.input_ln, self.EPS)
-            q = apply_rope(linear_i8(n, P["q_w"], P["q_s"], False), cos_t, sin_t, self.HD)
-            k = apply_rope(linear_i8(n, P["k_w"], P["k_s"], False), cos_t, sin_t, self.HD)
-            v = linear_i8(n, P["v_w"], P["v_s"], False)
+            th = self.threads
+            q = apply_rope(linear_i8(n, P["q_w"], P["q_s"], False, th), cos_t, sin_t, self.HD)
+            k = apply_rope(linear_i8(n, P["k_w"], P["k_s"], False, th), cos_t, sin_t, self.HD)
+            v = linear_i8(n, P["v_w"], P["v_s"], False, th)
             rk, rv = self.ring[li]
             rk[:, slot] = k.reshape(self.W.heads, self.HD)
             rv[:, slot] = v.reshape(self.W.heads, self.HD)
             fk, fv = self.ref[li]
             ctx = attention_decode(q.reshape(self.W.heads, self.HD), fk, fv, self.prefill_len,
                                    rk, rv, self.ring_len)
-            h = x + linear_i8(ctx.reshape(1, -1), P["o_w"], P["o_s"], False)
+            h = x + linear_i8(ctx.reshape(1, -1), P["o_w"], P["o_s"], False, th)
             n2 = rms_norm(h, L.post_ln, self.EPS)
-            if L.moe is not None:
+            if L.moe is not None and th:
+                M = L.moe
+                rc, idx, w = route(n2, M.router, M.topk, self.W.norm_topk_prob,
+                                   self.W.routed_scaling_factor)
+                assert rc == 0, rc
+                mlp = self.moe[li].cpu_forward(n2, idx, w, th)
+            elif L.moe is not None:
                 rc, mlp, _, _ = self.moe[li].decode(n2)
                 assert rc == 0, rc
+            elif th:
+                d = L.dense
+                g = linear_i8(n2, d["gate_w"], d["gate_s"], False, th)
+                u = linear_i8(n2, d["up_w"], d["up_s"], False, th)
+                act = np.empty_like(g)
+                lib.oracle_silu_mul(_p(g), _p(u), g.size, _p(act))
+                mlp = linear_i8(act, d["down_w"], d["down_s"], False, th)
             else:
                 mlp = swiglu_mlp_i8(n2, L.dense, False)
             x = h + mlp
@@ -432,7 +456,7 @@ class DecoderOracle:
 
     def lm_head(self, row):
         n = rms_norm(_c(row, np.float32).reshape(1, -1), self.W.final_norm, self.EPS)
-        return linear_i8(n, self.W.lm_w, self.W.lm_s, False)[0]
+        return linear_i8(n, self.W.lm_w, self.W.lm_s, False, self.threads)[0]
 
     def generate(self, embeds, n_tokens, hiddens=None):
         h = self.prefill(embeds)

@@ -142,3 +142,19 @@ def test_decoder_oracle_ring_wraps_and_is_deterministic(oracle):
     t2 = oracle.DecoderOracle(W).generate(e, 131)
     assert np.array_equal(t1, t2)
     assert t1.min() >= 0 and t1.max() < 256
+
+
+def test_threaded_cpu_decoder_matches_scalar_oracle(oracle):
+    """The timed CPU baseline (dispatched-tier projections, threaded MoE
+    driver) gives the scalar oracle's hidden states and tokens exactly."""
+    from franken_ocr_b200 import synth
+
+    W = synth.decoder_model(6, layers=2, n_experts=8, dense_inter=256, vocab=512,
+                            shared_inter=256)
+    e = synth.prompt_embeds(6, 7, W.hidden)
+    h1, h2 = [], []
+    t1 = oracle.DecoderOracle(W).generate(e, 6, hiddens=h1)
+    t2 = oracle.DecoderOracle(W, threads=4).generate(e, 6, hiddens=h2)
+    assert np.array_equal(t1, t2)
+    for a, b in zip(h1, h2):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
