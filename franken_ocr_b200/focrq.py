@@ -61,13 +61,15 @@ GROUP_SIZES = (16, 32)
 DEFAULT_MODEL_ID = "unlimited-ocr"
 MODEL_LICENSE_NOTICE = "Baidu Unlimited-OCR - Copyright (c) 2026 Baidu, MIT License"
 # Architecture registry: id -> the notice its artifacts must carry
-# (src/native_engine/model_arch.rs:180-380).
+# (src/native_engine/model_arch.rs:180-425).
 MODEL_REGISTRY = {
     "unlimited-ocr": MODEL_LICENSE_NOTICE,
     "got-ocr2": "GOT-OCR2.0 (StepFun) - Apache-2.0",
     "smolvlm2": "SmolVLM2 (HuggingFaceTB) - Apache-2.0",
     "onechart": "OneChart - Apache-2.0",
     "tromr": "Polyphonic-TrOMR (NetEase) - Apache-2.0",
+    "trocr": "TrOCR (Microsoft) - MIT",
+    "pix2tex": "pix2tex / LaTeX-OCR - MIT",
 }
 
 

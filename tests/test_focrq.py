@@ -361,3 +361,27 @@ def test_decoder_weights_rejects_bad_shapes():
     focrq.write_decoder(wr, W)
     with pytest.raises(FormatMismatch, match="o_proj"):
         focrq.decoder_weights(Weights.from_bytes(wr.to_bytes()))
+
+
+# -- golden fixtures from the reference (tests/golden/make_golden.py) -----------------
+GOLDEN = __import__("pathlib").Path(__file__).resolve().parent / "golden"
+
+
+def test_registry_matches_the_reference_registry():
+    want = json.loads((GOLDEN / "model_registry.json").read_text())
+    assert focrq.MODEL_REGISTRY == want
+    assert focrq.MODEL_LICENSE_NOTICE == want["unlimited-ocr"]
+
+
+def test_reference_minimal_header_example_loads():
+    """The format document's minimal header, as a writer would emit it
+    (canonical JSON), loads with an empty directory and keeps its metadata."""
+    hdr = json.loads((GOLDEN / "focrq_minimal_header.json").read_text())
+    hj = json.dumps(hdr, sort_keys=True, separators=(",", ":")).encode()
+    b = (b"FOCRQ\0" + struct.pack("<IB", hdr["format_version"], hdr["arch_target"]) + bytes(32)
+         + struct.pack("<Q", len(hj)) + hj)
+    w = Weights.from_bytes(b)
+    assert len(w) == 0 and w.model_id == "unlimited-ocr" and w.arch_target == 0
+    assert w.source_sha256 == "0" * 64
+    assert w.header["model_config"]["hidden_size"] == 1280
+    assert w.header["packing_manifest"]["rounding"] == "round_ties_to_even"
