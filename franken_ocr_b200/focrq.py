@@ -622,6 +622,14 @@ def decoder_weights(w: Weights, n_layers: int | None = None, heads: int = 10, to
                     raise FormatMismatch(f"{p}.mlp.{r}_proj.weight: shape "
                                          f"{list(L.dense[r + '_w'].shape)} != {list(shp)}")
         layers.append(L)
+    cfg = w.header.get("model_config")
+    if isinstance(cfg, dict):
+        # format document "Frozen model_config": a mismatch with the tensors
+        # is FormatMismatch, not a warning
+        for key, have in (("hidden_size", hidden), ("num_attention_heads", heads),
+                          ("num_hidden_layers", n_layers), ("vocab_size", vocab)):
+            if key in cfg and cfg[key] != have:
+                raise FormatMismatch(f"model_config.{key} = {cfg[key]} but the tensors give {have}")
     lm_w, lm_s = w.int8_rows("lm_head.weight")
     if lm_w.shape != (vocab, hidden):
         raise FormatMismatch(f"lm_head.weight: shape {list(lm_w.shape)} != {[vocab, hidden]}")

@@ -385,3 +385,16 @@ def test_reference_minimal_header_example_loads():
     assert w.source_sha256 == "0" * 64
     assert w.header["model_config"]["hidden_size"] == 1280
     assert w.header["packing_manifest"]["rounding"] == "round_ties_to_even"
+
+
+def test_decoder_model_config_must_match_the_tensors():
+    W = synth.decoder_model(9, layers=1, dense_inter=128, vocab=64)
+    good = {"hidden_size": 1280, "num_attention_heads": 10, "num_hidden_layers": 1,
+            "vocab_size": 64}
+    wr = focrq.Writer(model_config=good)
+    focrq.write_decoder(wr, W)
+    focrq.decoder_weights(Weights.from_bytes(wr.to_bytes()))
+    wr = focrq.Writer(model_config={**good, "num_hidden_layers": 12})
+    focrq.write_decoder(wr, W)
+    with pytest.raises(FormatMismatch, match="num_hidden_layers"):
+        focrq.decoder_weights(Weights.from_bytes(wr.to_bytes()))
