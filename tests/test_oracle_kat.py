@@ -281,3 +281,33 @@ def test_vocab_tile_ranges(oracle, tiles):
     assert all(a[1] == b[0] for a, b in zip(r, r[1:]))
     lens = [e - s for s, e in r]
     assert max(lens) - min(lens) <= 1 and lens == sorted(lens, reverse=True)
+
+
+# ---- tests/int32_overflow_proof.rs -------------------------------------------
+
+def test_int32_boundary_k(oracle):
+    """stress_k_at_the_i32_boundary (:363-424): the largest U8S8 K whose
+    all-extreme dot fits i32 (66311 of 255*127) accumulates exactly; the S8S8
+    cliff is K = 133144 of 127*127."""
+    k = 66_311
+    assert k * 255 * 127 < 2 ** 31 - 1 < (k + 1) * 255 * 127
+    out = np.zeros(1, np.int32)
+    oracle.igemm_u8s8(np.full(k, 255, np.uint8), np.full(k, 127, np.int8), 1, k, 1, out)
+    assert int(out[0]) == k * 255 * 127
+    ks = 133_144
+    assert ks * 127 * 127 < 2 ** 31 - 1 < (ks + 1) * 127 * 127
+    out = np.zeros(1, np.int32)
+    oracle.igemm_s8s8(np.full(ks, 127, np.int8), np.full(ks, 127, np.int8), 1, ks, 1, out)
+    assert int(out[0]) == ks * 127 * 127
+
+
+def test_multi_channel_worst_case_accumulators(oracle):
+    """multi_channel_gemm_each_accumulator_independent (:426-464): a [3, 6848]
+    x [6848, 4] GEMM of extreme operands equals the i64 product cell by cell."""
+    m, k, n = 3, 6848, 4
+    g = np.random.default_rng(6848)
+    a = g.choice(np.array([-128, 127], np.int8), size=m * k)
+    b = g.choice(np.array([-128, 127], np.int8), size=n * k)
+    out = np.zeros(m * n, np.int32)
+    oracle.igemm_s8s8(a, b, m, k, n, out)
+    assert np.array_equal(out.astype(np.int64), i64_ref(a, b, m, k, n))
