@@ -34,7 +34,7 @@ sys.path.insert(0, str(ROOT))
 HIDDEN, INTER, NEXP, TOPK, SHARED = 1280, 896, 64, 6, 1792
 # DRAM bytes (read + write) of one config-2 step's two tensor-core kernels,
 # from one ncu capture of this workload (dram__bytes.sum.per_second x
-# gpu__time_duration); see profiles/moe_forward_config2_traffic.md
+# gpu__time_duration)
 CFG2_TRAFFIC_BYTES = 203.4e6
 CFG2_TRAFFIC_SOURCE = "ncu: MoeGateUp 136.1 MB + MoeDown 67.3 MB per step"
 TOKENS = 64

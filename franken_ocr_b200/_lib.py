@@ -33,6 +33,7 @@ EXPORTS = [
     "focr_attention_decode", "focr_linear_i8", "focr_swiglu", "focr_add",
     "focr_attention_prefill", "focr_rope_table", "focr_decode_prologue", "focr_rope_apply_at",
     "focr_ring_write", "focr_attention_decode_at", "focr_add_rms_norm",
+    "focr_igemm_status", "focr_status_check",
 ]
 
 
@@ -78,6 +79,8 @@ lib.focr_tier_string.restype = C.c_char_p
 for _name in ("focr_igemm_s8s8", "focr_igemm_u8s8"):
     getattr(lib, _name).argtypes = [vp, sz, vp, sz, sz, sz, sz, vp, sz, i32, vp]
 lib.focr_igemm_s4s8_packed.argtypes = [vp, sz, vp, sz, vp, sz, sz, sz, sz, sz, vp, sz, i32, vp]
+lib.focr_igemm_status.argtypes = [C.POINTER(i32), i32]
+lib.focr_status_check.argtypes = [i32]
 lib.focr_quantize_rows_i8.argtypes = [vp, sz, sz, i32, vp, vp, i32, vp]
 lib.focr_gemv_i8.argtypes = [vp, sz, sz, vp, vp, sz, vp, i32, vp]
 lib.focr_gemv_i8_noalloc.argtypes = [vp, sz, sz, vp, vp, sz, vp, vp]

@@ -107,7 +107,18 @@ static int igemm_entry(const char *ctx, bool au8, const void *a, size_t a_len, c
     if (rc) return rc;
     FOCR_CUDA_TRY(cudaMemcpyAsync(out, dout.p, m * n * 4, cudaMemcpyDeviceToHost, st));
     FOCR_CUDA_TRY(cudaStreamSynchronize(st));
-    return FOCR_OK;
+    // host mode: surface an expired bounded wait of the tensor-core kernel
+    int word = 0;
+    if ((rc = tc_status_read(&word, true))) return rc;
+    return status_word_check(ctx, word);
+}
+
+int status_word_check(const char *ctx, int word) {
+    if (word == 0) return FOCR_OK;
+    return fail(FOCR_E_TIMEOUT,
+                fmt("%s: a bounded device-side wait expired (status word 0x%x); the result is "
+                    "incomplete",
+                    ctx, word));
 }
 
 }  // namespace focr
@@ -119,6 +130,13 @@ extern "C" {
 const char *focr_last_error(void) { return g_err.c_str(); }
 
 const char *focr_tier_string(void) { return "sm100a"; }
+
+int focr_igemm_status(int *word, int clear) {
+    if (!word) return fail(FOCR_E_ARG, "igemm_status: null pointer");
+    return tc_status_read(word, clear != 0);
+}
+
+int focr_status_check(int word) { return status_word_check("igemm", word); }
 
 int focr_igemm_s8s8(const int8_t *a, size_t a_len, const int8_t *b, size_t b_len, size_t m,
                     size_t k, size_t n, int32_t *out, size_t out_len, int mem, void *stream) {

@@ -176,6 +176,12 @@ __global__ void gemv_s4_kernel(const int8_t *__restrict__ A, const uint8_t *__re
                                int N, float *__restrict__ out,
                                const float *__restrict__ dequant_a);
 
+// Per-device status word of the raw tcgen05 igemm (value 4: a bounded wait
+// expired): read, and optionally cleared, after the caller synchronised.
+int tc_status_read(int *word, bool clear);
+// FOCR_OK for a zero status word, else FOCR_E_TIMEOUT with a message.
+int status_word_check(const char *ctx, int word);
+
 // Host launchers (stream-ordered; all pointers device).
 int launch_igemm(const void *A, bool au8, const int8_t *B, size_t M, size_t K, size_t N,
                  int32_t *out, cudaStream_t st);

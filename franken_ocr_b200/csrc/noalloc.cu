@@ -17,6 +17,17 @@
 // start at zero (each call writes every scratch byte it reads), but calls that
 // overlap on the GPU -- on different streams, or on one stream from several
 // host threads without ordering -- race on it.
+//
+// Limits (checked up front, FOCR_E_SHAPE otherwise): m*k <= 262144 and
+// m <= 1024 (the scratch), and min(m, 8)*k <= 204800 (the GEMV stages up to
+// eight quantised rows in shared memory).  A single row (m == 1) takes the
+// fused decode GEMV that quantises inside the kernel and touches no scratch,
+// exactly as focr_gemv_i8 does.
+//
+// The scratch's device address is looked up once per device and kept for the
+// life of the process; it is not valid across cudaDeviceReset (or any other
+// teardown of the device's primary context), after which this entry point
+// must not be called again in the same process.
 #include <mutex>
 
 #include "gemv.cuh"
@@ -25,6 +36,7 @@ namespace focr {
 
 constexpr size_t NOALLOC_MAX_XQ = 256 * 1024;   // m * k bytes of quantised activations
 constexpr size_t NOALLOC_MAX_ROWS = 1024;       // m (one f32 scale per row)
+constexpr size_t NOALLOC_MAX_STAGED = 200 * 1024; // min(m, 8) * k bytes staged per GEMV CTA
 
 static __device__ __align__(256) unsigned char
     g_noalloc_scratch[NOALLOC_MAX_XQ + NOALLOC_MAX_ROWS * sizeof(float)];
@@ -59,16 +71,20 @@ extern "C" int focr_gemv_i8_noalloc(const float *x, size_t m, size_t k, const in
     if (m == 0 || n == 0) return FOCR_OK;
     if (!x || !w || !w_scale || !y) return fail(FOCR_E_ARG, "gemv_i8_noalloc: null pointer");
     size_t mk = 0;
-    if (!checked_mul(m, k, &mk) || mk > NOALLOC_MAX_XQ || m > NOALLOC_MAX_ROWS)
+    if (!checked_mul(m, k, &mk) || mk > NOALLOC_MAX_XQ || m > NOALLOC_MAX_ROWS ||
+        (m < 8 ? m : 8) * k > NOALLOC_MAX_STAGED)
         return fail(FOCR_E_SHAPE,
-                    "gemv_i8_noalloc: m*k must be <= 262144 and m <= 1024 (fixed scratch); "
-                    "use focr_gemv_i8 for larger inputs");
+                    "gemv_i8_noalloc: m*k must be <= 262144, m <= 1024 and min(m,8)*k <= 204800 "
+                    "(fixed scratch); use focr_gemv_i8 for larger inputs");
+    cudaStream_t st = (cudaStream_t)stream;
+    // one row: the fused GEMV quantises in-kernel and needs no scratch
+    int rc = m == 1 ? launch_gemv_q1(x, k, false, w, w_scale, n, y, st) : FOCR_E_UNSUPPORTED;
+    if (rc != FOCR_E_UNSUPPORTED) return rc;
     void *scratch = nullptr;
-    int rc = noalloc_scratch(&scratch);
+    rc = noalloc_scratch(&scratch);
     if (rc) return rc;
     int8_t *xq = static_cast<int8_t *>(scratch);
     float *xs = reinterpret_cast<float *>(static_cast<unsigned char *>(scratch) + NOALLOC_MAX_XQ);
-    cudaStream_t st = (cudaStream_t)stream;
     rc = launch_quantize_rows(x, m, k, false, xq, xs, st);
     if (rc) return rc;
     return launch_gemv_dequant(xq, xs, w, w_scale, m, k, n, y, st);

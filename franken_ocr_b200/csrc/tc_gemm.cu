@@ -195,10 +195,48 @@ static int run_raw(const void *A, size_t a_rows, const int8_t *B, size_t M, size
     return launch_tc(p, (int)(p.ntiles < sms ? p.ntiles : sms), st);
 }
 
-static int *tc_status_word() {
-    static int *w = nullptr;
-    if (!w) cudaMalloc(&w, sizeof(int) * 64);
-    return w;
+// One status word per device (bit 2: a bounded wait in the raw igemm kernel
+// expired), allocated and zeroed on the first raw igemm call on that device.
+constexpr int kMaxDevices = 64;
+static std::mutex g_status_mu;
+static int *g_status[kMaxDevices];
+
+int tc_status_word(int **out) {
+    int dev = 0;
+    FOCR_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return fail(FOCR_E_UNSUPPORTED, "device index >= 64");
+    std::lock_guard<std::mutex> lock(g_status_mu);
+    if (!g_status[dev]) {
+        int *w = nullptr;
+        cudaError_t e = cudaMalloc(&w, sizeof(int) * 64);
+        if (e != cudaSuccess) return fail(FOCR_E_ALLOC, "igemm status word: cudaMalloc failed");
+        e = cudaMemset(w, 0, sizeof(int) * 64);
+        if (e != cudaSuccess) {
+            cudaFree(w);
+            return cuda_fail(e, "igemm status word: cudaMemset");
+        }
+        g_status[dev] = w;
+    }
+    *out = g_status[dev];
+    return FOCR_OK;
+}
+
+// Reads (and optionally clears) the current device's status word; the caller
+// has synchronised the streams whose igemm calls it asks about.  0 when no
+// raw tcgen05 igemm ran on this device yet.
+int tc_status_read(int *word, bool clear) {
+    int dev = 0;
+    FOCR_CUDA_TRY(cudaGetDevice(&dev));
+    *word = 0;
+    int *w = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_status_mu);
+        if (dev >= 0 && dev < kMaxDevices) w = g_status[dev];
+    }
+    if (!w) return FOCR_OK;
+    FOCR_CUDA_TRY(cudaMemcpy(word, w, sizeof(int), cudaMemcpyDeviceToHost));
+    if (clear && *word) FOCR_CUDA_TRY(cudaMemset(w, 0, sizeof(int)));
+    return FOCR_OK;
 }
 
 // A has a_rows >= M rows (rows past M, if any, are padding; at least 128
@@ -206,7 +244,8 @@ static int *tc_status_word() {
 int launch_tc_igemm(const void *A, size_t a_rows, bool au8, const int8_t *B, size_t M, size_t K,
                     size_t N, int32_t *out, cudaStream_t st) {
     if (au8) return fail(FOCR_E_UNSUPPORTED, "tc igemm: u8 activations use the GEMV tier");
-    int *err = tc_status_word();
+    int *err = nullptr;
+    if (int rc = tc_status_word(&err)) return rc;
     const size_t mt = (M + 127) / 128;
     const int sms = num_sms();
     // widest tile that still gives every SM a CTA; the TMA reduce-add

@@ -13,7 +13,7 @@
 //   __device__ void epilogue(const TcJob &, uint32_t tmem, int quarter, int lane, void *smem) const
 //   __device__ void epilogue_done(int quarter, int lane) const  -- after the warp's last job
 //   __device__ void before_loads(const TcJob &) const  -- producer, before a job's first load
-//   int *err                     -- status word (bit 4: a bounded wait expired)
+//   int *err                     -- status word (value 4 is OR-ed in when a bounded wait expires)
 // A job computes D[128 x n_mma] = sum over kblocks of A[a_row.., k] . B[b_row.., k]
 // for every A operand (accumulator a at TMEM column offset a*BN of its buffer).
 // Each role walks the same deterministic job sequence with its own iterator.
@@ -202,14 +202,10 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__
 
 template <class P>
 int launch_tc(const P &p, int grid, cudaStream_t st) {
-    static bool attr = false;
     constexpr size_t smem = tc_smem_bytes<P>();
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<P>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return cuda_fail(e, "tc_gemm_kernel smem attribute");
-        attr = true;
-    }
+    // the opt-in is per (kernel, device): a process may drive several GPUs
+    cudaError_t e = set_max_dynamic_smem((const void *)tc_gemm_kernel<P>, (int)smem);
+    if (e != cudaSuccess) return cuda_fail(e, "tc_gemm_kernel smem attribute");
     if (grid < 1) grid = 1;
     P q = p;
     q.trace = host_trace();

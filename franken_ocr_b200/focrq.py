@@ -574,19 +574,31 @@ def decoder_tensor_names(n_layers: int, n_experts: int, first_dense: int = 1,
     return names
 
 
-def decoder_weights(w: Weights, n_layers: int | None = None, heads: int = 10, topk: int = 6):
+def decoder_weights(w: Weights, n_layers: int | None = None, heads: int | None = None,
+                    topk: int = 6):
     """The whole int8 decoder as a ``DecoderWeightsHost`` for ``DecoderI8``:
     per layer the two RMSNorm weights (high precision), the q/k/v/o
     projections and the dense MLP through ``quant_oc_loaded``, MoE layers
     through :func:`moe_layer_weights`; the final norm, the lm-head (int8) and
     the token embeddings (widened to f32).  A layer is MoE when its router
     ``mlp.gate.weight`` is present, dense otherwise; ``n_layers`` defaults to
-    the number of ``model.layers.{l}`` prefixes in the directory."""
+    the number of ``model.layers.{l}`` prefixes in the directory (a smaller
+    value loads that prefix of the layers).  ``heads`` defaults to the header's
+    ``model_config.num_attention_heads`` (10 when absent); an explicit value
+    that disagrees with it is a mismatch."""
     from .decoder import DecoderWeightsHost, LayerWeightsHost
 
+    ls = {int(nm.split(".")[2]) for nm in w.directory if nm.startswith("model.layers.")}
+    file_layers = max(ls) + 1 if ls else 0
     if n_layers is None:
-        ls = {int(nm.split(".")[2]) for nm in w.directory if nm.startswith("model.layers.")}
-        n_layers = max(ls) + 1 if ls else 0
+        n_layers = file_layers
+    cfg = w.header.get("model_config")
+    cfg = cfg if isinstance(cfg, dict) else {}
+    if heads is None:
+        heads = int(cfg.get("num_attention_heads", 10))
+    elif "num_attention_heads" in cfg and cfg["num_attention_heads"] != heads:
+        raise FormatMismatch(f"model_config.num_attention_heads = {cfg['num_attention_heads']} "
+                             f"but {heads} heads were asked for")
     if n_layers == 0:
         raise FormatMismatch("no decoder layers in the weights directory")
     embed = w.mat("model.embed_tokens.weight")
@@ -622,14 +634,13 @@ def decoder_weights(w: Weights, n_layers: int | None = None, heads: int = 10, to
                     raise FormatMismatch(f"{p}.mlp.{r}_proj.weight: shape "
                                          f"{list(L.dense[r + '_w'].shape)} != {list(shp)}")
         layers.append(L)
-    cfg = w.header.get("model_config")
-    if isinstance(cfg, dict):
-        # format document "Frozen model_config": a mismatch with the tensors
-        # is FormatMismatch, not a warning
-        for key, have in (("hidden_size", hidden), ("num_attention_heads", heads),
-                          ("num_hidden_layers", n_layers), ("vocab_size", vocab)):
-            if key in cfg and cfg[key] != have:
-                raise FormatMismatch(f"model_config.{key} = {cfg[key]} but the tensors give {have}")
+    # format document "Frozen model_config": a mismatch with the tensors is
+    # FormatMismatch, not a warning.  The layer count is the file's, not the
+    # (possibly smaller) number of layers asked for.
+    for key, have in (("hidden_size", hidden), ("num_attention_heads", heads),
+                      ("num_hidden_layers", file_layers), ("vocab_size", vocab)):
+        if key in cfg and cfg[key] != have:
+            raise FormatMismatch(f"model_config.{key} = {cfg[key]} but the tensors give {have}")
     lm_w, lm_s = w.int8_rows("lm_head.weight")
     if lm_w.shape != (vocab, hidden):
         raise FormatMismatch(f"lm_head.weight: shape {list(lm_w.shape)} != {[vocab, hidden]}")

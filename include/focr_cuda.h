@@ -74,6 +74,19 @@ int focr_igemm_s4s8_packed(const int8_t *a, size_t a_len, const uint8_t *b_packe
                            size_t group, size_t m, size_t k, size_t n, float *out,
                            size_t out_len, int mem, void *stream);
 
+/* Status of the tensor-core igemm on the current device: *word receives the
+ * OR of the error bits its launches recorded since the last clear (4 = a
+ * bounded device-side wait expired, so some output tile is incomplete); 0 when
+ * none.  clear != 0 resets it.  Host-mode igemm calls check it themselves and
+ * return FOCR_E_TIMEOUT; device-mode callers call this after synchronising
+ * their stream.  No counterpart in the reference (its CPU kernels cannot time
+ * out); the Rust shim maps FOCR_E_TIMEOUT to a panic like any other error. */
+int focr_igemm_status(int *word, int clear);
+
+/* FOCR_OK when `word` (from focr_igemm_status) is 0, else FOCR_E_TIMEOUT with
+ * focr_last_error() describing it.  Pure host logic. */
+int focr_status_check(int word);
+
 /* Per-row dynamic symmetric int8 quantisation: scale[r] = max|x[r,:]|/127
  * (1.0 if 0), xq = clamp(round(x * (1/scale)), +-127).  ties_even = 0 rounds
  * half away from zero (decoder.rs:1588-1597 quantize_row_i8), 1 rounds ties
@@ -93,10 +106,11 @@ int focr_gemv_i8(const float *x, size_t m, size_t k, const int8_t *w,
  * would block or is not allowed).  Same result as focr_gemv_i8; all pointers
  * are device memory on the current device, work is enqueued on `stream`.
  * Scratch is a fixed ~260 KB array inside the library (held by every GPU that
- * loads it until exit), so m*k <= 262144 and m <= 1024, otherwise
- * FOCR_E_SHAPE.  The first call on a device looks up that array's device
- * address (cudaGetSymbolAddress); make it before any stream capture.  Calls
- * share the array: calls that overlap on the GPU race. */
+ * loads it until exit), so m*k <= 262144, m <= 1024 and min(m,8)*k <= 204800,
+ * otherwise FOCR_E_SHAPE.  The first call on a device looks up that array's
+ * device address (cudaGetSymbolAddress); make it before any stream capture.
+ * The address is kept for the process's life and is not valid across
+ * cudaDeviceReset.  Calls share the array: calls that overlap on the GPU race. */
 int focr_gemv_i8_noalloc(const float *x, size_t m, size_t k, const int8_t *w,
                          const float *w_scale, size_t n, float *y, void *stream);
 

@@ -398,3 +398,19 @@ def test_decoder_model_config_must_match_the_tensors():
     focrq.write_decoder(wr, W)
     with pytest.raises(FormatMismatch, match="num_hidden_layers"):
         focrq.decoder_weights(Weights.from_bytes(wr.to_bytes()))
+
+
+def test_decoder_layer_prefix_and_heads_from_model_config():
+    """Loading a prefix of the layers is valid with a matching model_config;
+    heads come from model_config, and an explicit disagreeing value is a
+    mismatch."""
+    W = synth.decoder_model(9, layers=2, dense_inter=128, vocab=64)
+    cfg = {"hidden_size": 1280, "num_attention_heads": 10, "num_hidden_layers": 2,
+           "vocab_size": 64}
+    wr = focrq.Writer(model_config=cfg)
+    focrq.write_decoder(wr, W)
+    w = Weights.from_bytes(wr.to_bytes())
+    D = focrq.decoder_weights(w, n_layers=1)
+    assert len(D.layers) == 1 and D.heads == 10
+    with pytest.raises(FormatMismatch, match="num_attention_heads"):
+        focrq.decoder_weights(w, heads=5)

@@ -124,3 +124,14 @@ def test_zipf_routing_is_skewed_and_distinct():
     top = np.sort(counts)[::-1]
     assert top[0] > 4 * max(top[-8:].mean(), 1)   # heavy head, light tail
     assert np.allclose(w.sum(1), 1.0, atol=1e-5) and (np.diff(w, axis=1) <= 0).all()
+
+
+def test_status_word_check_reports_injected_expiry():
+    """A status word with the expired-wait bit (injected on the host) maps to
+    FOCR_E_TIMEOUT with a message; 0 maps to success.  Pure host logic."""
+    from franken_ocr_b200._lib import FOCR_E_TIMEOUT, FOCR_OK, lib
+
+    assert lib.focr_status_check(0) == FOCR_OK
+    assert lib.focr_status_check(4) == FOCR_E_TIMEOUT
+    msg = lib.focr_last_error().decode()
+    assert "bounded device-side wait expired" in msg and "0x4" in msg

@@ -29,9 +29,12 @@ def test_gemv_noalloc_matches_allocating_entry_point(cuda):
 
     stream = torch.cuda.current_stream().cuda_stream
     g = torch.Generator(device="cuda").manual_seed(2024)
-    # two calls in a row with different shapes: the second reuses (and must
-    # fully overwrite) the scratch the first one left behind
-    for (m, k, n) in [(8, 1280, 1792), (3, 896, 1280)]:
+    # calls in a row with different shapes: each reuses (and must fully
+    # overwrite) the scratch the previous one left behind.  m = 1 is the decode
+    # row (the fused in-kernel-quantising GEMV on both entry points), m = 9
+    # spans two eight-row GEMV chunks, m = 1024 fills the scratch exactly.
+    for (m, k, n) in [(8, 1280, 1792), (3, 896, 1280), (1, 1280, 1792), (9, 896, 1280),
+                      (1024, 256, 64), (2, 1280, 1792)]:
         x = torch.randn((m, k), device="cuda", generator=g)
         w = torch.randint(-127, 128, (n, k), dtype=torch.int8, device="cuda", generator=g)
         ws = torch.rand(n, device="cuda", generator=g) * 0.02 + 0.001
@@ -57,3 +60,11 @@ def test_gemv_noalloc_rejects_oversize(cuda):
     rc = _run(lib, "focr_gemv_i8_noalloc", x, w, ws, y, torch.cuda.current_stream().cuda_stream)
     assert rc == FOCR_E_SHAPE
     assert b"262144" in lib.focr_last_error()
+    # one row within the scratch but wider than the GEMV's shared-memory stage
+    x1 = torch.zeros((1, 262144), device="cuda")
+    w1 = torch.zeros((4, 262144), dtype=torch.int8, device="cuda")
+    y1 = torch.empty((1, 4), device="cuda")
+    rc = _run(lib, "focr_gemv_i8_noalloc", x1, w1, torch.ones(4, device="cuda"), y1,
+              torch.cuda.current_stream().cuda_stream)
+    assert rc == FOCR_E_SHAPE
+    assert b"204800" in lib.focr_last_error()
