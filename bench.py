@@ -688,6 +688,9 @@ def config3(args, dev, prefill=1024, n_tokens=256, seed=3):
 
     for _ in range(max(3, args.warmup)):
         toks0, _, _ = run()
+    golden = json.loads((ROOT / "tests" / "golden" / "decoder_config3_greedy256.json").read_text())
+    assert (golden["seed"], golden["prefill_tokens"], golden["n_tokens"]) == (seed, prefill, n_tokens)
+    assert toks0 == golden["tokens"], "greedy tokens differ from the CPU oracle's"
     clocks = Clocks(dev.index or 0)
     clocks.start()
     pre, dec = [], []
@@ -724,7 +727,8 @@ def config3(args, dev, prefill=1024, n_tokens=256, seed=3):
         "e2e": {"value": n_tokens / (e2e_ms / 1e3), "unit": "tokens/s (prefill included)",
                 "h2d_bytes_per_step": prefill * W.hidden * 4, "d2h_bytes_per_step": n_tokens * 4},
         "roofline": roof, "gpu_launches": launches,
-        "cpu_baseline": cpu, "clocks": clk, "tokens_head": toks0[:16]}), flush=True)
+        "cpu_baseline": cpu, "clocks": clk, "tokens_head": toks0[:16],
+        "parity": "all 256 greedy tokens equal the CPU oracle's (tests/golden)"}), flush=True)
     D.close()
 
 
