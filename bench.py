@@ -434,21 +434,31 @@ def capture(step, idxs):
 
 def run_ep(args, ws, rank, local):
     """N > 1: expert parallel, 64 tokens per GPU (weak scaling), each GPU
-    owning 64/N routed experts and a replica of the shared expert; NCCL
-    all-to-all dispatch / return (franken_ocr_b200/ep.py)."""
+    owning 64/N routed experts and a replica of the router and the shared
+    expert.  The library's data plane (focr_ep_*): routed int8 rows written
+    into the owners' staging buffers over NVLink, partials written back by
+    the owners' down GEMM epilogue, slot-ordered combine at the source; NCCL
+    (focr_comm) bootstraps the peer mappings."""
     import torch
     import torch.distributed as dist
 
     from franken_ocr_b200 import synth
-    from franken_ocr_b200.ep import EpMoeRank
+    from franken_ocr_b200.ep import Comm, EpMoe, nccl_unique_id
+    from franken_ocr_b200.moe import MoeLayer
 
     dev = torch.device("cuda", local)
     hbm_peak, peak_kind = peaks()
     e_local = NEXP // ws
     R = 2
-    layers = [EpMoeRank(synth.moe_layer(100 + r, shared_inter=SHARED, expert_begin=rank * e_local,
-                                        expert_count=e_local), rank, ws, TOKENS)
-              for r in range(R)]
+    obj = [nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    comm = Comm(obj[0], rank, ws)
+    layers = []
+    for r in range(R):
+        L = EpMoe(synth.moe_layer(100 + r, shared_inter=SHARED, expert_begin=rank * e_local,
+                                  expert_count=e_local), rank, ws, TOKENS)
+        L.connect_comm(comm)
+        layers.append(L)
     n = args.steps + args.warmup
     seed = 7 + 1000 * rank
     xs = [synth.hidden_states(seed, TOKENS, idx=i) for i in range(n)]
@@ -460,7 +470,16 @@ def run_ep(args, ws, rank, local):
     def step(i):
         return layers[i % R].forward(xd[i], idd[i], wd[i])
 
-    for i in range(args.warmup):
+    # parity: the first step's output equals the single-GPU layer's, bit for bit
+    full = MoeLayer(synth.moe_layer(100, shared_inter=SHARED), max_tokens=TOKENS)
+    y0 = step(0).cpu().numpy()
+    want0 = full.forward(xs[0], *rts[0])
+    full.close()
+    parity = bool(np.array_equal(y0.view(np.uint32), want0.view(np.uint32)))
+    flag = torch.tensor([int(parity)], device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    parity = bool(flag.item())
+    for i in range(1, args.warmup):
         step(i)
     torch.cuda.synchronize()
     dist.barrier()
@@ -540,13 +559,16 @@ def run_ep(args, ws, rank, local):
         "e2e": {"value": args.steps * TOKENS * ws / (e2e_ms / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": TOKENS * HIDDEN * 4 + TOKENS * TOPK * 8,
                 "d2h_bytes_per_step": TOKENS * HIDDEN * 4},
-        "gpu_launches": 11 * args.steps,
+        "gpu_launches": 9 * args.steps,
+        "parity": "rank outputs bit-identical to the single-GPU layer" if parity else "MISMATCH",
+        "ep_status": max(L.status() for L in layers),
         "clocks": clk,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
     for L in layers:
         L.close()
+    comm.close()
 
 
 def cpu_baseline_config3(W, seed, prefill=32, seconds=10.0, max_steps=200):

@@ -27,13 +27,17 @@ EXPORTS = [
     "focr_last_error", "focr_tier_string", "focr_igemm_s8s8", "focr_igemm_u8s8",
     "focr_igemm_s4s8_packed", "focr_quantize_rows_i8", "focr_gemv_i8", "focr_gemv_i8_noalloc",
     "focr_moe_create", "focr_moe_destroy", "focr_moe_route", "focr_moe_forward",
-    "focr_moe_decode", "focr_moe_prefill", "focr_moe_forward_rows", "focr_moe_combine", "focr_ep_pack",
+    "focr_moe_decode", "focr_moe_prefill", "focr_moe_forward_rows", "focr_moe_combine",
     "focr_lmhead_create", "focr_lmhead_destroy", "focr_lmhead_top1",
     "focr_top1_combine", "focr_selftest", "focr_trace_set", "focr_rms_norm", "focr_rope_apply",
     "focr_attention_decode", "focr_linear_i8", "focr_swiglu", "focr_add",
     "focr_attention_prefill", "focr_rope_table", "focr_decode_prologue", "focr_rope_apply_at",
     "focr_ring_write", "focr_attention_decode_at", "focr_add_rms_norm",
     "focr_igemm_status", "focr_status_check",
+    "focr_nccl_unique_id", "focr_comm_create", "focr_comm_destroy", "focr_top1_allgather",
+    "focr_ep_create", "focr_ep_destroy", "focr_ep_ipc_handle", "focr_ep_connect",
+    "focr_ep_connect_comm", "focr_ep_connect_local", "focr_ep_forward", "focr_ep_dispatch",
+    "focr_ep_experts", "focr_ep_combine", "focr_ep_decode", "focr_ep_status",
 ]
 
 
@@ -92,7 +96,23 @@ lib.focr_moe_decode.argtypes = [vp, vp, sz, vp, vp, vp, i32, vp]
 lib.focr_moe_prefill.argtypes = [vp, vp, sz, vp, vp, vp, i32, vp]
 lib.focr_moe_combine.argtypes = [vp, vp, vp, sz, sz, sz, vp, vp]
 lib.focr_moe_forward_rows.argtypes = [vp, vp, sz, vp, vp, vp, sz, vp]
-lib.focr_ep_pack.argtypes = [vp, vp, vp, sz, sz, sz, sz, sz, sz, vp, vp, vp, vp, vp, vp, vp]
+lib.focr_nccl_unique_id.argtypes = [vp]
+lib.focr_comm_create.argtypes = [vp, C.c_uint32, C.c_uint32, C.POINTER(vp)]
+lib.focr_comm_destroy.argtypes = [vp]
+lib.focr_top1_allgather.argtypes = [vp, vp, vp, sz, vp, vp, vp]
+lib.focr_ep_create.argtypes = [C.POINTER(MoeConfig), C.POINTER(MoeWeights), C.c_uint32,
+                               C.c_uint32, C.POINTER(vp)]
+lib.focr_ep_destroy.argtypes = [vp]
+lib.focr_ep_ipc_handle.argtypes = [vp, vp]
+lib.focr_ep_connect.argtypes = [vp, vp]
+lib.focr_ep_connect_comm.argtypes = [vp, vp]
+lib.focr_ep_connect_local.argtypes = [vp, sz]
+lib.focr_ep_forward.argtypes = [vp, vp, sz, vp, vp, vp, vp]
+lib.focr_ep_dispatch.argtypes = [vp, vp, sz, vp, vp, vp]
+lib.focr_ep_experts.argtypes = [vp, vp]
+lib.focr_ep_combine.argtypes = [vp, vp, vp]
+lib.focr_ep_decode.argtypes = [vp, vp, sz, vp, vp, vp, vp]
+lib.focr_ep_status.argtypes = [vp, C.POINTER(i32)]
 lib.focr_lmhead_create.argtypes = [vp, vp, sz, sz, sz, sz, C.POINTER(vp)]
 lib.focr_lmhead_destroy.argtypes = [vp]
 lib.focr_lmhead_top1.argtypes = [vp, vp, sz, vp, vp, vp, i32, vp]

@@ -73,6 +73,35 @@ int comm_all_gather_bytes(focr_comm *c, const void *send, void *recv, size_t byt
     return FOCR_OK;
 }
 
+__global__ void top1_pack_kernel(const float *__restrict__ val, const int32_t *__restrict__ idx,
+                                 int m, uint64_t *__restrict__ out) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r < m)
+        out[r] = ((uint64_t)(uint32_t)idx[r] << 32) | (uint64_t)__float_as_uint(val[r]);
+}
+
+// argmax_row across shards in rank order: first maximum (v <= best keeps the
+// earlier shard, whose vocab range is lower), NaN and empty shards skipped,
+// all-NaN -> 0 (sampler.rs:168-186).
+__global__ void top1_combine_kernel(const uint64_t *__restrict__ all, int world, int m,
+                                    uint32_t *__restrict__ token, float *__restrict__ token_val) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= m) return;
+    int32_t b = -1;
+    float bv = 0.0f;
+    for (int s = 0; s < world; s++) {
+        const uint64_t p = all[(size_t)s * m + r];
+        const int32_t i = (int32_t)(p >> 32);
+        const float v = __uint_as_float((uint32_t)p);
+        if (i < 0 || v != v) continue;
+        if (b >= 0 && v <= bv) continue;
+        b = i;
+        bv = v;
+    }
+    token[r] = b < 0 ? 0u : (uint32_t)b;
+    if (token_val) token_val[r] = b < 0 ? __int_as_float(0x7fc00000) : bv;
+}
+
 }  // namespace focr
 
 using namespace focr;
@@ -113,8 +142,37 @@ int focr_comm_create(const void *nccl_id, uint32_t rank, uint32_t world, focr_co
     return FOCR_OK;
 }
 
+int focr_top1_allgather(focr_comm *c, const float *best_val, const int32_t *best_idx, size_t m,
+                        uint32_t *token, float *token_val, void *stream) {
+    if (!c) return fail(FOCR_E_ARG, "top1_allgather: null communicator");
+    if (m == 0) return FOCR_OK;
+    if (!best_val || !best_idx || !token) return fail(FOCR_E_ARG, "top1_allgather: null pointer");
+    if (m > (1u << 24)) return fail(FOCR_E_UNSUPPORTED, "top1_allgather: m too large");
+    cudaStream_t st = (cudaStream_t)stream;
+    if (m > c->top1_rows) {
+        cudaFree(c->top1_send);
+        cudaFree(c->top1_recv);
+        c->top1_send = c->top1_recv = nullptr;
+        c->top1_rows = 0;
+        cudaError_t e = cudaMalloc(&c->top1_send, m * 8);
+        if (e == cudaSuccess) e = cudaMalloc(&c->top1_recv, m * 8 * c->world);
+        if (e != cudaSuccess) return fail(FOCR_E_ALLOC, "top1_allgather: cudaMalloc failed");
+        c->top1_rows = m;
+    }
+    const unsigned g = (unsigned)((m + 255) / 256);
+    top1_pack_kernel<<<g, 256, 0, st>>>(best_val, best_idx, (int)m, c->top1_send);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    int rc = comm_all_gather_bytes(c, c->top1_send, c->top1_recv, m * 8, st);
+    if (rc) return rc;
+    top1_combine_kernel<<<g, 256, 0, st>>>(c->top1_recv, (int)c->world, (int)m, token, token_val);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    return FOCR_OK;
+}
+
 int focr_comm_destroy(focr_comm *c) {
     if (!c) return FOCR_OK;
+    cudaFree(c->top1_send);
+    cudaFree(c->top1_recv);
     CommImpl *impl = static_cast<CommImpl *>(c->impl);
     if (impl && impl->comm) nccl().comm_destroy(impl->comm);
     delete impl;

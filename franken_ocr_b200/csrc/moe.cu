@@ -490,10 +490,15 @@ void launch_act_quant(focr_moe_layer *L, int m, int sh0, cudaStream_t st, bool t
 
 int moe_route_dev(focr_moe_layer *L, const float *x, int m, int32_t *idx, float *w,
                   cudaStream_t st) {
+    return moe_route_topk(L, x, m, (int)L->cfg.topk, idx, w, st);
+}
+
+int moe_route_topk(focr_moe_layer *L, const float *x, int m, int topk, int32_t *idx, float *w,
+                   cudaStream_t st) {
     const int E = L->cfg.n_experts, H = L->cfg.hidden;
     dim3 g1((E + 7) / 8, m);
     router_logits_kernel<<<g1, 256, 0, st>>>(x, L->router, H, E, L->logits);
-    topk_kernel<<<m, 32, 0, st>>>(L->logits, E, L->cfg.topk, L->cfg.norm_topk_prob,
+    topk_kernel<<<m, 32, 0, st>>>(L->logits, E, topk, L->cfg.norm_topk_prob,
                                   L->cfg.routed_scaling_factor, idx, w, L->err);
     FOCR_CUDA_TRY(cudaGetLastError());
     return FOCR_OK;

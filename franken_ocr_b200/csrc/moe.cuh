@@ -53,6 +53,10 @@ namespace focr {
 
 int moe_route_dev(focr_moe_layer *L, const float *x, int m, int32_t *idx, float *w,
                   cudaStream_t st);
+// Router with an explicit top-k (the expert-parallel layer keeps one slot per
+// row internally but routes with the model's top-k); m <= max_tokens.
+int moe_route_topk(focr_moe_layer *L, const float *x, int m, int topk, int32_t *idx, float *w,
+                   cudaStream_t st);
 // prefill: moe_block_i8 semantics (decoder.rs:2142-2181) -- ties-even
 // activation quantisation and each token's partials summed in ascending
 // expert order; otherwise decode_mlp_i8's (half-away quantisation, slot order)
@@ -67,6 +71,18 @@ int moe_tc_setup(focr_moe_layer *L);
 void moe_tc_free(focr_moe_layer *L);
 int moe_tc_experts(focr_moe_layer *L, const float *x, int m, const int32_t *idx, const float *w,
                    int sh0, cudaStream_t st, bool te = false);
+// Expert-parallel return targets of the down GEMM: back[s] is rank s's
+// return buffer mapped on this device ([world][cap][hidden] f32).
+struct EpReturn {
+    float *back[8];
+    int world, cap, rank;
+};
+// The three tensor-core launches (gate+up, requantisation, down) over pairs
+// already bucketed into the layer's sorted buffers (offsets, active list,
+// pair_tok/slot, xq_sorted, xs_sorted, sched zeroed).  ret != nullptr sends
+// every routed partial to its source rank (see MoeDown).
+int moe_tc_gemms(focr_moe_layer *L, int m, const float *w, int sh0, cudaStream_t st, bool te,
+                 const EpReturn *ret);
 void launch_act_quant(focr_moe_layer *L, int m, int sh0, cudaStream_t st, bool te = false);
 
 }  // namespace focr

@@ -279,6 +279,13 @@ struct MoeDown {
     const float *down_s, *sh_down_s, *as2, *sh_as, *w;
     float *part, *sh_y;
     int *err;
+    // Expert-parallel return (peer_back[0] != nullptr): a routed pair's row r
+    // = s * ep_cap + pos (received from rank s at position pos) is written
+    // straight into rank s's return buffer, row ep_rank * ep_cap + pos, over
+    // NVLink (peer_back[s] is that buffer mapped on this device); part is
+    // unused.  topk is 1 in this mode (pair_slot 0).
+    float *peer_back[8];
+    int ep_cap, ep_rank;
 
     __device__ void prefetch() const {
         tc::prefetch_tmap(&td);
@@ -350,30 +357,33 @@ struct MoeDown {
             // per-column pair data: one load per lane, broadcast by shuffle
             // (keeps global-load latency out of the column loop)
             float my_as = 0.0f, my_w = 0.0f;
-            int my_dst = 0;
+            float *my_row = nullptr;   // this column's output row (local or a peer's)
             if (lane < lim) {
                 const int p = jb.t2 + c0 + lane;
                 if (routed) {
                     const int slot_row = pair_tok[p] * topk + pair_slot[p];
                     my_as = __ldcg(as2 + p);
                     my_w = w[slot_row];
-                    my_dst = slot_row;
+                    if (peer_back[0]) {
+                        const int src = slot_row / ep_cap, pos = slot_row - src * ep_cap;
+                        my_row = peer_back[src] + (size_t)(ep_rank * ep_cap + pos) * H;
+                    } else {
+                        my_row = part + (size_t)slot_row * H;
+                    }
                 } else {
                     my_as = __ldcg(sh_as + p);
-                    my_dst = p;
+                    my_row = sh_y + (size_t)p * H;
                 }
             }
 #pragma unroll
             for (int k = 0; k < 16; k++) {
                 const float as = __shfl_sync(0xffffffffu, my_as, k);
                 const float wk = __shfl_sync(0xffffffffu, my_w, k);
-                const int dst = __shfl_sync(0xffffffffu, my_dst, k);
+                float *row = reinterpret_cast<float *>(
+                    __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(my_row), k));
                 if (valid && k < lim) {
                     const float y = __fmul_rn(__fmul_rn((float)v[k], as), dsc);
-                    if (routed)
-                        part[(size_t)dst * H + c] = __fmul_rn(y, wk);
-                    else
-                        sh_y[(size_t)dst * H + c] = y;
+                    row[c] = routed ? __fmul_rn(y, wk) : y;
                 }
             }
         }
@@ -925,6 +935,9 @@ int moe_tc_setup(focr_moe_layer *L) {
     d.w = nullptr;
     d.part = L->part; d.sh_y = L->sh_y;
     d.err = L->err;
+    for (int i = 0; i < 8; i++) d.peer_back[i] = nullptr;
+    d.ep_cap = 1;
+    d.ep_rank = 0;
     const size_t nfl = 2 * (size_t)(E + 1) * MoeFusedTC::FLAG_STRIDE;
     if (cudaMalloc(&st->flags, nfl * sizeof(int)) != cudaSuccess) {
         delete st;
@@ -1002,6 +1015,15 @@ int moe_tc_experts(focr_moe_layer *L, const float *x, int m, const int32_t *idx,
         const int tiles = (int)L->E * (f.g.itiles + f.d.htiles) + (S ? f.g.stiles + f.d.htiles : 0);
         return launch_tc(f, tiles < sms ? tiles : sms, st);
     }
+    return moe_tc_gemms(L, m, w, sh0, st, te, nullptr);
+}
+
+int moe_tc_gemms(focr_moe_layer *L, int m, const float *w, int sh0, cudaStream_t st, bool te,
+                 const EpReturn *ret) {
+    MoeTcState *s = static_cast<MoeTcState *>(L->tc_state);
+    const int K = L->cfg.topk, S = L->cfg.shared_inter;
+    const int P = m * K;
+    const int sms = num_sms();
     MoeGateUp g = s->gu;
     g.T = m;
     g.sh0 = sh0;
@@ -1018,6 +1040,12 @@ int moe_tc_experts(focr_moe_layer *L, const float *x, int m, const int32_t *idx,
     d.T = m;
     d.sh0 = sh0;
     d.w = w;
+    for (int i = 0; i < 8; i++) d.peer_back[i] = nullptr;
+    if (ret) {
+        for (int i = 0; i < ret->world; i++) d.peer_back[i] = ret->back[i];
+        d.ep_cap = ret->cap;
+        d.ep_rank = ret->rank;
+    }
     tiles = (int)L->E * d.htiles + (S ? d.htiles : 0);
     return launch_tc(d, tiles < sms ? tiles : sms, st);
 }

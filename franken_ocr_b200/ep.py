@@ -1,153 +1,190 @@
-"""Expert-parallel MoE layer over N GPUs (one process per GPU).
+"""Expert-parallel MoE layer and vocab-parallel lm-head over N GPUs.
 
-The reference has no distributed code (it runs the 6 routed experts of a
-token as rayon tasks, native_engine/decoder.rs:2231-2252); this module splits
-the same computation by expert: rank r owns routed experts
-[r*E/N, (r+1)*E/N) and a replica of the fused shared expert.  One forward of
-T local tokens with given routing (idx, w of shape [T, topk]):
+Bindings of the library's multi-GPU entry points (``focr_comm_*``,
+``focr_ep_*``, ``focr_top1_allgather``).  The data plane lives in the CUDA
+library: dispatch writes each routed (token, slot) row -- int8 + scale, only
+the routed ones -- into the owning rank's staging buffer over NVLink, the
+owner's down GEMM writes each weighted partial back into the source rank's
+return buffer, and the source sums them in slot order
+(native_engine/decoder.rs:2231-2261), bit-identical to one GPU.  NCCL (loaded
+by the library) bootstraps the peer mappings and carries the lm-head's
+all-gather of per-shard top-1.
 
-1. dispatch -- focr_ep_pack places every (token, slot) pair in the block of
-   rows reserved for the rank owning its expert (fixed capacity C =
-   max_tokens*topk rows per peer, unused rows marked with expert id -1): the
-   token's f32 row plus (global expert id, routing weight).  Two equal-split
-   all-to-alls move the blocks; no host synchronisation is needed.  The
-   receiver quantises the rows itself, which reproduces the sender's
-   quantisation exactly (row quantisation is deterministic).
-2. experts -- one focr_moe_forward_rows call on the rank's layer (its expert
-   subset + the shared expert) over [N*C received pairs | T own tokens]: each
-   received pair is a one-slot row whose output is p = expert(x) * w,
-   bit-identical to the partial the single-GPU layer forms
-   (decoder.rs:2236-2247); the own tokens (ids -1) get the shared expert.
-3. return -- the partials travel back by the reverse all-to-all and
-   focr_moe_combine gathers them per (token, slot) and forms
-   ((0 + p_0) + ... + p_{k-1}) + s (decoder.rs:2253-2261).
+The reference is single-process; these classes have no counterpart there.
 """
 from __future__ import annotations
 
+import ctypes as C
+
 import numpy as np
 
-from ._lib import check, lib
-from .moe import MoeLayer
+from ._lib import MoeConfig, MoeWeights, check, lib
 from .synth import MoeWeightsHost
 
 
+def _stream():
+    import torch
+
+    return torch.cuda.current_stream().cuda_stream
+
+
+def nccl_unique_id() -> bytes:
+    buf = C.create_string_buffer(128)
+    check(lib.focr_nccl_unique_id(buf))
+    return buf.raw
+
+
+class Comm:
+    """One rank of a communicator (collective create: every rank at once)."""
+
+    def __init__(self, uid: bytes, rank: int, world: int):
+        if len(uid) != 128:
+            raise ValueError("the NCCL unique id is 128 bytes")
+        self.rank, self.world = rank, world
+        h = C.c_void_p()
+        check(lib.focr_comm_create(C.c_char_p(uid), rank, world, C.byref(h)))
+        self._h = h
+
+    @property
+    def handle(self):
+        return self._h
+
+    def top1_allgather(self, best_val, best_idx):
+        """Per-shard top-1 (device tensors [m]) -> (token u32 as int64 tensor,
+        value) of the whole vocab on every rank."""
+        import torch
+
+        m = best_val.shape[0]
+        tok = torch.empty(m, dtype=torch.int32, device=best_val.device)
+        val = torch.empty(m, dtype=torch.float32, device=best_val.device)
+        check(lib.focr_top1_allgather(self._h, best_val.data_ptr(), best_idx.data_ptr(), m,
+                                      tok.data_ptr(), val.data_ptr(), _stream()))
+        return tok.to(torch.int64) & 0xFFFFFFFF, val
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib.focr_comm_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+
 def rank_weights(W: MoeWeightsHost, rank: int, world: int) -> MoeWeightsHost:
-    """Rank's slice of W's routed experts + W's shared expert, as a one-slot
-    layer (each received pair is a row with one routed expert)."""
+    """Rank's slice of W's routed experts + the router and the shared expert."""
     if W.n_experts % world:
         raise ValueError(f"{W.n_experts} experts do not split over {world} ranks")
     e = W.n_experts // world
     b = rank * e - W.expert_begin
     if b < 0 or b + e > W.expert_count:
         raise ValueError("weights do not hold this rank's experts")
-    out = MoeWeightsHost(W.hidden, W.inter, W.n_experts, 1, W.shared_inter, rank * e, e, W.group)
+    out = MoeWeightsHost(W.hidden, W.inter, W.n_experts, W.topk, W.shared_inter, rank * e, e,
+                         W.group)
     out.router = W.router
     for k, v in W.arrays.items():
         out.arrays[k] = v if k.startswith("sh_") else np.ascontiguousarray(v[b:b + e])
     return out
 
 
-class EpMoeRank:
-    """One rank of an expert-parallel MoE layer (device tensors, torch)."""
+class EpMoe:
+    """Rank `rank` of an expert-parallel MoE layer (focr_ep_*).  ``W`` holds at
+    least this rank's experts (a full layer is sliced)."""
 
-    def __init__(self, W: MoeWeightsHost, rank: int, world: int, max_tokens: int):
-        import torch
-
-        self.rank, self.world = rank, world
+    def __init__(self, W: MoeWeightsHost, rank: int, world: int, max_tokens: int,
+                 norm_topk_prob: bool = True, routed_scaling_factor: float = 1.0):
+        if W.expert_count != W.n_experts // world or W.expert_begin != rank * (W.n_experts // world):
+            W = rank_weights(W, rank, world)
+        self.rank, self.world, self.max_tokens = rank, world, max_tokens
         self.hidden, self.topk = W.hidden, W.topk
-        self.e_local = W.n_experts // world
-        self.max_tokens = max_tokens
-        self.cap = max_tokens * W.topk        # rows reserved per peer
-        self.layer = MoeLayer(rank_weights(W, rank, world),
-                              max_tokens=world * self.cap + max_tokens)
-        dev = torch.device("cuda", torch.cuda.current_device())
-        n = world * self.cap
-        self.send_x = torch.empty((n, self.hidden), dtype=torch.float32, device=dev)
-        self.send_meta = torch.empty((n, 2), dtype=torch.int32, device=dev)
-        self.recv_x = torch.empty((n + max_tokens, self.hidden), dtype=torch.float32, device=dev)
-        self.recv_meta = torch.empty((n + max_tokens, 2), dtype=torch.int32, device=dev)
-        self.rows = torch.empty(max_tokens * self.topk, dtype=torch.int32, device=dev)
-        self.out = torch.empty((n + max_tokens, self.hidden), dtype=torch.float32, device=dev)
-        self.back = torch.empty((n, self.hidden), dtype=torch.float32, device=dev)
-        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        cfg = MoeConfig(W.hidden, W.inter, W.n_experts, W.topk, W.shared_inter,
+                        int(norm_topk_prob), float(routed_scaling_factor), W.group,
+                        W.expert_begin, W.expert_count, max_tokens)
+        wt = MoeWeights()
+        keep = [np.ascontiguousarray(W.router, dtype=np.float32)]
+        wt.router = keep[0].ctypes.data
+        for name, arr in W.arrays.items():
+            setattr(wt, name, arr.ctypes.data)
+            keep.append(arr)
+        h = C.c_void_p()
+        check(lib.focr_ep_create(C.byref(cfg), C.byref(wt), rank, world, C.byref(h)))
+        self._h = h
+        del keep
 
-    def _stream(self):
+    @property
+    def handle(self):
+        return self._h
+
+    def ipc_handle(self) -> bytes:
+        buf = C.create_string_buffer(64)
+        check(lib.focr_ep_ipc_handle(self._h, buf))
+        return buf.raw
+
+    def connect(self, handles: list[bytes]):
+        blob = b"".join(handles)
+        check(lib.focr_ep_connect(self._h, C.c_char_p(blob)))
+
+    def connect_comm(self, comm: Comm):
+        check(lib.focr_ep_connect_comm(self._h, comm.handle))
+
+    @staticmethod
+    def connect_local(ranks: list["EpMoe"]):
+        arr = (C.c_void_p * len(ranks))(*[r.handle.value for r in ranks])
+        check(lib.focr_ep_connect_local(arr, len(ranks)))
+
+    def forward(self, x, idx, w, y=None):
         import torch
 
-        return torch.cuda.current_stream().cuda_stream
-
-    def pack(self, x, idx, w):
         T = x.shape[0]
-        if T > self.max_tokens:
-            raise ValueError(f"{T} tokens > max_tokens {self.max_tokens}")
-        check(lib.focr_ep_pack(x.data_ptr(), idx.data_ptr(), w.data_ptr(), T, self.topk,
-                               self.hidden, self.e_local, self.world, self.cap,
-                               self.send_x.data_ptr(), self.send_meta.data_ptr(),
-                               self.recv_x.data_ptr(), self.recv_meta.data_ptr(),
-                               self.rows.data_ptr(), self.status.data_ptr(), self._stream()))
-
-    def experts(self, T):
-        """Forward over [received pairs | own tokens] (recv buffers filled)."""
-        import torch
-
-        n = self.world * self.cap
-        m = n + T
-        ridx = self.recv_meta[:m, 0:1].contiguous()
-        rw = self.recv_meta[:m, 1:2].contiguous().view(torch.float32)
-        return self.layer.forward_rows(self.recv_x[:m], ridx, rw, n, self.out[:m])
-
-    def combine(self, T, back):
-        import torch
-
-        n = self.world * self.cap
-        y = torch.empty((T, self.hidden), dtype=torch.float32, device=back.device)
-        check(lib.focr_moe_combine(back.data_ptr(), self.rows.data_ptr(),
-                                   self.out[n:].data_ptr(), T, self.topk, self.hidden,
-                                   y.data_ptr(), self._stream()))
+        y = torch.empty((T, self.hidden), dtype=torch.float32, device=x.device) if y is None else y
+        check(lib.focr_ep_forward(self._h, x.data_ptr(), T, idx.data_ptr(), w.data_ptr(),
+                                  y.data_ptr(), _stream()))
         return y
 
-    def forward(self, x, idx, w, group=None):
-        """Distributed forward over torch.distributed (NCCL) for this rank."""
-        import torch.distributed as dist
+    def decode(self, x, y=None):
+        import torch
 
         T = x.shape[0]
-        n = self.world * self.cap
-        self.pack(x, idx, w)
-        if self.world == 1:
-            self.recv_x[:n].copy_(self.send_x)
-            self.recv_meta[:n].copy_(self.send_meta)
-        else:
-            dist.all_to_all_single(self.recv_x[:n], self.send_x, group=group)
-            dist.all_to_all_single(self.recv_meta[:n], self.send_meta, group=group)
-        self.experts(T)
-        if self.world == 1:
-            back = self.out[:n]
-        else:
-            dist.all_to_all_single(self.back, self.out[:n], group=group)
-            back = self.back
-        return self.combine(T, back)
+        y = torch.empty((T, self.hidden), dtype=torch.float32, device=x.device) if y is None else y
+        idx = torch.empty((T, self.topk), dtype=torch.int32, device=x.device)
+        w = torch.empty((T, self.topk), dtype=torch.float32, device=x.device)
+        check(lib.focr_ep_decode(self._h, x.data_ptr(), T, y.data_ptr(), idx.data_ptr(),
+                                 w.data_ptr(), _stream()))
+        return y, idx, w
+
+    def dispatch(self, x, idx, w):
+        check(lib.focr_ep_dispatch(self._h, x.data_ptr(), x.shape[0], idx.data_ptr(),
+                                   w.data_ptr(), _stream()))
+
+    def experts(self):
+        check(lib.focr_ep_experts(self._h, _stream()))
+
+    def combine(self, y):
+        check(lib.focr_ep_combine(self._h, y.data_ptr(), _stream()))
+        return y
+
+    def status(self) -> int:
+        word = C.c_int(0)
+        check(lib.focr_ep_status(self._h, C.byref(word)))
+        return word.value
 
     def close(self):
-        self.layer.close()
+        if getattr(self, "_h", None):
+            lib.focr_ep_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
 
 
-def emulated_forward(ranks, xs, idxs, ws):
-    """Run the expert-parallel forward of len(ranks) ranks on one device,
-    doing the equal-split all-to-alls by slicing (the exchange under test)."""
+def emulated_forward(ranks: list[EpMoe], xs, idxs, ws):
+    """Run `len(ranks)` ranks that share one GPU, phase by phase on one stream
+    (every wait is satisfied by an earlier launch): all dispatches, then all
+    expert phases, then all combines."""
     import torch
 
-    N = len(ranks)
-    C = ranks[0].cap
     for r, x, i, w in zip(ranks, xs, idxs, ws):
-        r.pack(x, i, w)
-    for d in range(N):
-        ranks[d].recv_x[:N * C] = torch.cat([ranks[s].send_x[d * C:(d + 1) * C] for s in range(N)])
-        ranks[d].recv_meta[:N * C] = torch.cat([ranks[s].send_meta[d * C:(d + 1) * C]
-                                                for s in range(N)])
-    for d in range(N):
-        ranks[d].experts(xs[d].shape[0])
-    ys = []
-    for s in range(N):
-        back = torch.cat([ranks[d].out[s * C:(s + 1) * C] for d in range(N)])
-        ys.append(ranks[s].combine(xs[s].shape[0], back))
-    return ys
+        r.dispatch(x, i, w)
+    for r in ranks:
+        r.experts()
+    return [r.combine(torch.empty((x.shape[0], r.hidden), dtype=torch.float32, device=x.device))
+            for r, x in zip(ranks, xs)]

@@ -200,19 +200,80 @@ int focr_moe_forward_rows(focr_moe_layer *layer, const float *x, size_t m,
 int focr_moe_combine(const float *part, const int32_t *rows, const float *shared, size_t m,
                      size_t topk, size_t hidden, float *y, void *stream);
 
-/* Expert-parallel dispatch packing (no counterpart in the single-process
- * reference).  For T tokens x [T][hidden] with routing idx/w [T][topk]:
- * pair p = t*topk + j goes to rank dest = idx[p] / experts_per_rank, into
- * row dest*cap + (number of earlier pairs with that dest) of send_x
- * [world*cap][hidden] / send_meta [world*cap][2] = {expert id, weight bits};
- * other send_meta rows get id -1.  rows[p] receives that row.  The tokens
- * themselves are copied to rows [world*cap, world*cap + T) of recv_x /
- * recv_meta (id -1).  status bit 2 is set for an out-of-range expert id.
- * Device pointers; enqueued on `stream`. */
-int focr_ep_pack(const float *x, const int32_t *idx, const float *w, size_t T, size_t topk,
-                 size_t hidden, size_t experts_per_rank, size_t world, size_t cap,
-                 float *send_x, int32_t *send_meta, float *recv_x, int32_t *recv_meta,
-                 int32_t *rows, int32_t *status, void *stream);
+/* ---- multi-GPU: communicator, expert parallel, vocab parallel ----------
+ * None of this has a counterpart in the reference, which is single-process
+ * (it runs a token's experts as rayon tasks, decoder.rs:2231-2252, and its
+ * vocab tiles as tasks of one process, decoder.rs:1851-1927).  One process
+ * (or thread) per GPU, all on one node. */
+
+typedef struct focr_comm focr_comm;
+
+/* Writes a fresh 128-byte NCCL unique id (rank 0 creates it and hands it to
+ * the other ranks by any host channel).  NCCL is loaded at run time
+ * (libnccl.so.2); FOCR_E_UNSUPPORTED when it cannot be. */
+int focr_nccl_unique_id(void *id128);
+/* Collective: every rank calls it with the same id, its rank and world
+ * (<= 8), with its GPU current. */
+int focr_comm_create(const void *id128, uint32_t rank, uint32_t world, focr_comm **out);
+int focr_comm_destroy(focr_comm *comm);
+
+/* Vocab-parallel lm-head step (decoder.rs:1851-1927 vocab tiles turned into
+ * one shard per rank; sampler.rs:168-186 argmax_row): each rank passes its
+ * shard's top-1 (best_val[m], best_idx[m] global, from focr_lmhead_top1 in
+ * device mode); an NCCL all-gather of the m (value, index) pairs, then on
+ * device the first maximum in rank order (rank r holds a lower vocab range
+ * than rank r+1), NaN and -1 skipped, all-NaN -> 0.  token[m] (u32) and
+ * token_val[m] (may be NULL) on every rank.  Device pointers; collective.
+ * The first call (and any call with a larger m) allocates exchange buffers,
+ * so make it before any stream capture. */
+int focr_top1_allgather(focr_comm *comm, const float *best_val, const int32_t *best_idx,
+                        size_t m, uint32_t *token, float *token_val, void *stream);
+
+typedef struct focr_ep focr_ep;
+
+/* Rank `rank` of an expert-parallel MoE layer over `world` GPUs: cfg is the
+ * model's layer config with expert_begin = rank*n_experts/world,
+ * expert_count = n_experts/world and max_tokens = tokens per rank per step;
+ * w holds those experts (arrays start at expert_begin), the full router and
+ * the shared expert.  int8 experts, hidden/inter/shared_inter multiples of
+ * 128, world*max_tokens*topk <= 8192.  Allocates the rank's exchange region
+ * (staging for received rows, return buffer for this rank's partials). */
+int focr_ep_create(const focr_moe_config *cfg, const focr_moe_weights *w, uint32_t rank,
+                   uint32_t world, focr_ep **out);
+int focr_ep_destroy(focr_ep *ep);
+/* The CUDA IPC handle (64 bytes) of this rank's exchange region. */
+int focr_ep_ipc_handle(focr_ep *ep, void *handle64);
+/* Maps every other rank's region: handles = world x 64 bytes in rank order
+ * (this rank's entry is ignored).  Or let the communicator exchange them
+ * (focr_ep_connect_comm, collective), or, for ranks that live in one process
+ * (on one or several GPUs), connect them directly (focr_ep_connect_local). */
+int focr_ep_connect(focr_ep *ep, const void *handles);
+int focr_ep_connect_comm(focr_ep *ep, focr_comm *comm);
+int focr_ep_connect_local(focr_ep *const *eps, size_t world);
+
+/* One expert-parallel forward of this rank's T <= max_tokens tokens with
+ * given routing (idx/w [T][topk], global expert ids, < 0 = empty slot):
+ * y[T][hidden] equals the single-GPU focr_moe_forward bit for bit.  Device
+ * pointers, enqueued on `stream`; every rank must make the same sequence of
+ * calls (the ranks wait for each other on the GPU, each wait bounded by 2 s
+ * of global time; an expired wait sets bit 8 of focr_ep_status).  The three
+ * phases may also be issued separately -- dispatch (rows to their owners),
+ * experts (this rank's experts over what it received; partials back to
+ * their sources), combine (slot-ordered sum) -- e.g. to drive ranks that
+ * share one GPU phase by phase from one stream. */
+int focr_ep_forward(focr_ep *ep, const float *x, size_t T, const int32_t *idx, const float *w,
+                    float *y, void *stream);
+int focr_ep_dispatch(focr_ep *ep, const float *x, size_t T, const int32_t *idx, const float *w,
+                     void *stream);
+int focr_ep_experts(focr_ep *ep, void *stream);
+int focr_ep_combine(focr_ep *ep, float *y, void *stream);
+/* Route (moe::route with the model's top-k, on this rank's router replica)
+ * then focr_ep_forward.  idx/w outputs may be NULL. */
+int focr_ep_decode(focr_ep *ep, const float *x, size_t T, float *y, int32_t *idx, float *w,
+                   void *stream);
+/* Synchronises the device, returns and clears the rank's status word (2: a
+ * routed expert id out of range, 8: a cross-GPU wait expired). */
+int focr_ep_status(focr_ep *ep, int *word);
 
 /* ---- lm-head (decoder.rs:2275-2296, 1851-1927; sampler.rs:168-186) ---- */
 

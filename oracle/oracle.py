@@ -471,3 +471,23 @@ class DecoderOracle:
                 break
             h = self.decode_step(self.W.embed[tok], seq + i)
         return np.array(out, np.int64)
+
+
+def ep_dispatch_layout(idx, e_local, world, cap):
+    """Host restatement of the expert-parallel dispatch layout (the library's
+    ep_dispatch_kernel): pair b = t*topk + j with expert e >= 0 goes to owner
+    d = e // e_local, at position pos = number of earlier pairs (in b order)
+    with the same owner; its partial comes back to return row d*cap + pos.
+    Returns (rows [P] (-1 = empty slot), per-owner lists of (pos, b))."""
+    flat = np.asarray(idx, np.int64).reshape(-1)
+    rows = np.full(flat.size, -1, np.int64)
+    sends = [[] for _ in range(world)]
+    for b, e in enumerate(flat):
+        if e < 0:
+            continue
+        d = int(e) // e_local
+        pos = len(sends[d])
+        assert pos < cap
+        sends[d].append((pos, b))
+        rows[b] = d * cap + pos
+    return rows, sends
