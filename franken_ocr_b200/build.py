@@ -44,7 +44,7 @@ def nvcc() -> str:
 
 def _compile(src: Path, verbose: bool) -> Path:
     obj = OBJ / (src.stem + ".o")
-    deps = [src] + sorted(CSRC.glob("*.cuh")) + [ROOT / "include" / "focr_cuda.h"]
+    deps = [src] + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + [ROOT / "include" / "focr_cuda.h"]
     if obj.exists() and obj.stat().st_mtime >= max(d.stat().st_mtime for d in deps):
         return obj
     cmd = [nvcc(), *ARCH, *NVCC_FLAGS, "-c", str(src), "-o", str(obj)]

@@ -14,6 +14,7 @@
 #include <string>
 
 #include "../../include/focr_cuda.h"
+#include "libm_expf.h"
 
 namespace focr {
 
@@ -77,11 +78,8 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 
 // ---- device numerics -----------------------------------------------------
 
-// expf with the result rounded from CUDA's double-precision exp (relative
-// error of the double result < 2^-52, so the float result is within
-// 0.5 + 2^-29 ulp).  The reference calls libm expf (f32::exp); the two differ
-// by at most one ulp on rare inputs.
-__device__ __forceinline__ float dexpf(float x) { return (float)exp((double)x); }
+// The reference's f32::exp: glibc's expf, bit for bit (libm_expf.h).
+__device__ __forceinline__ float dexpf(float x) { return libm_expf(x); }
 
 // decoder.rs:1081 silu(x) = x / (1 + e^-x)
 __device__ __forceinline__ float silu_f(float x) {

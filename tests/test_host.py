@@ -135,3 +135,53 @@ def test_status_word_check_reports_injected_expiry():
     assert lib.focr_status_check(4) == FOCR_E_TIMEOUT
     msg = lib.focr_last_error().decode()
     assert "bounded device-side wait expired" in msg and "0x4" in msg
+
+
+def test_libm_expf_table_recomputed():
+    """Entry i of the device exp's table = bits of the double nearest
+    2^(i/32), minus i << 47 (recomputed here at 60 digits)."""
+    import struct
+    from decimal import Decimal, getcontext
+
+    getcontext().prec = 60
+    txt = (ROOT / "franken_ocr_b200" / "csrc" / "libm_expf.h").read_text()
+    got = [int(v, 16) for v in re.findall(r"0x([0-9a-f]{16})ULL", txt)]
+    ln2 = Decimal(2).ln()
+    want = []
+    for i in range(32):
+        b = struct.unpack("<Q", struct.pack("<d", float((ln2 * i / 32).exp())))[0]
+        want.append((b - (i << 47)) & (2**64 - 1))
+    assert got == want
+
+
+def test_libm_expf_matches_glibc_on_every_float(tmp_path):
+    """The device exp (csrc/libm_expf.h, compiled for the host here) equals
+    this host's libm expf -- the function the reference's f32::exp calls --
+    on all 2^32 inputs."""
+    import subprocess
+
+    src = tmp_path / "t.cc"
+    src.write_text(r'''
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include "libm_expf.h"
+int main() {
+    long bad = 0;
+    #pragma omp parallel for reduction(+:bad) schedule(dynamic, 1 << 16)
+    for (long u = 0; u < (1L << 32); u++) {
+        float x; unsigned b = (unsigned)u; std::memcpy(&x, &b, 4);
+        float r = expf(x), m = libm_expf(x);
+        if (r != r && m != m) continue;
+        if (std::memcmp(&r, &m, 4)) bad++;
+    }
+    std::printf("%ld\n", bad);
+    return 0;
+}
+''')
+    exe = tmp_path / "t"
+    subprocess.run(["g++", "-O2", "-ffp-contract=off", "-fopenmp", "-I",
+                    str(ROOT / "franken_ocr_b200" / "csrc"), str(src), "-o", str(exe), "-lm"],
+                   check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout
+    assert out.strip() == "0"
