@@ -1,10 +1,10 @@
 """GPU parity of the MoE decode layer and the lm-head against the oracle.
 
 Bars (the north star's): identical top-6 expert selection, f32 outputs within
-1e-5 relative, identical greedy tokens.  The only f32 step that is not
-bit-identical by construction is exp (device: correctly rounded from double;
-oracle: libm expf), so most outputs also match bit for bit -- the tests report
-that fraction and require it to be high.
+1e-5 relative, identical greedy tokens -- and beyond them, bit-identical f32
+outputs: every f32 step follows the reference's order with separately rounded
+operations, and exp is glibc's expf on both sides, so assert_close_rel checks
+the 1e-5 bound and then requires every element to match bit for bit.
 """
 import numpy as np
 import pytest
@@ -14,7 +14,7 @@ pytestmark = pytest.mark.gpu
 RTOL = 1e-5
 
 
-def assert_close_rel(got, want, what, min_exact=0.95):
+def assert_close_rel(got, want, what):
     got = np.asarray(got, np.float32)
     want = np.asarray(want, np.float32)
     scale = np.sqrt(np.mean(want.astype(np.float64) ** 2, axis=-1, keepdims=True)) + 1e-30
@@ -57,7 +57,7 @@ def test_router_kats_on_gpu(cuda, oracle):
         rc, oi, ow = oracle.route(x, W.router, 6, norm, 1.0)
         assert rc == 0 and idx.tolist() == oi.tolist()
         assert idx[0].tolist() == [10, 11, 12, 13, 14, 15]
-        assert np.allclose(w, ow, rtol=1e-6, atol=0)
+        assert np.array_equal(w.view(np.uint32), ow.view(np.uint32))
         if norm:
             assert abs(float(w[0].sum()) - 1.0) < 1e-5
         L.close()
@@ -88,7 +88,7 @@ def test_route_matches_oracle(cuda, oracle, layer0, m):
     rc, oi, ow = oracle.route(x, layer0.router, 6, True, 1.0)
     assert rc == 0
     assert np.array_equal(idx, oi)
-    assert_close_rel(w, ow, "router weights", min_exact=0.8)
+    assert_close_rel(w, ow, "router weights")
     L.close()
 
 

@@ -27,6 +27,5 @@ def test_prefill_matches_oracle(cuda, oracle, monkeypatch, kind, m):
     rc, oy, oi, ow = MoeOracle(W).prefill(x)
     assert rc == 0
     assert np.array_equal(idx, oi)
-    # a 1-ulp router weight (device exp vs libm expf) moves one token's row
-    assert_close_rel(y, oy, f"prefill {kind} m={m}", min_exact=0.5)
+    assert_close_rel(y, oy, f"prefill {kind} m={m}")
     L.close()
