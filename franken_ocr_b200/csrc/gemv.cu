@@ -289,6 +289,11 @@ int launch_gemv_s4(const int8_t *A, const uint8_t *Bp, const float *scales, size
                    size_t M, size_t K, size_t N, float *out, const float *dequant_a,
                    cudaStream_t st) {
     if (M == 0 || N == 0) return FOCR_OK;
+    if (tc_s4_eligible(A, Bp, scales, group, M, K, N)) {
+        int *err = nullptr;
+        if (int rc = tc_status_word(&err)) return rc;
+        return launch_tc_s4(A, Bp, scales, group, M, K, N, out, dequant_a, err, st);
+    }
     FOCR_CUDA_TRY(set_max_dynamic_smem((const void *)gemv_s4_kernel, 200 * 1024));
     for (size_t m0 = 0; m0 < M; m0 += 8) {
         const int mc = (int)((M - m0) < 8 ? (M - m0) : 8);

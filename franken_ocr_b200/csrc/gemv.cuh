@@ -179,6 +179,8 @@ __global__ void gemv_s4_kernel(const int8_t *__restrict__ A, const uint8_t *__re
 // Per-device status word of the raw tcgen05 igemm (value 4: a bounded wait
 // expired): read, and optionally cleared, after the caller synchronised.
 int tc_status_read(int *word, bool clear);
+// The current device's status word (allocated on first use).
+int tc_status_word(int **out);
 // FOCR_OK for a zero status word, else FOCR_E_TIMEOUT with a message.
 int status_word_check(const char *ctx, int word);
 
@@ -196,6 +198,13 @@ int launch_quantize_rows(const float *x, size_t M, size_t K, bool te, int8_t *xq
 // 16-byte aligned x and B; returns FOCR_E_UNSUPPORTED otherwise.
 int launch_gemv_q1(const float *x, size_t K, bool te, const int8_t *B, const float *w_scale,
                    size_t N, float *y, cudaStream_t st);
+// tcgen05 path of the packed int4 GEMM (tc_s4.cu): M >= 64 (32 for groups of
+// 16), N >= 128, K % 128 == 0, 16-byte aligned operands.
+bool tc_s4_eligible(const int8_t *A, const uint8_t *Bp, const float *scales, size_t group,
+                    size_t M, size_t K, size_t N);
+int launch_tc_s4(const int8_t *A, const uint8_t *Bp, const float *scales, size_t group, size_t M,
+                 size_t K, size_t N, float *out, const float *dequant_a, int *err,
+                 cudaStream_t st);
 int launch_gemv_s4(const int8_t *A, const uint8_t *Bp, const float *scales, size_t group,
                    size_t M, size_t K, size_t N, float *out, const float *dequant_a,
                    cudaStream_t st);

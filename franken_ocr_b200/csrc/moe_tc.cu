@@ -13,6 +13,8 @@
 //   gate+up:  g = (acc_g * a_scale) * gate_s[i]; u likewise; act = silu(g)*u
 //             (decoder.rs:1621-1640, :1744-1755)
 //   down:     y = (acc * a_scale2) * down_s[c]; p = y * w   (decoder.rs:2236-2247)
+#include <string.h>
+
 #include "gemv.cuh"
 #include "moe.cuh"
 #include "tc_kernel.cuh"
@@ -55,7 +57,7 @@ struct DynIter {
 };
 
 template <class P>
-__device__ void sched_stage(const P &p, void *js) {
+__device__ void sched_stage(const P &p, void *js, int freed_count = 4) {
     SchedSmem *sm = static_cast<SchedSmem *>(js);
     for (int i = threadIdx.x; i <= p.E; i += blockDim.x) {
         sm->offsets[i] = p.offsets[i];
@@ -64,7 +66,7 @@ __device__ void sched_stage(const P &p, void *js) {
     if (threadIdx.x == 0) {
         for (int r = 0; r < RING; r++) {
             tc::mbar_init(&sm->ready[r], 1);
-            tc::mbar_init(&sm->freed[r], 4);
+            tc::mbar_init(&sm->freed[r], freed_count);
         }
         tc::fence_barrier_init();
     }
@@ -264,6 +266,13 @@ struct MoeGateUp {
     }
 };
 
+// Activation scale of a row from its |act| maximum (float bits folded with
+// atomicMax): amax/127, or 1 for an all-zero row (decoder.rs:1588-1597).
+__device__ __forceinline__ float amax_scale(const float *am) {
+    const float a = __uint_as_float(__ldcg(reinterpret_cast<const unsigned *>(am)));
+    return a > 0.0f ? __fdiv_rn(a, 127.0f) : 1.0f;
+}
+
 struct MoeDown {
     static constexpr int NA = 1, BN = 128, STAGES = 6, EPI_SMEM = 0, JOB_SMEM = MOE_JOB_SMEM;
     static constexpr int NBUF = 4;
@@ -286,6 +295,10 @@ struct MoeDown {
     // unused.  topk is 1 in this mode (pair_slot 0).
     float *peer_back[8];
     int ep_cap, ep_rank;
+    // Non-null in the fused launch with on-load requantisation: the pair's
+    // activation scale is amax/127 (1 if 0) from the gate+up epilogue's
+    // per-row |act| maximum, as act_quant_rows_kernel would have computed.
+    const float *amax_rows, *sh_amax_rows;
 
     __device__ void prefetch() const {
         tc::prefetch_tmap(&td);
@@ -362,7 +375,7 @@ struct MoeDown {
                 const int p = jb.t2 + c0 + lane;
                 if (routed) {
                     const int slot_row = pair_tok[p] * topk + pair_slot[p];
-                    my_as = __ldcg(as2 + p);
+                    my_as = amax_rows ? amax_scale(amax_rows + p) : __ldcg(as2 + p);
                     my_w = w[slot_row];
                     if (peer_back[0]) {
                         const int src = slot_row / ep_cap, pos = slot_row - src * ep_cap;
@@ -371,7 +384,7 @@ struct MoeDown {
                         my_row = part + (size_t)slot_row * H;
                     }
                 } else {
-                    my_as = __ldcg(sh_as + p);
+                    my_as = sh_amax_rows ? amax_scale(sh_amax_rows + p) : __ldcg(sh_as + p);
                     my_row = sh_y + (size_t)p * H;
                 }
             }
@@ -550,6 +563,149 @@ struct MoeFusedTC {
         if (tid == 0)
             asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(ready + ei * FLAG_STRIDE), "r"(1)
                          : "memory");
+    }
+};
+
+// ---------------------------------------------------------------------------
+// Gate+up and down in ONE persistent launch, the down B operand requantised
+// on load.
+//
+// The tile queue holds every gate+up tile (shared expert first, then the
+// routed experts, most pairs first), then every down tile (routed experts in
+// the same order, the shared expert last).  A gate+up job folds its tile's
+// per-row |act| maximum into amax (float bits, atomicMax) and, once its act
+// stores are issued, bumps its expert's job counter (release).  A down job's
+// weights stream by TMA as soon as the job is claimed; its B operand (the
+// expert's act rows, int8) is written into shared memory by XW producer
+// warps, which first wait (acquire, bounded) until every gate+up job of the
+// expert has been counted, then quantise each 16-value piece of act with the
+// row's final scale amax/127 (half away from zero, decoder.rs:1751) -- the
+// values act_quant_rows_kernel would have produced.  So there is no
+// requantisation launch and no gap between the two GEMMs: down tiles fill
+// the SMs while the last gate+up tiles drain.  Every gate+up job is claimed
+// before any down job and never waits on one, so the counters always
+// complete.
+// ---------------------------------------------------------------------------
+
+struct MoeFusedQ {
+    static constexpr int NA = 1, BN = 128, STAGES = 6, XW = 4;
+    static constexpr int EPI_SMEM = MoeGateUp::EPI_SMEM + 16 * 4 + 16;
+    static constexpr int NBUF = 4;
+    static constexpr int JOB_SMEM = MOE_JOB_SMEM;
+    static constexpr uint32_t KERNEL_ID = 6;
+    static constexpr int DOWN = 1 << 30;     // TcJob::t1 flag of a down job
+    static constexpr int FLAG_STRIDE = 32;   // one 128-byte line per counter
+    TraceBuf trace;
+    MoeGateUp g;
+    MoeDown d;
+    int *done;               // [E + 1] job counters, FLAG_STRIDE apart (E = shared), zeroed by prep
+    float *amax, *sh_amax;   // per pair / per token |act| max bits, zeroed by prep
+    int te;
+    int *sched, *err;
+
+    __device__ void prefetch() const {
+        g.prefetch();
+        d.prefetch();
+    }
+    using Iter = DynIter;
+    __device__ void load_job_state(void *js) const { sched_stage(g, js, 4 + XW); }
+    __device__ void iter_init(Iter &it, void *js) const { sched_init<MoeFusedQ>(it, js); }
+    __device__ bool iter_next(Iter &it, TcJob &jb) const { return sched_next(*this, it, jb); }
+
+    __device__ int num_tiles(const SchedSmem *sm) const {
+        return g.num_tiles(sm) + d.num_tiles(sm);
+    }
+    __device__ int down_tile(int t, const SchedSmem *sm) const {
+        const int sh = d.S ? d.htiles : 0;
+        const int routed = d.num_tiles(sm) - sh;
+        return t < routed ? t + sh : t - routed;
+    }
+    __device__ int num_chunks(int t, const SchedSmem *sm) const {
+        const int gu = g.num_tiles(sm);
+        return t < gu ? g.num_chunks(t, sm) : d.num_chunks(down_tile(t - gu, sm), sm);
+    }
+    __device__ void make_job(int t, int chunk, const SchedSmem *sm, TcJob &jb) const {
+        const int gu = g.num_tiles(sm);
+        if (t < gu) {
+            g.make_job(t, chunk, sm, jb);
+        } else {
+            d.make_job(down_tile(t - gu, sm), chunk, sm, jb);
+            jb.t1 |= DOWN;
+            jb.b = nullptr;   // B written by the producer warps
+        }
+    }
+    __device__ void before_loads(const TcJob &) const {}
+    __device__ void epilogue_done(int, int) const {}
+
+    // gate+up jobs the expert (ei == g.E: the shared expert) must complete
+    __device__ int expert_jobs(int ei) const {
+        int cnt;
+        if (ei < g.E) cnt = __ldg(g.offsets + ei + 1) - __ldg(g.offsets + ei);
+        else cnt = g.T - g.sh0;
+        return (ei < g.E ? g.itiles : g.stiles) * ((cnt + BN - 1) / BN);
+    }
+
+    __device__ void produce_b(const TcJob &jb, int kb, uint8_t *bsm, int x, int lane) const {
+        const bool routed = jb.t0 >= 0;
+        const int ei = routed ? jb.t0 : g.E;
+        if (kb == 0) {
+            if (lane == 0) {
+                const int want = expert_jobs(ei);
+                const int *f = done + ei * FLAG_STRIDE;
+                uint32_t n = 0;
+                for (;;) {
+                    int v;
+                    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+                    if (v >= want) break;
+                    if (++n > (1u << 26)) {
+                        atomicOr(err, 4);
+                        break;
+                    }
+                }
+            }
+            __syncwarp();
+            asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        }
+        const int L = routed ? g.I : g.S;
+        const float *act = routed ? g.act : g.sh_act;
+        const float *am = routed ? amax : sh_amax;
+        const int nv = jb.t3, p0 = jb.t2;
+        for (int task = x * 32 + lane; task < nv * 8; task += XW * 32) {
+            const int r = task >> 3, c = task & 7, pr = p0 + r;
+            const float sc = amax_scale(am + pr);
+            const float inv = __fdiv_rn(1.0f, sc);
+            const float4 *src =
+                reinterpret_cast<const float4 *>(act + (size_t)pr * L + kb * 128 + c * 16);
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) v[u] = __ldcg(src + u);
+            uint32_t w[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                w[u] = (uint32_t)(quant_i8(v[u].x, inv, te != 0) & 0xFF) |
+                       ((uint32_t)(quant_i8(v[u].y, inv, te != 0) & 0xFF) << 8) |
+                       ((uint32_t)(quant_i8(v[u].z, inv, te != 0) & 0xFF) << 16) |
+                       ((uint32_t)(quant_i8(v[u].w, inv, te != 0) & 0xFF) << 24);
+            *reinterpret_cast<uint4 *>(bsm + r * 128 + ((c ^ (r & 7)) << 4)) =
+                make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    }
+
+    __device__ void epilogue(const TcJob &jb, uint32_t tmem, int q, int lane, void *smem) const {
+        if (jb.t1 & DOWN) {
+            TcJob j2 = jb;
+            j2.t1 &= ~DOWN;
+            d.epilogue(j2, tmem, q, lane, smem);
+            return;
+        }
+        g.epilogue_impl<true>(jb, tmem, q, lane, smem, amax, sh_amax);
+        asm volatile("bar.sync 1, 128;" ::: "memory");   // every act store / amax fold issued
+        if (32 * q + lane == 0) {
+            __threadfence();
+            asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(
+                             done + (jb.t0 >= 0 ? jb.t0 : g.E) * FLAG_STRIDE)
+                         : "memory");
+        }
     }
 };
 
@@ -875,6 +1031,7 @@ struct MoeTcState {
     MoeGateUp gu;
     MoeDown dn;
     MoeFusedTC fu;
+    MoeFusedQ fq;
     int *flags = nullptr;    // [2 (E + 1) FLAG_STRIDE]: per-expert job counters, ready flags
     ~MoeTcState() {
         if (flags) cudaFree(flags);
@@ -938,6 +1095,7 @@ int moe_tc_setup(focr_moe_layer *L) {
     for (int i = 0; i < 8; i++) d.peer_back[i] = nullptr;
     d.ep_cap = 1;
     d.ep_rank = 0;
+    d.amax_rows = d.sh_amax_rows = nullptr;
     const size_t nfl = 2 * (size_t)(E + 1) * MoeFusedTC::FLAG_STRIDE;
     if (cudaMalloc(&st->flags, nfl * sizeof(int)) != cudaSuccess) {
         delete st;
@@ -955,6 +1113,12 @@ int moe_tc_setup(focr_moe_layer *L) {
     f.sh_as = L->sh_as;
     f.sched = L->sched;
     f.err = L->err;
+    MoeFusedQ &fq = st->fq;
+    fq.done = st->flags;
+    fq.amax = L->amax;
+    fq.sh_amax = L->sh_amax;
+    fq.sched = L->sched;
+    fq.err = L->err;
     L->tc_state = st;
     return FOCR_OK;
 }
@@ -975,7 +1139,13 @@ int moe_tc_experts(focr_moe_layer *L, const float *x, int m, const int32_t *idx,
     // FOCR_MOE_FUSED=1 selects the single persistent launch, which measured
     // slower on config 2 (the per-expert requantisation by the last gate+up
     // job serialises on one SM per expert)
-    const bool unfused = getenv("FOCR_MOE_FUSED") == nullptr;
+    // FOCR_MOE_PATH=fusedq selects the single launch with on-load
+    // requantisation (MoeFusedQ)
+    const char *path_env = getenv("FOCR_MOE_PATH");
+    const int path = (path_env && !strcmp(path_env, "fusedq")) ? 2
+                     : ((path_env && !strcmp(path_env, "fused")) || getenv("FOCR_MOE_FUSED")) ? 1
+                                                                                             : 0;
+    const bool unfused = path == 0;
     const int nflags = 2 * ((int)L->E + 1) * MoeFusedTC::FLAG_STRIDE;
     if (m <= 4096) {
         FOCR_CUDA_TRY(launch_pdl(moe_prep_kernel, dim3(m), dim3(256), 0, st, x, idx, m, H, K,
@@ -1002,6 +1172,21 @@ int moe_tc_experts(focr_moe_layer *L, const float *x, int m, const int32_t *idx,
                                                L->xq_sorted, L->xs_sorted);
     }
     const int sms = num_sms();
+    if (path == 2) {
+        MoeFusedQ f = s->fq;
+        f.g = s->gu;
+        f.g.T = m;
+        f.g.sh0 = sh0;
+        f.d = s->dn;
+        f.d.T = m;
+        f.d.sh0 = sh0;
+        f.d.w = w;
+        f.d.amax_rows = L->amax;
+        f.d.sh_amax_rows = L->sh_amax;
+        f.te = te ? 1 : 0;
+        const int tiles = (int)L->E * (f.g.itiles + f.d.htiles) + (S ? f.g.stiles + f.d.htiles : 0);
+        return launch_tc(f, tiles < sms ? tiles : sms, st);
+    }
     if (!unfused) {
         MoeFusedTC f = s->fu;
         f.g = s->gu;

@@ -186,5 +186,9 @@ __device__ __forceinline__ void tmem_ld_wait() {
 // out-of-range elements read as zero.
 int make_tmap_i8(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
                  uint32_t box_rows);
+// Host: 2-D byte tensor map, box = box_rows x box_cols bytes (box_cols % 16
+// == 0), 128-byte swizzle or none.
+int make_tmap_bytes(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
+                    uint32_t box_cols, uint32_t box_rows, bool swizzle128);
 
 }  // namespace focr

@@ -14,8 +14,7 @@
 
 namespace focr {
 
-int make_tmap_i8(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
-                 uint32_t box_rows) {
+static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
     static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     static std::once_flag once;
     std::call_once(once, [] {
@@ -26,34 +25,36 @@ int make_tmap_i8(CUtensorMap *map, const void *base, uint64_t rows, uint64_t col
             q == cudaDriverEntryPointSuccess)
             encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     });
+    return encode;
+}
+
+int make_tmap_bytes(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
+                    uint32_t box_cols, uint32_t box_rows, bool swizzle128) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tmap_encoder();
     if (!encode) return fail(FOCR_E_CUDA, "cuTensorMapEncodeTiled unavailable");
-    if (cols % 16 || (uintptr_t)base % 16 || rows == 0)
+    if (cols % 16 || (uintptr_t)base % 16 || rows == 0 || box_cols % 16)
         return fail(FOCR_E_ARG, "tensor map: base/cols must be 16-byte aligned");
     cuuint64_t dims[2] = {cols, rows};
     cuuint64_t strides[1] = {cols};
-    cuuint32_t box[2] = {128, box_rows};
+    cuuint32_t box[2] = {box_cols, box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(FOCR_E_CUDA, "cuTensorMapEncodeTiled failed");
     return FOCR_OK;
+}
+
+int make_tmap_i8(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
+                 uint32_t box_rows) {
+    return make_tmap_bytes(map, base, rows, cols, 128, box_rows, true);
 }
 
 // int32 output map for the TMA reduce-add epilogue: [rows][cols] s32, box
 // 32 x 32 (128-byte rows, 128-byte swizzle).
 static int make_tmap_out_s32(CUtensorMap *map, int32_t *base, uint64_t rows, uint64_t cols) {
-    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        cudaDriverEntryPointQueryResult q;
-        void *fn = nullptr;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    });
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tmap_encoder();
     if (!encode) return fail(FOCR_E_CUDA, "cuTensorMapEncodeTiled unavailable");
     cuuint64_t dims[2] = {cols, rows};
     cuuint64_t strides[1] = {cols * 4};

@@ -18,6 +18,13 @@
 // for every A operand (accumulator a at TMEM column offset a*BN of its buffer).
 // Each role walks the same deterministic job sequence with its own iterator.
 //
+// Optional B producers: a problem with `static constexpr int XW > 0` gets XW
+// more warps (6 .. 6+XW-1).  For every stage they wait until the stage is
+// free, call p.produce_b(job, kb, b_stage, x, lane) (x = 0..XW-1) to write
+// the B operand into shared memory themselves (jobs whose TcJob::b is null;
+// the TMA producer then loads only A), fence it for the async proxy and
+// arrive on the stage's full barrier (count 1 + XW).
+//
 // Roles (192 threads): warp 0 lane 0 issues TMA loads, warp 1 lane 0 issues
 // MMAs, warps 2..5 run the epilogue; epilogue warp w may only touch TMEM lanes
 // 32*(w%4)..+31, so it owns accumulator rows 32*(w%4)..+31.  Accumulators are
@@ -47,6 +54,20 @@ struct TcCols {
                                     : need <= 256 ? 256 : 512;
 };
 
+template <class P, class = void>
+struct TcXw {
+    static constexpr int value = 0;
+};
+template <class P>
+struct TcXw<P, decltype((void)P::XW)> {
+    static constexpr int value = P::XW;
+};
+
+template <class P>
+constexpr int tc_threads() {
+    return 192 + 32 * TcXw<P>::value;
+}
+
 template <class P>
 constexpr size_t tc_smem_bytes() {
     return (size_t)P::STAGES * (P::NA * 128 * 128 + P::BN * 128) + 1024 + 256 + P::EPI_SMEM +
@@ -54,8 +75,8 @@ constexpr size_t tc_smem_bytes() {
 }
 
 template <class P>
-__global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__ P p) {
-    constexpr int NA = P::NA, BN = P::BN, S = P::STAGES;
+__global__ void __launch_bounds__(tc_threads<P>(), 1) tc_gemm_kernel(const __grid_constant__ P p) {
+    constexpr int NA = P::NA, BN = P::BN, S = P::STAGES, XW = TcXw<P>::value;
     constexpr uint32_t A_BYTES = 128 * 128, B_BYTES = BN * 128;
     constexpr uint32_t STAGE_BYTES = NA * A_BYTES + B_BYTES;
     constexpr int NBUF = P::NBUF;
@@ -82,7 +103,7 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
-            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&full[s], 1 + XW);
             tc::mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < NBUF; b++) {
@@ -118,7 +139,7 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__
             for (int j = 0; ok && p.iter_next(itr, jb); j++) {
                 p.before_loads(jb);   // cross-CTA inputs of the job are ready
                 trace_event(tb, KID, j, TR_JOB_LOAD);
-                const uint32_t bytes = NA * A_BYTES + (uint32_t)jb.b_box * 128;
+                const uint32_t bytes = NA * A_BYTES + (jb.b ? (uint32_t)jb.b_box * 128 : 0u);
                 for (int kb = 0; kb < jb.kblocks; kb++, it++) {
                     const uint32_t s = it % S;
                     if (it >= (uint32_t)S && !(ok = tc::mbar_wait(&empty[s], ((it / S) & 1) ^ 1, err)))
@@ -134,7 +155,7 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__
                             tc::tma_load_2d(st + a * A_BYTES, jb.a[a], kb * tc::BK, jb.a_row,
                                             &full[s]);
                     }
-                    tc::tma_load_2d(st + NA * A_BYTES, jb.b, kb * tc::BK, jb.b_row, &full[s]);
+                    if (jb.b) tc::tma_load_2d(st + NA * A_BYTES, jb.b, kb * tc::BK, jb.b_row, &full[s]);
                 }
             }
         }
@@ -175,6 +196,26 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__
             }
         }
         __syncwarp();
+    } else if (XW && warp >= 6) {
+        if constexpr (XW > 0) {
+            // B producers: same stage sequence as the TMA producer
+            uint32_t it = 0;
+            bool ok = true;
+            TcJob jb;
+            typename P::Iter itr;
+            p.iter_init(itr, job_smem);
+            for (int j = 0; ok && p.iter_next(itr, jb); j++) {
+                for (int kb = 0; kb < jb.kblocks; kb++, it++) {
+                    const uint32_t s = it % S;
+                    if (it >= (uint32_t)S && !(ok = tc::mbar_wait(&empty[s], ((it / S) & 1) ^ 1, err)))
+                        break;
+                    if (!jb.b) p.produce_b(jb, kb, base + s * STAGE_BYTES + NA * A_BYTES, warp - 6, lane);
+                    tc::fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(&full[s]);
+                }
+            }
+        }
     } else {
         // epilogue warps 2..5
         TcJob jb;
@@ -209,7 +250,7 @@ int launch_tc(const P &p, int grid, cudaStream_t st) {
     if (grid < 1) grid = 1;
     P q = p;
     q.trace = host_trace();
-    FOCR_CUDA_TRY(launch_pdl(tc_gemm_kernel<P>, dim3(grid), dim3(192), smem, st, q));
+    FOCR_CUDA_TRY(launch_pdl(tc_gemm_kernel<P>, dim3(grid), dim3(tc_threads<P>()), smem, st, q));
     return FOCR_OK;
 }
 

@@ -172,3 +172,64 @@ def test_tc_accumulate_ragged(cuda, m, n, k):
         assert torch.equal(o64.sum(1), a64 @ b64.sum(0) + s64.sum(1))
         rows = torch.cat([torch.arange(4), torch.arange(m - 4, m)])
         assert torch.equal(o64[rows], a64[rows] @ b64.T + s64[rows])
+
+
+@pytest.mark.parametrize("m,k,n,group", [
+    (64, 1280, 1792, 32), (256, 1280, 896, 32), (256, 896, 1280, 32), (65, 1280, 16160, 32),
+    (32, 1280, 1792, 16), (100, 896, 1280, 16), (256, 1280, 130, 16), (300, 128, 257, 32)])
+def test_int4_tensor_core_shapes(cuda, oracle, m, k, n, group):
+    """The tcgen05 int4 path (M >= 64, or 32 for groups of 16; K a multiple of
+    128): bit-identical to the oracle in host and device mode, ragged M and N
+    included."""
+    import torch
+
+    from franken_ocr_b200 import simd
+
+    g = np.random.default_rng(m * 7 + n)
+    a = g.integers(-127, 128, m * k, dtype=np.int8)
+    bp = g.integers(0, 256, n * (k // 2), dtype=np.uint8)
+    sc = g.uniform(0.001, 0.02, n * (k // group)).astype(np.float32)
+    want = oracle.igemm_s4s8_packed(a, bp, sc, group, m, k, n)
+    got = np.full(m * n, 123.5, np.float32)
+    simd.igemm_s4s8_packed(a, bp, sc, group, m, k, n, got)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    da, db, ds = (torch.from_numpy(v).cuda() for v in (a, bp, sc))
+    dout = torch.full((m * n,), float("nan"), device="cuda")
+    simd.igemm_s4s8_packed(da, db, ds, group, m, k, n, dout)
+    torch.cuda.synchronize()
+    assert np.array_equal(dout.cpu().numpy().view(np.uint32), want.view(np.uint32))
+
+
+def test_int4_tensor_core_extremes(cuda, oracle):
+    """All weights -8 against +-127 activations: every group dot at its
+    extreme (-32512 / +32512 for groups of 32), through the tcgen05 path."""
+    from franken_ocr_b200 import simd
+
+    m, k, n = 64, 1280, 256
+    for group in (16, 32):
+        a = np.where(np.arange(m * k) % 3 == 0, -127, 127).astype(np.int8)
+        bp = np.full(n * (k // 2), 0x88, np.uint8)
+        sc = np.linspace(0.001, 0.05, n * (k // group)).astype(np.float32)
+        got = np.empty(m * n, np.float32)
+        simd.igemm_s4s8_packed(a, bp, sc, group, m, k, n, got)
+        want = oracle.igemm_s4s8_packed(a, bp, sc, group, m, k, n)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), group
+
+
+def test_igemm_status_query_clean(cuda):
+    """After tensor-core igemm calls the device status word is 0."""
+    import ctypes as C
+
+    import torch
+
+    from franken_ocr_b200 import simd
+    from franken_ocr_b200._lib import check, lib
+
+    a = torch.randint(-127, 128, (256, 1280), dtype=torch.int8, device="cuda")
+    b = torch.randint(-127, 128, (1792, 1280), dtype=torch.int8, device="cuda")
+    o = torch.zeros((256, 1792), dtype=torch.int32, device="cuda")
+    simd.igemm_s8s8(a, b, 256, 1280, 1792, o)
+    torch.cuda.synchronize()
+    w = C.c_int(-1)
+    check(lib.focr_igemm_status(C.byref(w), 1))
+    assert w.value == 0

@@ -226,3 +226,31 @@ def test_forward_fused_launch(cuda, oracle, monkeypatch, m):
     want = MoeOracle(W).forward(x, idx, w)
     assert np.array_equal(y.view(np.uint32), want.view(np.uint32))
     L.close()
+
+
+@pytest.mark.parametrize("m", [2, 64, 300])
+def test_forward_fusedq_launch(cuda, oracle, monkeypatch, m):
+    """The single persistent launch with on-load requantisation
+    (FOCR_MOE_PATH=fusedq: the down GEMM's producer warps quantise the act rows
+    with the gate+up epilogue's per-row maximum) gives the same bits as the
+    oracle, for decode (forward) and prefill (ties-even) semantics, twice in a
+    row on one handle."""
+    from franken_ocr_b200 import synth
+    from franken_ocr_b200.moe import MoeLayer
+    from oracle.oracle import MoeOracle
+
+    monkeypatch.setenv("FOCR_MOE_PATH", "fusedq")
+    W = synth.moe_layer(813, shared_inter=1792)
+    L = MoeLayer(W, max_tokens=m)
+    O = MoeOracle(W)
+    for step in range(2):
+        x = synth.hidden_states(814 + step, m)
+        idx, w = synth.zipf_routing(814 + step, m)
+        y = L.forward(x, idx, w)
+        want = O.forward(x, idx, w)
+        assert np.array_equal(y.view(np.uint32), want.view(np.uint32)), step
+    x = synth.hidden_states(820, m)
+    y, _, _ = L.prefill(x)
+    _, want, _, _ = O.prefill(x)
+    assert np.array_equal(y.view(np.uint32), want.view(np.uint32))
+    L.close()
