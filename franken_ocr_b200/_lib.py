@@ -28,7 +28,7 @@ EXPORTS = [
     "focr_igemm_s4s8_packed", "focr_quantize_rows_i8", "focr_gemv_i8", "focr_gemv_i8_noalloc",
     "focr_moe_create", "focr_moe_destroy", "focr_moe_route", "focr_moe_forward",
     "focr_moe_decode", "focr_moe_prefill", "focr_moe_forward_rows", "focr_moe_combine",
-    "focr_lmhead_create", "focr_lmhead_destroy", "focr_lmhead_top1",
+    "focr_lmhead_create", "focr_lmhead_create_s4", "focr_lmhead_destroy", "focr_lmhead_top1",
     "focr_top1_combine", "focr_selftest", "focr_trace_set", "focr_rms_norm", "focr_rope_apply",
     "focr_attention_decode", "focr_linear_i8", "focr_swiglu", "focr_add",
     "focr_attention_prefill", "focr_rope_table", "focr_decode_prologue", "focr_rope_apply_at",
@@ -114,6 +114,7 @@ lib.focr_ep_combine.argtypes = [vp, vp, vp]
 lib.focr_ep_decode.argtypes = [vp, vp, sz, vp, vp, vp, vp]
 lib.focr_ep_status.argtypes = [vp, C.POINTER(i32)]
 lib.focr_lmhead_create.argtypes = [vp, vp, sz, sz, sz, sz, C.POINTER(vp)]
+lib.focr_lmhead_create_s4.argtypes = [vp, vp, sz, sz, sz, sz, sz, C.POINTER(vp)]
 lib.focr_lmhead_destroy.argtypes = [vp]
 lib.focr_lmhead_top1.argtypes = [vp, vp, sz, vp, vp, vp, i32, vp]
 lib.focr_top1_combine.argtypes = [vp, vp, sz, sz, vp]

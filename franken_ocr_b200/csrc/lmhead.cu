@@ -8,7 +8,9 @@
 #include "gemv.cuh"
 
 struct focr_lmhead {
-    int8_t *w = nullptr;
+    int8_t *w = nullptr;        // int8 head [rows][hidden], per-row scales
+    uint8_t *wp = nullptr;      // or int4 head [rows][hidden/2], per-(row, group) scales
+    size_t group = 0;           // 0: int8; 16/32: int4
     float *scales = nullptr;
     size_t rows = 0, hidden = 0, row_begin = 0, max_tokens = 0;
     float *x = nullptr;        // [T][hidden] staging
@@ -106,7 +108,7 @@ extern "C" {
 
 int focr_lmhead_destroy(focr_lmhead *h) {
     if (!h) return FOCR_OK;
-    void *ptrs[] = {h->w, h->scales, h->x, h->xq, h->xs, h->logits, h->bv, h->bi};
+    void *ptrs[] = {h->w, h->wp, h->scales, h->x, h->xq, h->xs, h->logits, h->bv, h->bi};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     delete h;
@@ -159,8 +161,15 @@ int focr_lmhead_top1(focr_lmhead *h, const float *x, size_t m, float *best_val,
     }
     float *dlog = (mem == FOCR_MEM_DEVICE && logits) ? logits : h->logits;
     int rc = FOCR_E_UNSUPPORTED;
-    if (m == 1) rc = launch_gemv_q1(dx, h->hidden, false, h->w, h->scales, h->rows, dlog, st);
-    if (rc) {
+    if (h->group) {
+        // int4 head: logits = igemm_s4s8_packed(Q(x), W) * a_scale
+        rc = launch_quantize_rows(dx, m, h->hidden, false, h->xq, h->xs, st);
+        if (!rc) rc = launch_gemv_s4(h->xq, h->wp, h->scales, h->group, m, h->hidden, h->rows, dlog,
+                                     h->xs, st);
+    } else if (m == 1) {
+        rc = launch_gemv_q1(dx, h->hidden, false, h->w, h->scales, h->rows, dlog, st);
+    }
+    if (rc && !h->group) {
         rc = launch_quantize_rows(dx, m, h->hidden, false, h->xq, h->xs, st);
         if (!rc) rc = launch_gemv_dequant(h->xq, h->xs, h->w, h->scales, m, h->hidden, h->rows, dlog, st);
     }
@@ -177,6 +186,43 @@ int focr_lmhead_top1(focr_lmhead *h, const float *x, size_t m, float *best_val,
                                           cudaMemcpyDeviceToHost, st));
         FOCR_CUDA_TRY(cudaStreamSynchronize(st));
     }
+    return FOCR_OK;
+}
+
+int focr_lmhead_create_s4(const uint8_t *packed, const float *scales, size_t group, size_t rows,
+                          size_t hidden, size_t row_begin, size_t max_tokens, focr_lmhead **out) {
+    if (!packed || !scales || !out) return fail(FOCR_E_ARG, "lmhead_create_s4: null argument");
+    if (!rows || !hidden || !max_tokens) return fail(FOCR_E_ARG, "lmhead_create_s4: empty shape");
+    if ((group != 16 && group != 32) || hidden % group)
+        return fail(FOCR_E_SHAPE, "lmhead_create_s4: group must be 16 or 32 and divide hidden");
+    if (rows > (size_t)INT32_MAX || row_begin + rows > (size_t)INT32_MAX)
+        return fail(FOCR_E_UNSUPPORTED, "lmhead_create_s4: vocab exceeds int32");
+    focr_lmhead *h = new focr_lmhead();
+    h->rows = rows;
+    h->hidden = hidden;
+    h->row_begin = row_begin;
+    h->max_tokens = max_tokens;
+    h->group = group;
+    const size_t ns = rows * (hidden / group);
+    cudaError_t e = cudaSuccess;
+#define A(p, n)                                       \
+    if (e == cudaSuccess) e = cudaMalloc((void **)&p, (n));
+    A(h->wp, rows * hidden / 2);
+    A(h->scales, ns * 4);
+    A(h->x, max_tokens * hidden * 4);
+    A(h->xq, max_tokens * hidden);
+    A(h->xs, max_tokens * 4);
+    A(h->logits, max_tokens * rows * 4);
+    A(h->bv, max_tokens * 4);
+    A(h->bi, max_tokens * 4);
+#undef A
+    if (e == cudaSuccess) e = cudaMemcpy(h->wp, packed, rows * hidden / 2, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(h->scales, scales, ns * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        focr_lmhead_destroy(h);
+        return cuda_fail(e, "lmhead_create_s4");
+    }
+    *out = h;
     return FOCR_OK;
 }
 

@@ -18,16 +18,25 @@ def _ptr(a):
 
 
 class LmHeadShard:
-    """Rows [row_begin, row_begin + rows) of the [vocab, hidden] int8 head."""
+    """Rows [row_begin, row_begin + rows) of the [vocab, hidden] int8 head, or
+    of an int4 head (``group`` 16/32: ``w`` packed [rows, hidden/2],
+    ``scales`` [rows, hidden/group])."""
 
-    def __init__(self, w: np.ndarray, scales: np.ndarray, row_begin: int = 0, max_tokens: int = 1):
-        w = np.ascontiguousarray(w, dtype=np.int8)
+    def __init__(self, w: np.ndarray, scales: np.ndarray, row_begin: int = 0, max_tokens: int = 1,
+                 group: int = 0):
         scales = np.ascontiguousarray(scales, dtype=np.float32)
-        self.rows, self.hidden = w.shape
         self.row_begin = row_begin
         h = C.c_void_p()
-        check(lib.focr_lmhead_create(w.ctypes.data, scales.ctypes.data, self.rows, self.hidden,
-                                     row_begin, max_tokens, C.byref(h)))
+        if group:
+            w = np.ascontiguousarray(w, dtype=np.uint8)
+            self.rows, self.hidden = w.shape[0], w.shape[1] * 2
+            check(lib.focr_lmhead_create_s4(w.ctypes.data, scales.ctypes.data, group, self.rows,
+                                            self.hidden, row_begin, max_tokens, C.byref(h)))
+        else:
+            w = np.ascontiguousarray(w, dtype=np.int8)
+            self.rows, self.hidden = w.shape
+            check(lib.focr_lmhead_create(w.ctypes.data, scales.ctypes.data, self.rows, self.hidden,
+                                         row_begin, max_tokens, C.byref(h)))
         self._h = h
 
     def close(self):

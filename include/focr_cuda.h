@@ -284,6 +284,14 @@ typedef struct focr_lmhead focr_lmhead;
 int focr_lmhead_create(const int8_t *w, const float *scales, size_t rows,
                        size_t hidden, size_t row_begin, size_t max_tokens,
                        focr_lmhead **out);
+/* int4 shard (config 4's g32 head): packed [rows][hidden/2] (low nibble =
+ * even column), scales [rows][hidden/group], group 16 or 32.  Logits are
+ * igemm_s4s8_packed (simd/int4.rs:437) of the half-away-quantised row,
+ * times the row's activation scale -- the int4 counterpart of gemv_i8
+ * (decoder.rs:1607); the reference ships the int4 kernel but no int4 head,
+ * so this is the mapping its packing convention implies. */
+int focr_lmhead_create_s4(const uint8_t *packed, const float *scales, size_t group, size_t rows,
+                          size_t hidden, size_t row_begin, size_t max_tokens, focr_lmhead **out);
 int focr_lmhead_destroy(focr_lmhead *h);
 
 /* For each of m (already RMS-normed) rows: logits = gemv_i8(x, shard); top-1
