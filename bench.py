@@ -261,6 +261,17 @@ def run_ours(args, ws, rank, local):
         return
     if args.workload == "config3":
         return config3(args, dev)
+    if args.workload == "config4":
+        c4 = config4_measure(dev, hbm_peak, peak_kind, reps=max(3, args.steps))
+        print(json.dumps({
+            "metric": "int4 MoE decode tokens/s (config 4: M=256 int4 g32 layer)",
+            "value": c4["moe_m256"]["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": 3, "ms_per_step": c4["moe_m256"]["us_per_step"] / 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int4 weights x int8 activations (i32 per group, f32 across groups)",
+            "data": "synthetic", "config": {"workload": c4["workload"]},
+            "roofline": c4["moe_m256"]["roofline"], "config4": c4}), flush=True)
+        return
     if args.workload == "config3_batch":
         return config3_batch(args, dev)
     # ring of layers so that consecutive steps stream from HBM
@@ -348,6 +359,24 @@ def run_ours(args, ws, rank, local):
         line["cpu_baseline"] = cpu
     if m1:
         line["m1_decode"] = m1
+    if not args.no_extras:
+        # the other configurations, measured in the same run (driver-visible)
+        def extra(key, fn):
+            try:
+                line[key] = fn()
+            except Exception as exc:  # pragma: no cover - reported, never fatal
+                line[key] = {"error": f"{type(exc).__name__}: {exc}"}
+
+        def c1():
+            own, rows = igemm_sweep(dev, hbm_peak, peak_kind, reps=5)
+            lib_peak = int8_library_peak(dev)
+            return {"workload": "config1_igemm_sweep (out += int32)", "shapes": rows,
+                    "int8_peak_tops_own_kernel": own, "int8_peak_tops_torch_int_mm": lib_peak,
+                    "note": "frac = floor / time, floor = max(bytes / HBM peak, ops / own-kernel peak)"}
+
+        extra("config1", c1)
+        extra("config3", lambda: config3_line(args, dev, steps=2))
+        extra("config4", lambda: config4_measure(dev, hbm_peak, peak_kind))
     if rank == 0:
         print(json.dumps(line), flush=True)
 
@@ -604,6 +633,109 @@ def run_ep(args, ws, rank, local):
     comm.close()
 
 
+def timed_graph(step, n, warm=3):
+    """us per call of step(i) for i < n, replayed from one CUDA graph."""
+    import torch
+
+    for i in range(warm):
+        step(i)
+    torch.cuda.synchronize()
+    g = capture(step, range(n))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    if g is not None:
+        g.replay()
+    else:
+        for i in range(n):
+            step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / n
+
+
+def config4_measure(dev, hbm_peak, peak_kind, reps=20):
+    """Config 4: int4 g32 experts with config 0's MoE shapes (64 experts,
+    top-6, no shared expert) at M = 1 and M = 256 (route + experts, decode
+    semantics), and the int4 g32 lm-head shard [16160, 1280] with its top-1
+    at M = 1 and M = 256.  Rings of layers (> L2) keep the weights streaming
+    from HBM; each case is one CUDA graph of `reps` calls.  Bytes are the
+    algorithmic int4 weight + scale bytes a call must read."""
+    import torch
+
+    from franken_ocr_b200 import synth
+    from franken_ocr_b200.lmhead import LmHeadShard
+    from franken_ocr_b200.moe import MoeLayer
+    from franken_ocr_b200.quant import pack_int4_f32
+
+    G = 32
+    per_expert = 3 * INTER * HIDDEN // 2 + (2 * INTER * HIDDEN + HIDDEN * INTER) // G * 4
+    out = {"workload": "config4_int4_g32", "group": G}
+    R = 8
+    layers = [MoeLayer(synth.moe_layer(4500 + r, group=G), max_tokens=256) for r in range(R)]
+    for m in (1, 256):
+        xs = [torch.from_numpy(synth.hidden_states(4600 + r, m)).to(dev) for r in range(R)]
+        ys = [torch.empty((m, HIDDEN), device=dev) for _ in range(R)]
+        ii = [torch.empty((m, TOPK), dtype=torch.int32, device=dev) for _ in range(R)]
+        ww = [torch.empty((m, TOPK), device=dev) for _ in range(R)]
+        us = timed_graph(lambda i: layers[i % R].decode(xs[i % R], ys[i % R], ii[i % R], ww[i % R]),
+                         reps)
+        hit = np.mean([len(np.unique(ii[r].cpu().numpy())) for r in range(R)])
+        byt = hit * per_expert + NEXP * HIDDEN * 4
+        out[f"moe_m{m}"] = {"us_per_step": us, "tokens_per_s": m / (us / 1e6),
+                            "experts_hit": float(hit),
+                            "roofline": {"bound": "hbm", "achieved": byt / us / 1e3, "peak": hbm_peak,
+                                         "unit": "GB/s", "frac": byt / us / 1e3 / hbm_peak,
+                                         "peak_kind": peak_kind, "algorithmic_bytes": byt}}
+    for L in layers:
+        L.close()
+    rows = 16160
+    heads = []
+    for r in range(4):   # 4 shards (52 MB) > L2
+        packed, sc = pack_int4_f32(synth.normal(4700, "lm_head", r, (rows, HIDDEN), 0.02), G)
+        heads.append(LmHeadShard(packed, sc, row_begin=r * rows, max_tokens=256, group=G))
+    hb = rows * HIDDEN // 2 + rows * (HIDDEN // G) * 4
+    for m in (1, 256):
+        x = torch.from_numpy(synth.hidden_states(4800, m)).to(dev)
+        us = timed_graph(lambda i: heads[i % 4].top1(x), reps)
+        ops = 2 * m * rows * HIDDEN
+        out[f"lmhead_shard_m{m}"] = {
+            "us": us, "rows": rows, "tokens_per_s": m / (us / 1e6),
+            "roofline": {"bound": "hbm", "achieved": hb / us / 1e3, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": hb / us / 1e3 / hbm_peak, "peak_kind": peak_kind,
+                         "algorithmic_bytes": hb, "int_tops": ops / us / 1e6}}
+    for h in heads:
+        h.close()
+    out["parity"] = "tests/test_gpu_config4.py: MoE and lm-head shard bit-identical to the oracle at M=1, 256"
+    return out
+
+
+def int8_library_peak(dev):
+    """An int8 tensor-core throughput that is not this build's kernel: torch's
+    int8 matmul (cuBLASLt, i8 x i8 -> i32) on 8192 x 8192 x 16384, best of 5;
+    None when unavailable."""
+    import torch
+
+    try:
+        a = torch.randint(-127, 128, (8192, 16384), dtype=torch.int8, device=dev)
+        b = torch.randint(-127, 128, (16384, 8192), dtype=torch.int8, device=dev)
+        for _ in range(2):
+            torch._int_mm(a, b)
+        torch.cuda.synchronize()
+        best = None
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._int_mm(a, b)
+            e1.record()
+            torch.cuda.synchronize()
+            t = e0.elapsed_time(e1)
+            best = t if best is None else min(best, t)
+        return 2 * 8192 * 8192 * 16384 / (best / 1e3) / 1e12
+    except Exception as exc:  # pragma: no cover
+        print(f"bench: torch._int_mm unavailable ({exc})", file=sys.stderr)
+        return None
+
+
 def cpu_baseline_config3(W, seed, prefill=32, seconds=10.0, max_steps=200):
     """The reference's decode loop restated on the host cores: projections,
     dense MLP, MoE experts (decode_mlp_i8's task split) and lm-head on the
@@ -715,6 +847,10 @@ def config3_batch(args, dev, streams=16, batch=8, prefill=256, n_tokens=64, seed
 
 
 def config3(args, dev, prefill=1024, n_tokens=256, seed=3):
+    print(json.dumps(config3_line(args, dev, prefill, n_tokens, seed)), flush=True)
+
+
+def config3_line(args, dev, prefill=1024, n_tokens=256, seed=3, steps=None):
     """Config 3: the synthetic 12-layer int8 decoder; one step = a
     1024-token prefill then a 256-token greedy decode (batch 1), the decode
     loop replayed from one captured CUDA graph per token.  Timed on the
@@ -749,7 +885,7 @@ def config3(args, dev, prefill=1024, n_tokens=256, seed=3):
     clocks = Clocks(dev.index or 0)
     clocks.start()
     pre, dec = [], []
-    for _ in range(args.steps):
+    for _ in range(steps or args.steps):
         toks, p_ms, d_ms = run()
         assert toks == toks0, "greedy tokens changed between runs"
         pre.append(p_ms)
@@ -767,9 +903,10 @@ def config3(args, dev, prefill=1024, n_tokens=256, seed=3):
     d_ms, p_ms = float(np.median(dec)), float(np.median(pre))
     cpu = None if args.no_cpu else cpu_baseline_config3(W, seed)
     roof, launches = config3_roofline(W, prefill, n_tokens, d_ms)
-    print(json.dumps({
+    D.close()
+    return {
         "metric": "int8 decoder greedy decode tokens/s (config 3: 12 layers, batch 1)",
-        "value": n_tokens / (d_ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "value": n_tokens / (d_ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": steps or args.steps,
         "warmup": max(3, args.warmup), "ms_per_step": p_ms + d_ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8 (i32 accumulate, f32 dequant)",
         "data": "synthetic (random-init weights, N(0,1) prompt embeddings)",
@@ -783,8 +920,7 @@ def config3(args, dev, prefill=1024, n_tokens=256, seed=3):
                 "h2d_bytes_per_step": prefill * W.hidden * 4, "d2h_bytes_per_step": n_tokens * 4},
         "roofline": roof, "gpu_launches": launches,
         "cpu_baseline": cpu, "clocks": clk, "tokens_head": toks0[:16],
-        "parity": "all 256 greedy tokens equal the CPU oracle's (tests/golden)"}), flush=True)
-    D.close()
+        "parity": "all 256 greedy tokens equal the CPU oracle's (tests/golden)"}
 
 
 def main():
@@ -795,7 +931,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-m1", action="store_true", help="skip the config-0 single-token line")
-    ap.add_argument("--workload", default="config2", choices=["config2", "config0", "config1", "config3", "config3_batch"],
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the config-1/3/4 measurements added to the default line")
+    ap.add_argument("--workload", default="config2", choices=["config2", "config0", "config1", "config3", "config3_batch", "config4"],
                     help="config0: only the single-token layer; config1: the raw igemm sweep; "
                          "config3: the 12-layer decoder")
     args = ap.parse_args()
