@@ -14,7 +14,7 @@ pytestmark = pytest.mark.gpu
 RTOL = 1e-5
 
 
-def assert_close_rel(got, want, what):
+def assert_close_rel(got, want, what, min_exact=1.0):
     got = np.asarray(got, np.float32)
     want = np.asarray(want, np.float32)
     scale = np.sqrt(np.mean(want.astype(np.float64) ** 2, axis=-1, keepdims=True)) + 1e-30
