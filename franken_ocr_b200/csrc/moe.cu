@@ -235,6 +235,46 @@ __global__ void act_quant_kernel(const float *__restrict__ act, int I, const int
     for (int i = threadIdx.x; i < I; i += blockDim.x) q[i] = (int8_t)quant_i8(row[i], inv, te != 0);
 }
 
+// int4 tensor-core path: act = silu(g) * u from the grouped GEMM's g and u
+// rows (already times the activation scale, expert_s4 order), then the row's
+// requantisation (decoder.rs:1751), one block per pair (rows >= count skipped).
+__global__ void s4_swiglu_quant_kernel(const float *__restrict__ g, const float *__restrict__ u,
+                                       int I, const int32_t *__restrict__ count,
+                                       int8_t *__restrict__ aq, float *__restrict__ as, int te) {
+    if ((int)blockIdx.x >= *count) return;
+    __shared__ float red[32];
+    __shared__ float s_inv;
+    const float *gr = g + (size_t)blockIdx.x * I, *ur = u + (size_t)blockIdx.x * I;
+    int8_t *q = aq + (size_t)blockIdx.x * I;
+    constexpr int V = 2048 / 128;
+    float a[V];
+    float m = 0.0f;
+#pragma unroll
+    for (int v = 0; v < V; v++) {
+        const int i = threadIdx.x + 128 * v;
+        a[v] = i < I ? __fmul_rn(silu_f(gr[i]), ur[i]) : 0.0f;
+        m = fmaxf(m, fabsf(a[v]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float mx = 0.0f;
+        for (int wi = 0; wi < (int)(blockDim.x >> 5); wi++) mx = fmaxf(mx, red[wi]);
+        const float sc = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 1.0f;
+        as[blockIdx.x] = sc;
+        s_inv = __fdiv_rn(1.0f, sc);
+    }
+    __syncthreads();
+    const float inv = s_inv;
+#pragma unroll
+    for (int v = 0; v < V; v++) {
+        const int i = threadIdx.x + 128 * v;
+        if (i < I) q[i] = (int8_t)quant_i8(a[v], inv, te != 0);
+    }
+}
+
 // Down GEMV: one warp per down row c of a local expert (K = I) or of the
 // shared expert (K = S); writes p = y * w for routed pairs and y for shared.
 __global__ void __launch_bounds__(MOE_THREADS) expert_down_kernel(MoeDev d) {
@@ -479,6 +519,10 @@ static MoeDev make_dev(focr_moe_layer *L, int T, const float *w, float *part) {
 
 static int moe_grid() { return num_sms() * 8; }
 
+// Smallest batch the int4 experts take through the tensor cores; single
+// tokens and small batches keep the dp4a GEMV-grouped kernels.
+constexpr int S4_TC_MIN_TOKENS = 16;
+
 void launch_act_quant(focr_moe_layer *L, int m, int sh0, cudaStream_t st, bool te) {
     act_quant_kernel<<<m * L->cfg.topk, 256, 0, st>>>(L->act, L->cfg.inter, L->offsets + L->E,
                                                       L->aq, L->as2, (int)te);
@@ -512,17 +556,51 @@ int moe_forward_dev(focr_moe_layer *L, const float *x, int m, const int32_t *idx
         rc = moe_tc_experts(L, x, m, idx, w, sh0, st, prefill);
         if (rc) return rc;
     } else {
-        check_idx_kernel<<<1, 256, 0, st>>>(idx, m * K, (int)L->cfg.expert_begin,
-                                            (int)(L->cfg.expert_begin + L->E), L->err);
-        rc = launch_quantize_rows(x, m, H, prefill, L->xq, L->xs, st);
-        if (rc) return rc;
-        bucket_kernel<<<1, 1024, 0, st>>>(idx, m, K, L->E, L->cfg.expert_begin, L->offsets,
-                                          L->pair_tok, L->pair_slot);
-        // empty slots (negative ids) contribute +0 to the combine
-        FOCR_CUDA_TRY(cudaMemsetAsync(L->part, 0, (size_t)m * K * H * sizeof(float), st));
+        const bool s4tc = L->cfg.group && L->ubuf && m >= S4_TC_MIN_TOKENS && m <= 4096;
+        if (!s4tc) {
+            check_idx_kernel<<<1, 256, 0, st>>>(idx, m * K, (int)L->cfg.expert_begin,
+                                                (int)(L->cfg.expert_begin + L->E), L->err);
+            rc = launch_quantize_rows(x, m, H, prefill, L->xq, L->xs, st);
+            if (rc) return rc;
+            bucket_kernel<<<1, 1024, 0, st>>>(idx, m, K, L->E, L->cfg.expert_begin, L->offsets,
+                                              L->pair_tok, L->pair_slot);
+            // empty slots (negative ids) contribute +0 to the combine
+            FOCR_CUDA_TRY(cudaMemsetAsync(L->part, 0, (size_t)m * K * H * sizeof(float), st));
+        }
         MoeDev d = make_dev(L, m, w, L->part);
         d.sh0 = sh0;
-        if (d.group) {
+        if (s4tc) {
+            // int4 routed experts on the tensor cores: bucket + quantise +
+            // gather, grouped gate|up GEMM, SwiGLU + requantisation, grouped
+            // down GEMM writing the weighted partials; the shared expert
+            // stays int8 (GEMV-grouped kernels)
+            MoeDev dsh = d;
+            dsh.E = 0;
+            rc = moe_tc_prep(L, x, m, idx, prefill, st);
+            if (rc) return rc;
+            const int E = (int)L->E, I = L->cfg.inter, P = m * K;
+            const size_t Pp = P < 128 ? 128 : P;
+            rc = launch_tc_s4_moe(false, d.group, E, I, H, L->gate_p, L->gate_gs, L->up_p,
+                                  L->up_gs, L->xq_sorted, Pp, L->offsets, L->counts, L->xs_sorted,
+                                  L->act, L->ubuf, nullptr, nullptr, nullptr, nullptr, K, L->err,
+                                  st);
+            if (rc) return rc;
+            s4_swiglu_quant_kernel<<<P, 128, 0, st>>>(L->act, L->ubuf, I, L->offsets + E, L->aq,
+                                                      L->as2, (int)prefill);
+            if (d.S && m > sh0) {
+                expert_gateup_kernel<<<moe_grid(), MOE_THREADS, 0, st>>>(dsh);
+                const int S = (int)d.S;
+                act_quant_kernel<<<m - sh0, 256, 0, st>>>(L->sh_act + (size_t)sh0 * S, S, nullptr,
+                                                          L->sh_aq + (size_t)sh0 * S,
+                                                          L->sh_as + sh0, (int)prefill);
+                expert_down_kernel<<<moe_grid(), MOE_THREADS, 0, st>>>(dsh);
+            }
+            rc = launch_tc_s4_moe(true, d.group, E, H, I, L->down_p, L->down_gs, nullptr, nullptr,
+                                  L->aq, Pp, L->offsets, L->counts, L->as2, nullptr, nullptr,
+                                  L->pair_tok, L->pair_slot, w, L->part, K, L->err, st);
+            if (rc) return rc;
+            FOCR_CUDA_TRY(cudaGetLastError());
+        } else if (d.group) {
             // int4 routed experts; the shared expert stays int8 (E = 0 leaves
             // only its rows to the int8 kernels)
             MoeDev dsh = d;
@@ -597,7 +675,7 @@ int focr_moe_destroy(focr_moe_layer *L) {
                     L->counts, L->offsets, L->pair_tok, L->pair_slot, L->act, L->amax, L->aq,
                     L->as2, L->part, L->sh_act, L->sh_amax, L->sh_as, L->sh_y, L->sh_aq, L->err,
                     L->sync, L->sched, L->xq_sorted, L->xs_sorted, L->gate_t, L->up_t, L->down_t,
-                    L->sh_gate_t, L->sh_up_t, L->sh_down_t, L->tagged};
+                    L->sh_gate_t, L->sh_up_t, L->sh_down_t, L->tagged, L->ubuf};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     delete L;
@@ -673,6 +751,8 @@ int focr_moe_create(const focr_moe_config *cfg, const focr_moe_weights *wt,
     TRY(dev_alloc(&L->pair_tok, P));
     TRY(dev_alloc(&L->pair_slot, P));
     TRY(dev_alloc(&L->act, P * I));
+    if (c.group && H % 128 == 0 && I % 128 == 0 && !getenv("FOCR_DISABLE_TC"))
+        TRY(dev_alloc(&L->ubuf, P * I));
     TRY(dev_alloc(&L->amax, P));
     TRY(dev_alloc(&L->aq, (P < 128 ? 128 : P) * I));
     TRY(dev_alloc(&L->as2, P));

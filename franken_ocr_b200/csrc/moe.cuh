@@ -30,6 +30,7 @@ struct focr_moe_layer {
     int32_t *offsets = nullptr;                    // [E+2]
     int32_t *pair_tok = nullptr, *pair_slot = nullptr;  // [P]
     float *act = nullptr;                          // [P][I]
+    float *ubuf = nullptr;                         // [P][I] int4 tensor-core path: up halves
     float *amax = nullptr;                         // [P]   (pairs), then [T] shared
     int8_t *aq = nullptr;                          // [P][I]
     float *as2 = nullptr;                          // [P]
@@ -83,6 +84,15 @@ struct EpReturn {
 // every routed partial to its source rank (see MoeDown).
 int moe_tc_gemms(focr_moe_layer *L, int m, const float *w, int sh0, cudaStream_t st, bool te,
                  const EpReturn *ret);
+int launch_tc_s4_moe(bool down, int group, int E, int rows, int K, const uint8_t *w0,
+                     const float *s0, const uint8_t *w1, const float *s1, const int8_t *b,
+                     size_t b_rows, const int32_t *offsets, const int32_t *active,
+                     const float *row_scale, float *out0, float *out1, const int32_t *pair_tok,
+                     const int32_t *pair_slot, const float *wts, float *part, int topk, int *err,
+                     cudaStream_t st);
+// Bucket + quantise + gather for the tensor-core expert paths (moe_tc.cu).
+int moe_tc_prep(focr_moe_layer *L, const float *x, int m, const int32_t *idx, bool te,
+                cudaStream_t st);
 void launch_act_quant(focr_moe_layer *L, int m, int sh0, cudaStream_t st, bool te = false);
 
 }  // namespace focr

@@ -1203,6 +1203,17 @@ int moe_tc_experts(focr_moe_layer *L, const float *x, int m, const int32_t *idx,
     return moe_tc_gemms(L, m, w, sh0, st, te, nullptr);
 }
 
+int moe_tc_prep(focr_moe_layer *L, const float *x, int m, const int32_t *idx, bool te,
+                cudaStream_t st) {
+    const int H = L->cfg.hidden, K = L->cfg.topk;
+    FOCR_CUDA_TRY(launch_pdl(moe_prep_kernel, dim3(m), dim3(256), 0, st, x, idx, m, H, K,
+                             (int)L->E, (int)L->cfg.expert_begin, L->xq, L->xs, L->offsets,
+                             L->pair_tok, L->pair_slot, L->xq_sorted, L->xs_sorted, L->counts,
+                             L->sched, L->part, L->err, (int)te, (int *)nullptr, 0,
+                             (float *)nullptr, (float *)nullptr));
+    return FOCR_OK;
+}
+
 int moe_tc_gemms(focr_moe_layer *L, int m, const float *w, int sh0, cudaStream_t st, bool te,
                  const EpReturn *ret) {
     MoeTcState *s = static_cast<MoeTcState *>(L->tc_state);

@@ -45,15 +45,125 @@ struct S4Cfg {
     static constexpr size_t SMEM = (size_t)S4_STAGES * STAGE + 1024 + 256;
 };
 
-struct S4Params {
+// One job: 128 weight rows (from tensor map `a` at row a_row) against NC
+// activation rows (b_row.., nv of them valid); group scales of weight row r
+// at scales[r * G + g] with r counted from scale_row0.
+struct S4Job {
+    const CUtensorMap *a;
+    const float *scales;   // scales of the job's first weight row
+    int a_row, b_row, nv;
+    int n0;                // first weight row index within its matrix (tile * 128)
+    int e, kind;           // problem tags
+};
+
+// The plain packed GEMM (igemm_s4s8_packed): jobs (tile, chunk), chunk fastest.
+struct S4Raw {
     CUtensorMap tw;          // packed weights [N rows][K/2 bytes], box 128 x 64 B, no swizzle
-    CUtensorMap ta;          // activations [M rows][K], box NC x 128 B, 128-byte swizzle
-    const float *scales;     // [N][K/GROUP]
+    const float *scales;     // [N][G]
     const float *dequant_a;  // [M] or nullptr
     float *out;              // [M][N]
-    int M, N, K, G;          // G = K / GROUP
+    int M, N, G, NC;
     int tiles, chunks;       // ceil(N/128), ceil(M/NC)
+    static constexpr int STAGE_SMEM = 0;
+    __device__ void stage(void *) const {}
+    __device__ bool job(int j, const void *, S4Job &jb) const {
+        if (j >= tiles * chunks) return false;
+        const int tile = j / chunks, chunk = j % chunks;
+        jb.a = &tw;
+        jb.a_row = tile * 128;
+        jb.n0 = tile * 128;
+        jb.b_row = chunk * NC;
+        jb.nv = min(NC, M - chunk * NC);
+        jb.scales = scales + (size_t)tile * 128 * G;
+        jb.e = 0;
+        jb.kind = 0;
+        return true;
+    }
+    __device__ bool row_valid(const S4Job &jb, int r) const { return jb.n0 + r < N; }
+    __device__ void store(const S4Job &jb, int r, int col, float acc) const {
+        const int m = jb.b_row + col, n = jb.n0 + r;
+        out[(size_t)m * N + n] = dequant_a ? __fmul_rn(acc, dequant_a[m]) : acc;
+    }
+    __device__ void prefetch() const { tc::prefetch_tmap(&tw); }
+};
+
+// Grouped int4 expert GEMMs of the MoE layer over pairs bucketed by expert
+// (the layer's prep kernel: offsets, most-pairs-first active list,
+// xq_sorted / aq rows in pair order).  Jobs run expert by expert (active
+// order), then matrix (kind), then 128-row tile, then NC-pair chunk (fastest,
+// so the CTAs sharing a weight tile run together and re-read it from L2).
+//   GU   (kinds 2): out[kind][p][i] = fold(xq_sorted[p] . W_kind[e][i]) * xs_sorted[p]
+//                   -- g and u of int4 expert_s4 (kind 0 gate, 1 up)
+//   down (kinds 1): part[tok(p)*topk + slot(p)][o] = (fold(aq[p] . Wd[e][o]) * as2[p]) * w
+struct S4Moe {
+    CUtensorMap tw[2];        // packed [E * rows][K / 2] per kind
+    const float *gs[2];       // group scales [E * rows][G] per kind
+    int E, rows, tiles, kinds, NC, G;
+    const int32_t *offsets, *active;
+    int down;                 // 0: GU, 1: down
+    float *out[2];            // GU: [P][rows] per kind
+    const float *row_scale;   // GU: xs_sorted; down: as2
+    const int32_t *pair_tok, *pair_slot;
+    const float *w;
+    float *part;
+    int topk;
+    static constexpr int STAGE_SMEM = 2 * 1032 * 4;
+    __device__ void prefetch() const {
+        tc::prefetch_tmap(&tw[0]);
+        if (kinds > 1) tc::prefetch_tmap(&tw[1]);
+    }
+    __device__ void stage(void *js) const {
+        int *so = static_cast<int *>(js);
+        for (int i = threadIdx.x; i <= E; i += blockDim.x) {
+            so[i] = offsets[i];
+            so[1032 + i] = active[i];
+        }
+    }
+    __device__ bool job(int j, const void *js, S4Job &jb) const {
+        const int *so = static_cast<const int *>(js), *act = so + 1032;
+        const int na = act[E];
+        for (int ai = 0; ai < na; ai++) {
+            const int e = act[ai];
+            const int p0 = so[e], cnt = so[e + 1] - p0;
+            const int nch = (cnt + NC - 1) / NC;
+            const int per = kinds * tiles * nch;
+            if (j >= per) {
+                j -= per;
+                continue;
+            }
+            const int kind = j / (tiles * nch), rem = j % (tiles * nch);
+            const int tile = rem / nch, chunk = rem % nch;
+            jb.a = &tw[kind];
+            jb.a_row = e * rows + tile * 128;
+            jb.n0 = tile * 128;
+            jb.b_row = p0 + chunk * NC;
+            jb.nv = min(NC, cnt - chunk * NC);
+            jb.scales = gs[kind] + (size_t)(e * rows + tile * 128) * G;
+            jb.e = e;
+            jb.kind = kind;
+            return true;
+        }
+        return false;
+    }
+    __device__ bool row_valid(const S4Job &jb, int r) const { return jb.n0 + r < rows; }
+    __device__ void store(const S4Job &jb, int r, int col, float acc) const {
+        const int pp = jb.b_row + col, n = jb.n0 + r;
+        const float y = __fmul_rn(acc, row_scale[pp]);
+        if (!down) {
+            out[jb.kind][(size_t)pp * rows + n] = y;
+        } else {
+            const int slot_row = pair_tok[pp] * topk + pair_slot[pp];
+            part[(size_t)slot_row * rows + n] = __fmul_rn(y, w[slot_row]);
+        }
+    }
+};
+
+template <class Prob>
+struct S4Params {
+    CUtensorMap ta;          // activations [rows][K], box NC x 128 B, 128-byte swizzle
+    int K, G;                // G = K / GROUP
     int *err;
+    Prob prob;
 };
 
 // Sign-extend the 16 nibbles of 8 packed bytes (k = 2j low nibble, 2j+1
@@ -65,13 +175,17 @@ __device__ __forceinline__ int4 unpack16_s4(uint2 w) {
     return make_int4(a, b, c, d);
 }
 
-template <int GROUP>
-__global__ void __launch_bounds__(S4_THREADS, 1) tc_s4_kernel(const __grid_constant__ S4Params p) {
+template <int GROUP, class Prob>
+__global__ void __launch_bounds__(S4_THREADS, 1)
+    tc_s4_kernel(const __grid_constant__ S4Params<Prob> p) {
     using C = S4Cfg<GROUP>;
     constexpr int S = S4_STAGES, SLOTS = C::SLOTS, NC = C::NC, NA = C::NA;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                 ~uintptr_t(1023));
+    // job-scheduling state the problem stages once (after the barriers)
+    void *job_smem = base + S * C::STAGE + 256;
+    const Prob &pr = p.prob;
     // stage s: [NA unpacked A tiles][B tile][packed staging]
     uint64_t *full = reinterpret_cast<uint64_t *>(base + S * C::STAGE);
     uint64_t *unpacked = full + S;
@@ -100,29 +214,30 @@ __global__ void __launch_bounds__(S4_THREADS, 1) tc_s4_kernel(const __grid_const
     tc::fence_after();
     const uint32_t tmem = *tslot;
     if (threadIdx.x == 0) {
-        tc::prefetch_tmap(&p.tw);
+        pr.prefetch();
         tc::prefetch_tmap(&p.ta);
     }
     pdl_trigger();
     pdl_wait();
+    pr.stage(job_smem);
+    __syncthreads();
 
     const int kblocks = p.K / 128;
-    const int jobs = p.tiles * p.chunks;
+    S4Job jb;
 
     if (warp == 0) {
         if (lane == 0) {
             uint32_t it = 0;
             bool ok = true;
-            for (int j = blockIdx.x; ok && j < jobs; j += gridDim.x) {
-                const int tile = j / p.chunks, chunk = j % p.chunks;
+            for (int j = blockIdx.x; ok && pr.job(j, job_smem, jb); j += gridDim.x) {
                 for (int kb = 0; kb < kblocks; kb++, it++) {
                     const uint32_t s = it % S;
                     if (it >= (uint32_t)S && !(ok = tc::mbar_wait(&empty[s], ((it / S) & 1) ^ 1, err)))
                         break;
                     uint8_t *st = base + s * C::STAGE;
                     tc::mbar_arrive_expect_tx(&full[s], C::PACKED + C::BTILE);
-                    tc::tma_load_2d(st + NA * C::ATILE + C::BTILE, &p.tw, kb * 64, tile * 128, &full[s]);
-                    tc::tma_load_2d(st + NA * C::ATILE, &p.ta, kb * 128, chunk * NC, &full[s]);
+                    tc::tma_load_2d(st + NA * C::ATILE + C::BTILE, jb.a, kb * 64, jb.a_row, &full[s]);
+                    tc::tma_load_2d(st + NA * C::ATILE, &p.ta, kb * 128, jb.b_row, &full[s]);
                 }
             }
         }
@@ -132,7 +247,7 @@ __global__ void __launch_bounds__(S4_THREADS, 1) tc_s4_kernel(const __grid_const
         const int t = threadIdx.x - 320;
         uint32_t it = 0;
         bool ok = true;
-        for (int j = blockIdx.x; ok && j < jobs; j += gridDim.x) {
+        for (int j = blockIdx.x; ok && pr.job(j, job_smem, jb); j += gridDim.x) {
             for (int kb = 0; kb < kblocks; kb++, it++) {
                 const uint32_t s = it % S;
                 if (!(ok = tc::mbar_wait(&full[s], (it / S) & 1, err))) break;
@@ -163,10 +278,8 @@ __global__ void __launch_bounds__(S4_THREADS, 1) tc_s4_kernel(const __grid_const
         if (lane == 0) {
             uint32_t it = 0, kbi = 0;   // kbi: K blocks issued (accumulator buffer sequence)
             bool ok = true;
-            for (int j = blockIdx.x; ok && j < jobs; j += gridDim.x) {
-                const int chunk = j % p.chunks;
-                const int nv = min(NC, p.M - chunk * NC);
-                const uint32_t idesc = tc::idesc_i8(128, (nv + 15) & ~15);
+            for (int j = blockIdx.x; ok && pr.job(j, job_smem, jb); j += gridDim.x) {
+                const uint32_t idesc = tc::idesc_i8(128, (jb.nv + 15) & ~15);
                 for (int kb = 0; kb < kblocks; kb++, it++, kbi++) {
                     const uint32_t s = it % S, buf = kbi & 1;
                     if (kbi >= 2 && !(ok = tc::mbar_wait(&tempty[buf], ((kbi >> 1) - 1) & 1, err))) break;
@@ -196,11 +309,10 @@ __global__ void __launch_bounds__(S4_THREADS, 1) tc_s4_kernel(const __grid_const
         constexpr int HC = NC / 2;   // columns per thread
         const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + half * HC;
         uint32_t kbi = 0;
-        for (int j = blockIdx.x; j < jobs; j += gridDim.x) {
-            const int tile = j / p.chunks, chunk = j % p.chunks;
-            const int n = tile * 128 + 32 * q + lane;
-            const bool nvalid = n < p.N;
-            const float *srow = p.scales + (size_t)(nvalid ? n : 0) * p.G;
+        for (int j = blockIdx.x; pr.job(j, job_smem, jb); j += gridDim.x) {
+            const int r = 32 * q + lane;
+            const bool nvalid = pr.row_valid(jb, r);
+            const float *srow = jb.scales + (size_t)(nvalid ? r : 0) * p.G;
             float acc[HC];
 #pragma unroll
             for (int c = 0; c < HC; c++) acc[c] = 0.0f;
@@ -232,10 +344,8 @@ __global__ void __launch_bounds__(S4_THREADS, 1) tc_s4_kernel(const __grid_const
             if (nvalid) {
 #pragma unroll
                 for (int c = 0; c < HC; c++) {
-                    const int m = chunk * NC + half * HC + c;
-                    if (m < p.M)
-                        p.out[(size_t)m * p.N + n] =
-                            p.dequant_a ? __fmul_rn(acc[c], p.dequant_a[m]) : acc[c];
+                    const int col = half * HC + c;
+                    if (col < jb.nv) pr.store(jb, r, col, acc[c]);
                 }
             }
         }
@@ -260,37 +370,84 @@ bool tc_s4_eligible(const int8_t *A, const uint8_t *Bp, const float *scales, siz
            M <= (size_t)INT32_MAX / 2 && N <= (size_t)INT32_MAX / 2 && K <= 65536;
 }
 
+template <class Prob>
+static int launch_s4(const S4Params<Prob> &p, size_t group, int grid, cudaStream_t st) {
+    if (group == 16) {
+        constexpr size_t smem = S4Cfg<16>::SMEM + Prob::STAGE_SMEM;
+        FOCR_CUDA_TRY(set_max_dynamic_smem((const void *)tc_s4_kernel<16, Prob>, (int)smem));
+        FOCR_CUDA_TRY(launch_pdl(tc_s4_kernel<16, Prob>, dim3(grid), dim3(S4_THREADS), smem, st, p));
+    } else {
+        constexpr size_t smem = S4Cfg<32>::SMEM + Prob::STAGE_SMEM;
+        FOCR_CUDA_TRY(set_max_dynamic_smem((const void *)tc_s4_kernel<32, Prob>, (int)smem));
+        FOCR_CUDA_TRY(launch_pdl(tc_s4_kernel<32, Prob>, dim3(grid), dim3(S4_THREADS), smem, st, p));
+    }
+    return FOCR_OK;
+}
+
 int launch_tc_s4(const int8_t *A, const uint8_t *Bp, const float *scales, size_t group, size_t M,
                  size_t K, size_t N, float *out, const float *dequant_a, int *err,
                  cudaStream_t st) {
-    S4Params p;
-    int rc = make_tmap_packed(&p.tw, Bp, N, K / 2);
+    S4Params<S4Raw> p;
     const int nc = group == 16 ? 32 : 64;
+    int rc = make_tmap_packed(&p.prob.tw, Bp, N, K / 2);
     if (!rc) rc = make_tmap_i8(&p.ta, A, M, K, (uint32_t)nc);
     if (rc) return rc;
-    p.scales = scales;
-    p.dequant_a = dequant_a;
-    p.out = out;
-    p.M = (int)M;
-    p.N = (int)N;
     p.K = (int)K;
     p.G = (int)(K / group);
-    p.tiles = (int)((N + 127) / 128);
-    p.chunks = (int)((M + nc - 1) / nc);
     p.err = err;
-    const long jobs = (long)p.tiles * p.chunks;
+    S4Raw &r = p.prob;
+    r.scales = scales;
+    r.dequant_a = dequant_a;
+    r.out = out;
+    r.M = (int)M;
+    r.N = (int)N;
+    r.G = p.G;
+    r.NC = nc;
+    r.tiles = (int)((N + 127) / 128);
+    r.chunks = (int)((M + nc - 1) / nc);
+    const long jobs = (long)r.tiles * r.chunks;
     const int sms = num_sms();
-    const int grid = (int)(jobs < sms ? jobs : sms);
-    if (group == 16) {
-        constexpr size_t smem = S4Cfg<16>::SMEM;
-        FOCR_CUDA_TRY(set_max_dynamic_smem((const void *)tc_s4_kernel<16>, (int)smem));
-        FOCR_CUDA_TRY(launch_pdl(tc_s4_kernel<16>, dim3(grid), dim3(S4_THREADS), smem, st, p));
-    } else {
-        constexpr size_t smem = S4Cfg<32>::SMEM;
-        FOCR_CUDA_TRY(set_max_dynamic_smem((const void *)tc_s4_kernel<32>, (int)smem));
-        FOCR_CUDA_TRY(launch_pdl(tc_s4_kernel<32>, dim3(grid), dim3(S4_THREADS), smem, st, p));
-    }
-    return FOCR_OK;
+    return launch_s4(p, group, (int)(jobs < sms ? jobs : sms), st);
+}
+
+// int4 expert gate+up or down over the layer's bucketed pairs (see S4Moe).
+// `b` is xq_sorted (GU) or aq (down) with b_rows >= 128 rows of K bytes.
+int launch_tc_s4_moe(bool down, int group, int E, int rows, int K, const uint8_t *w0,
+                     const float *s0, const uint8_t *w1, const float *s1, const int8_t *b,
+                     size_t b_rows, const int32_t *offsets, const int32_t *active,
+                     const float *row_scale, float *out0, float *out1, const int32_t *pair_tok,
+                     const int32_t *pair_slot, const float *wts, float *part, int topk, int *err,
+                     cudaStream_t st) {
+    S4Params<S4Moe> p;
+    const int nc = group == 16 ? 32 : 64;
+    S4Moe &m = p.prob;
+    int rc = make_tmap_packed(&m.tw[0], w0, (uint64_t)E * rows, K / 2);
+    if (!rc && !down) rc = make_tmap_packed(&m.tw[1], w1, (uint64_t)E * rows, K / 2);
+    if (!rc) rc = make_tmap_i8(&p.ta, b, b_rows, K, (uint32_t)nc);
+    if (rc) return rc;
+    p.K = K;
+    p.G = K / group;
+    p.err = err;
+    m.gs[0] = s0;
+    m.gs[1] = down ? nullptr : s1;
+    m.E = E;
+    m.rows = rows;
+    m.tiles = rows / 128;
+    m.kinds = down ? 1 : 2;
+    m.NC = nc;
+    m.G = p.G;
+    m.offsets = offsets;
+    m.active = active;
+    m.down = down ? 1 : 0;
+    m.out[0] = out0;
+    m.out[1] = out1;
+    m.row_scale = row_scale;
+    m.pair_tok = pair_tok;
+    m.pair_slot = pair_slot;
+    m.w = wts;
+    m.part = part;
+    m.topk = topk;
+    return launch_s4(p, (size_t)group, num_sms(), st);
 }
 
 }  // namespace focr
