@@ -119,9 +119,14 @@ __device__ bool sched_next(const P &p, DynIter &it, TcJob &jb) {
 // (tile_gate_up_kernel) -- so one MMA yields g and u for 64 intermediate rows
 // and a tile is 64 intermediate rows x all of K (half the work of a
 // 128-gate + 128-up tile, which keeps the persistent CTAs balanced).
+// epilogue scratch of one warp quad: both halves of one 16-column chunk plus
+// the chunk's column maxima
+constexpr int GU_EPI_ONE = 2 * 64 * 17 * 4 + 16 * 4;
+
 struct MoeGateUp {
     static constexpr int NA = 1, BN = 128, STAGES = 6;
-    static constexpr int EPI_SMEM = 2 * 64 * 17 * 4;   // both halves of one 16-column chunk
+    static constexpr int EPI_WARPS = 8;                 // two quads, alternate 16-column chunks
+    static constexpr int EPI_SMEM = 2 * GU_EPI_ONE;
     static constexpr int NBUF = 4;                      // TMEM accumulator buffers
     static constexpr int JOB_SMEM = MOE_JOB_SMEM;
     static constexpr uint32_t KERNEL_ID = 2;
@@ -144,7 +149,7 @@ struct MoeGateUp {
     }
 
     using Iter = DynIter;
-    __device__ void load_job_state(void *js) const { sched_stage(*this, js); }
+    __device__ void load_job_state(void *js) const { sched_stage(*this, js, EPI_WARPS); }
     __device__ void iter_init(Iter &it, void *js) const { sched_init<MoeGateUp>(it, js); }
     __device__ bool iter_next(Iter &it, TcJob &jb) const { return sched_next(*this, it, jb); }
 
@@ -199,15 +204,19 @@ struct MoeGateUp {
     // SwiGLU evaluations per thread, all loads before any store.
     __device__ void epilogue_done(int, int) const {}
     __device__ void before_loads(const TcJob &) const {}
-    __device__ void epilogue(const TcJob &jb, uint32_t tmem, int q, int lane, void *smem) const {
-        epilogue_impl<false>(jb, tmem, q, lane, smem, nullptr, nullptr);
+    __device__ void epilogue8(const TcJob &jb, uint32_t tmem, int q, int sub, int lane,
+                              void *smem) const {
+        epilogue_impl<false>(jb, tmem, q, lane, static_cast<uint8_t *>(smem) + sub * GU_EPI_ONE,
+                             nullptr, nullptr, sub, 2);
     }
     // AMAX: also fold the tile's per-column |act| max into amax (pairs) /
     // sh_amax (tokens) as non-negative float bits (NaN skipped, as fmaxf
     // drops it); `smem` then carries 16 extra ints after the accumulators.
+    // Warp quad `sub` of `nsub` takes the 16-column chunks sub, sub + nsub, ...
+    // with its own scratch (smem) and named barrier 1 + sub.
     template <bool AMAX>
     __device__ void epilogue_impl(const TcJob &jb, uint32_t tmem, int q, int lane, void *smem,
-                                  float *amax, float *sh_amax_) const {
+                                  float *amax, float *sh_amax_, int sub = 0, int nsub = 1) const {
         int *acc = static_cast<int *>(smem);   // [2 halves][64 rows][17] (padded)
         unsigned *cm = reinterpret_cast<unsigned *>(acc + 2 * 64 * 17);   // [16] column max
         const bool routed = jb.t0 >= 0;
@@ -222,14 +231,14 @@ struct MoeGateUp {
         const float *scl = routed ? xs_sorted : xs;
         const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
         if (AMAX && tid < 16) cm[tid] = 0u;
-        for (int c0 = 0; c0 < jb.t3; c0 += 16) {
+        for (int c0 = 16 * sub; c0 < jb.t3; c0 += 16 * nsub) {
             int v[16];
             tc::tmem_ld16(lane_base + c0, v);
             tc::tmem_ld_wait();
             int *mine = acc + (half * 64 + r_in) * 17;
 #pragma unroll
             for (int c = 0; c < 16; c++) mine[c] = v[c];
-            asm volatile("bar.sync 1, 128;" ::: "memory");
+            asm volatile("bar.sync %0, 128;" ::"r"(1 + sub) : "memory");
             const int lim = min(16, jb.t3 - c0);
             int ga[8], ua[8];
             float as[8];
@@ -256,7 +265,7 @@ struct MoeGateUp {
                     if (mag == mag) atomicMax(&cm[c], __float_as_uint(mag));
                 }
             }
-            asm volatile("bar.sync 1, 128;" ::: "memory");
+            asm volatile("bar.sync %0, 128;" ::"r"(1 + sub) : "memory");
             if (AMAX && tid < lim) {
                 float *am = routed ? amax : sh_amax_;
                 atomicMax(reinterpret_cast<unsigned *>(am + jb.t2 + c0 + tid), cm[tid]);
@@ -275,7 +284,12 @@ __device__ __forceinline__ float amax_scale(const float *am) {
 
 struct MoeDown {
     static constexpr int NA = 1, BN = 128, STAGES = 6, EPI_SMEM = 0, JOB_SMEM = MOE_JOB_SMEM;
+    static constexpr int EPI_WARPS = 8;   // two quads, alternate 16-column chunks
     static constexpr int NBUF = 4;
+    // the down weights and the job list (from the prep kernel, complete
+    // before the gate+up launch completes) are ready before the
+    // requantisation launch is: stream the first stages' weights early
+    static constexpr bool EARLY_A = true;
     static constexpr uint32_t KERNEL_ID = 3;
     TraceBuf trace;
     CUtensorMap td, tsd;
@@ -307,7 +321,7 @@ struct MoeDown {
     }
 
     using Iter = DynIter;
-    __device__ void load_job_state(void *js) const { sched_stage(*this, js); }
+    __device__ void load_job_state(void *js) const { sched_stage(*this, js, EPI_WARPS); }
     __device__ void iter_init(Iter &it, void *js) const { sched_init<MoeDown>(it, js); }
     __device__ bool iter_next(Iter &it, TcJob &jb) const { return sched_next(*this, it, jb); }
 
@@ -356,13 +370,18 @@ struct MoeDown {
 
     __device__ void epilogue_done(int, int) const {}
     __device__ void before_loads(const TcJob &) const {}
-    __device__ void epilogue(const TcJob &jb, uint32_t tmem, int q, int lane, void *) const {
+    __device__ void epilogue8(const TcJob &jb, uint32_t tmem, int q, int sub, int lane,
+                              void *smem) const {
+        epilogue(jb, tmem, q, lane, smem, sub, 2);
+    }
+    __device__ void epilogue(const TcJob &jb, uint32_t tmem, int q, int lane, void *,
+                             int sub = 0, int nsub = 1) const {
         const bool routed = jb.t0 >= 0;
         const int c = jb.t1 * 128 + 32 * q + lane;
         const bool valid = c < H;
         const float dsc = valid ? (routed ? down_s[(size_t)jb.t0 * H + c] : sh_down_s[c]) : 0.0f;
         const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
-        for (int c0 = 0; c0 < jb.t3; c0 += 16) {
+        for (int c0 = 16 * sub; c0 < jb.t3; c0 += 16 * nsub) {
             int v[16];
             tc::tmem_ld16(lane_base + c0, v);
             tc::tmem_ld_wait();
@@ -420,7 +439,7 @@ struct MoeDown {
 
 struct MoeFusedTC {
     static constexpr int NA = 1, BN = 128, STAGES = 6;
-    static constexpr int EPI_SMEM = MoeGateUp::EPI_SMEM + 16 * 4 + 16;
+    static constexpr int EPI_SMEM = GU_EPI_ONE + 16;
     static constexpr int NBUF = 4;
     static constexpr int JOB_SMEM = MOE_JOB_SMEM;
     static constexpr uint32_t KERNEL_ID = 5;
@@ -441,7 +460,7 @@ struct MoeFusedTC {
         d.prefetch();
     }
     using Iter = DynIter;
-    __device__ void load_job_state(void *js) const { sched_stage(g, js); }
+    __device__ void load_job_state(void *js) const { sched_stage(g, js, 4); }
     __device__ void iter_init(Iter &it, void *js) const { sched_init<MoeFusedTC>(it, js); }
     __device__ bool iter_next(Iter &it, TcJob &jb) const { return sched_next(*this, it, jb); }
 
@@ -500,8 +519,7 @@ struct MoeFusedTC {
         g.epilogue_impl<true>(jb, tmem, q, lane, smem, amax, sh_amax);
         // job accounting: the last gate+up job of this expert requantises it
         const int tid = 32 * q + lane;
-        int *flag = reinterpret_cast<int *>(static_cast<uint8_t *>(smem) + MoeGateUp::EPI_SMEM +
-                                            16 * 4);
+        int *flag = reinterpret_cast<int *>(static_cast<uint8_t *>(smem) + GU_EPI_ONE);
         const bool routed = jb.t0 >= 0;
         const int ei = routed ? jb.t0 : g.E;
         int p0, cnt;
@@ -589,7 +607,7 @@ struct MoeFusedTC {
 
 struct MoeFusedQ {
     static constexpr int NA = 1, BN = 128, STAGES = 6, XW = 4;
-    static constexpr int EPI_SMEM = MoeGateUp::EPI_SMEM + 16 * 4 + 16;
+    static constexpr int EPI_SMEM = GU_EPI_ONE + 16;
     static constexpr int NBUF = 4;
     static constexpr int JOB_SMEM = MOE_JOB_SMEM;
     static constexpr uint32_t KERNEL_ID = 6;

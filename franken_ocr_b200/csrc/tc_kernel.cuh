@@ -25,8 +25,8 @@
 // the TMA producer then loads only A), fence it for the async proxy and
 // arrive on the stage's full barrier (count 1 + XW).
 //
-// Roles (192 threads): warp 0 lane 0 issues TMA loads, warp 1 lane 0 issues
-// MMAs, warps 2..5 run the epilogue; epilogue warp w may only touch TMEM lanes
+// Roles (64 + 32 * (EPI_WARPS + XW) threads): warp 0 lane 0 issues TMA loads,
+// warp 1 lane 0 issues MMAs, warps 2.. run the epilogue; epilogue warp w may only touch TMEM lanes
 // 32*(w%4)..+31, so it owns accumulator rows 32*(w%4)..+31.  Accumulators are
 // held in P::NBUF TMEM buffers (job j uses buffer j % NBUF), so the epilogue
 // of job j overlaps the loads and MMAs of the following jobs.
@@ -63,9 +63,34 @@ struct TcXw<P, decltype((void)P::XW)> {
     static constexpr int value = P::XW;
 };
 
+// Epilogue warps: 4 (one per TMEM lane quarter) or 8 (two per quarter; a
+// problem with EPI_WARPS = 8 provides epilogue8(job, tmem, quarter, sub,
+// lane, smem) where sub = 0/1 picks its share of the job).
+template <class P, class = void>
+struct TcEw {
+    static constexpr int value = 4;
+};
+template <class P>
+struct TcEw<P, decltype((void)P::EPI_WARPS)> {
+    static constexpr int value = P::EPI_WARPS;
+};
+
+// EARLY_A: the problem's job state and A operand (weights) do not depend on
+// the preceding kernel (only B and the epilogue inputs do), so the producer
+// claims jobs and issues the A loads of the first STAGES stages before the
+// programmatic-dependency wait, and the B loads after it.
+template <class P, class = void>
+struct TcEarly {
+    static constexpr bool value = false;
+};
+template <class P>
+struct TcEarly<P, decltype((void)P::EARLY_A)> {
+    static constexpr bool value = P::EARLY_A;
+};
+
 template <class P>
 constexpr int tc_threads() {
-    return 192 + 32 * TcXw<P>::value;
+    return 64 + 32 * TcEw<P>::value + 32 * TcXw<P>::value;
 }
 
 template <class P>
@@ -76,7 +101,8 @@ constexpr size_t tc_smem_bytes() {
 
 template <class P>
 __global__ void __launch_bounds__(tc_threads<P>(), 1) tc_gemm_kernel(const __grid_constant__ P p) {
-    constexpr int NA = P::NA, BN = P::BN, S = P::STAGES, XW = TcXw<P>::value;
+    constexpr int NA = P::NA, BN = P::BN, S = P::STAGES, XW = TcXw<P>::value, EW = TcEw<P>::value;
+    static_assert(EW == 4 || EW == 8, "4 or 8 epilogue warps");
     constexpr uint32_t A_BYTES = 128 * 128, B_BYTES = BN * 128;
     constexpr uint32_t STAGE_BYTES = NA * A_BYTES + B_BYTES;
     constexpr int NBUF = P::NBUF;
@@ -108,7 +134,7 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1) tc_gemm_kernel(const __gri
         }
         for (int b = 0; b < NBUF; b++) {
             tc::mbar_init(&tfull[b], 1);
-            tc::mbar_init(&tempty[b], 4);
+            tc::mbar_init(&tempty[b], EW);
         }
         tc::fence_barrier_init();
     }
@@ -124,10 +150,16 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1) tc_gemm_kernel(const __gri
         trace_event(tb, KID, 0, TR_KERNEL_START);
     }
     pdl_trigger();
-    pdl_wait();   // inputs written by the preceding kernel are visible from here on
-    if (threadIdx.x == 0) trace_event(tb, KID, 0, TR_DEPS_READY);
+    constexpr bool EARLY = TcEarly<P>::value;
+    if (!EARLY) {
+        pdl_wait();   // inputs written by the preceding kernel are visible from here on
+        if (threadIdx.x == 0) trace_event(tb, KID, 0, TR_DEPS_READY);
+    }
     p.load_job_state(job_smem);
     __syncthreads();
+    // EARLY: every role except the producer waits here; the producer waits
+    // once its first STAGES stages of A are in flight
+    if (EARLY && threadIdx.x != 0) pdl_wait();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -136,12 +168,27 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1) tc_gemm_kernel(const __gri
             TcJob jb;
             typename P::Iter itr;
             p.iter_init(itr, job_smem);
+            // B loads held back until the dependency wait (EARLY only)
+            const CUtensorMap *pend_map[S];
+            int pend_x[S], pend_y[S];
+            for (int i = 0; i < S; i++) pend_map[i] = nullptr;
+            uint32_t npend = 0;
+            bool waited = !EARLY;
+            auto flush = [&]() {
+                pdl_wait();
+                trace_event(tb, KID, 0, TR_DEPS_READY);
+                for (uint32_t i = 0; i < npend; i++)
+                    if (pend_map[i]) tc::tma_load_2d(base + (i % S) * STAGE_BYTES + NA * A_BYTES, pend_map[i],
+                                    pend_x[i], pend_y[i], &full[i % S]);
+                waited = true;
+            };
             for (int j = 0; ok && p.iter_next(itr, jb); j++) {
                 p.before_loads(jb);   // cross-CTA inputs of the job are ready
                 trace_event(tb, KID, j, TR_JOB_LOAD);
                 const uint32_t bytes = NA * A_BYTES + (jb.b ? (uint32_t)jb.b_box * 128 : 0u);
                 for (int kb = 0; kb < jb.kblocks; kb++, it++) {
                     const uint32_t s = it % S;
+                    if (!waited && it >= (uint32_t)S) flush();
                     if (it >= (uint32_t)S && !(ok = tc::mbar_wait(&empty[s], ((it / S) & 1) ^ 1, err)))
                         break;
                     tc::mbar_arrive_expect_tx(&full[s], bytes);
@@ -155,9 +202,19 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1) tc_gemm_kernel(const __gri
                             tc::tma_load_2d(st + a * A_BYTES, jb.a[a], kb * tc::BK, jb.a_row,
                                             &full[s]);
                     }
-                    if (jb.b) tc::tma_load_2d(st + NA * A_BYTES, jb.b, kb * tc::BK, jb.b_row, &full[s]);
+                    if (jb.b) {
+                        if (waited) {
+                            tc::tma_load_2d(st + NA * A_BYTES, jb.b, kb * tc::BK, jb.b_row, &full[s]);
+                        } else {   // it < S: stage s == it
+                            pend_map[it] = jb.b;
+                            pend_x[it] = kb * tc::BK;
+                            pend_y[it] = jb.b_row;
+                            npend = it + 1;
+                        }
+                    }
                 }
             }
+            if (!waited) flush();
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -196,7 +253,7 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1) tc_gemm_kernel(const __gri
             }
         }
         __syncwarp();
-    } else if (XW && warp >= 6) {
+    } else if (XW && warp >= 2 + EW) {
         if constexpr (XW > 0) {
             // B producers: same stage sequence as the TMA producer
             uint32_t it = 0;
@@ -209,7 +266,7 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1) tc_gemm_kernel(const __gri
                     const uint32_t s = it % S;
                     if (it >= (uint32_t)S && !(ok = tc::mbar_wait(&empty[s], ((it / S) & 1) ^ 1, err)))
                         break;
-                    if (!jb.b) p.produce_b(jb, kb, base + s * STAGE_BYTES + NA * A_BYTES, warp - 6, lane);
+                    if (!jb.b) p.produce_b(jb, kb, base + s * STAGE_BYTES + NA * A_BYTES, warp - 2 - EW, lane);
                     tc::fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) tc::mbar_arrive(&full[s]);
@@ -217,7 +274,7 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1) tc_gemm_kernel(const __gri
             }
         }
     } else {
-        // epilogue warps 2..5
+        // epilogue warps 2 .. 2+EW-1
         TcJob jb;
         typename P::Iter itr;
         p.iter_init(itr, job_smem);
@@ -226,7 +283,11 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1) tc_gemm_kernel(const __gri
             if (!tc::mbar_wait(&tfull[buf], (j / NBUF) & 1, err)) break;
             tc::fence_after();
             if (threadIdx.x == 64) trace_event(tb, KID, j, TR_JOB_EPI);
-            p.epilogue(jb, tmem + (uint32_t)(buf * NA * BN), warp & 3, lane, epi_smem);
+            if constexpr (EW == 8)
+                p.epilogue8(jb, tmem + (uint32_t)(buf * NA * BN), warp & 3, (warp - 2) >> 2, lane,
+                            epi_smem);
+            else
+                p.epilogue(jb, tmem + (uint32_t)(buf * NA * BN), warp & 3, lane, epi_smem);
             tc::fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&tempty[buf]);
