@@ -286,10 +286,10 @@ struct MoeDown {
     static constexpr int NA = 1, BN = 128, STAGES = 6, EPI_SMEM = 0, JOB_SMEM = MOE_JOB_SMEM;
     static constexpr int EPI_WARPS = 8;   // two quads, alternate 16-column chunks
     static constexpr int NBUF = 4;
-    // the down weights and the job list (from the prep kernel, complete
-    // before the gate+up launch completes) are ready before the
-    // requantisation launch is: stream the first stages' weights early
-    static constexpr bool EARLY_A = true;
+    // EARLY_A (stream the first stages' weights before the dependency wait)
+    // measured no faster on config 2: the early loads only moved HBM time
+    // from the down kernel into the requantisation launch
+    static constexpr bool EARLY_A = false;
     static constexpr uint32_t KERNEL_ID = 3;
     TraceBuf trace;
     CUtensorMap td, tsd;
