@@ -185,6 +185,7 @@ struct MoeGateUp {
         jb.a[1] = nullptr;
         jb.a_kbt = (H + tc::BK - 1) / tc::BK;
         jb.b = routed ? &tx[bi] : &txt[bi];
+        jb.bx = nullptr;
         jb.b_box = box_rows(bi);
         // 128-row block index of (expert, 64-row tile) in the interleaved array
         jb.a_row = (routed ? e * itiles + rt : rt) * 128;
@@ -357,6 +358,7 @@ struct MoeDown {
         jb.a[1] = nullptr;
         jb.a_kbt = ((routed ? I : S) + tc::BK - 1) / tc::BK;
         jb.b = routed ? &ta[bi] : &tsa[bi];
+        jb.bx = nullptr;
         jb.b_box = box_rows(bi);
         jb.a_row = routed ? e * H + rt * 128 : rt * 128;
         jb.b_row = p0 + chunk * BN;
@@ -582,6 +584,33 @@ struct MoeFusedTC {
             asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(ready + ei * FLAG_STRIDE), "r"(1)
                          : "memory");
     }
+};
+
+// ---------------------------------------------------------------------------
+// MoeFusedTC with the down jobs' B loads split off: the TMA producer streams
+// every job's weights without ever waiting (a down job's weights do not
+// depend on the gate+up results), and one extra warp issues the down jobs'
+// B loads (the requantised act rows) once the expert's ready flag is set.
+// So the down weights of the first experts stream while the last gate+up
+// tiles drain, and no SM sits idle on a flag with its loads stopped.
+// ---------------------------------------------------------------------------
+
+struct MoeFusedTC2 : MoeFusedTC {
+    static constexpr int XW = 1;
+    static constexpr bool XB_TMA = true;
+    static constexpr uint32_t KERNEL_ID = 7;
+    __device__ void load_job_state(void *js) const { sched_stage(g, js, 4 + XW); }
+    __device__ void iter_init(Iter &it, void *js) const { sched_init<MoeFusedTC2>(it, js); }
+    __device__ bool iter_next(Iter &it, TcJob &jb) const { return sched_next(*this, it, jb); }
+    __device__ void make_job(int t, int chunk, const SchedSmem *sm, TcJob &jb) const {
+        MoeFusedTC::make_job(t, chunk, sm, jb);
+        if (jb.t1 & DOWN) {
+            jb.bx = jb.b;
+            jb.b = nullptr;
+        }
+    }
+    __device__ void before_loads(const TcJob &) const {}
+    __device__ void before_b(const TcJob &jb) const { MoeFusedTC::before_loads(jb); }
 };
 
 // ---------------------------------------------------------------------------
@@ -1160,7 +1189,8 @@ int moe_tc_experts(focr_moe_layer *L, const float *x, int m, const int32_t *idx,
     // FOCR_MOE_PATH=fusedq selects the single launch with on-load
     // requantisation (MoeFusedQ)
     const char *path_env = getenv("FOCR_MOE_PATH");
-    const int path = (path_env && !strcmp(path_env, "fusedq")) ? 2
+    const int path = (path_env && !strcmp(path_env, "fused2")) ? 3
+                     : (path_env && !strcmp(path_env, "fusedq")) ? 2
                      : ((path_env && !strcmp(path_env, "fused")) || getenv("FOCR_MOE_FUSED")) ? 1
                                                                                              : 0;
     const bool unfused = path == 0;
@@ -1201,6 +1231,20 @@ int moe_tc_experts(focr_moe_layer *L, const float *x, int m, const int32_t *idx,
         f.d.w = w;
         f.d.amax_rows = L->amax;
         f.d.sh_amax_rows = L->sh_amax;
+        f.te = te ? 1 : 0;
+        const int tiles = (int)L->E * (f.g.itiles + f.d.htiles) + (S ? f.g.stiles + f.d.htiles : 0);
+        return launch_tc(f, tiles < sms ? tiles : sms, st);
+    }
+    if (path == 3) {
+        MoeFusedTC2 f;
+        static_cast<MoeFusedTC &>(f) = s->fu;
+        f.g = s->gu;
+        f.g.T = m;
+        f.g.sh0 = sh0;
+        f.d = s->dn;
+        f.d.T = m;
+        f.d.sh0 = sh0;
+        f.d.w = w;
         f.te = te ? 1 : 0;
         const int tiles = (int)L->E * (f.g.itiles + f.d.htiles) + (S ? f.g.stiles + f.d.htiles : 0);
         return launch_tc(f, tiles < sms ? tiles : sms, st);

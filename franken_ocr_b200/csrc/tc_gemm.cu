@@ -103,6 +103,7 @@ struct RawIgemm {
         jb.a[0] = &ta;
         jb.a[1] = nullptr;
         jb.b = &tb;
+        jb.bx = nullptr;
         jb.b_box = BN;
         jb.a_kbt = 0;
         jb.a_row = mt * 128;

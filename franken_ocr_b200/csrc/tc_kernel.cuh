@@ -42,6 +42,7 @@ struct TcJob {
     const CUtensorMap *b;
     int a_row, b_row, kblocks, n_mma;
     int b_box;            // rows in the B box (TMA transfer size), >= n_mma
+    const CUtensorMap *bx;  // B map loaded by the extra warp (XB_TMA problems), or null
     int a_kbt;            // 0: A maps are row-major [rows, K]; else A is TMA-tiled with
                           // a_kbt K blocks per 128-row block (see tile_rows_kernel)
     int t0, t1, t2, t3;   // problem-specific tags (expert, tile, pair base, count)
@@ -86,6 +87,19 @@ struct TcEarly {
 template <class P>
 struct TcEarly<P, decltype((void)P::EARLY_A)> {
     static constexpr bool value = P::EARLY_A;
+};
+
+// XB_TMA: the XW (= 1) extra warp's lane 0 issues the B loads by TMA itself
+// for jobs that carry their B map in TcJob::bx (the producer then loads only
+// A); before a job's first B load it calls p.before_b(job), which may wait
+// for the B rows to be ready.  Jobs with bx null only get an arrive.
+template <class P, class = void>
+struct TcXbTma {
+    static constexpr bool value = false;
+};
+template <class P>
+struct TcXbTma<P, decltype((void)P::XB_TMA)> {
+    static constexpr bool value = P::XB_TMA;
 };
 
 template <class P>
@@ -254,7 +268,32 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1) tc_gemm_kernel(const __gri
         }
         __syncwarp();
     } else if (XW && warp >= 2 + EW) {
-        if constexpr (XW > 0) {
+        if constexpr (XW > 0 && TcXbTma<P>::value) {
+            if (lane == 0 && warp == 2 + EW) {
+                // B loads by TMA, after the job's B rows are ready
+                uint32_t it = 0;
+                bool ok = true;
+                TcJob jb;
+                typename P::Iter itr;
+                p.iter_init(itr, job_smem);
+                for (int j = 0; ok && p.iter_next(itr, jb); j++) {
+                    if (jb.bx) p.before_b(jb);
+                    for (int kb = 0; kb < jb.kblocks; kb++, it++) {
+                        const uint32_t s = it % S;
+                        if (it >= (uint32_t)S && !(ok = tc::mbar_wait(&empty[s], ((it / S) & 1) ^ 1, err)))
+                            break;
+                        if (jb.bx) {
+                            tc::mbar_arrive_expect_tx(&full[s], (uint32_t)jb.b_box * 128);
+                            tc::tma_load_2d(base + s * STAGE_BYTES + NA * A_BYTES, jb.bx, kb * tc::BK,
+                                            jb.b_row, &full[s]);
+                        } else {
+                            tc::mbar_arrive(&full[s]);
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+        } else if constexpr (XW > 0) {
             // B producers: same stage sequence as the TMA producer
             uint32_t it = 0;
             bool ok = true;

@@ -228,18 +228,21 @@ def test_forward_fused_launch(cuda, oracle, monkeypatch, m):
     L.close()
 
 
+@pytest.mark.parametrize("path", ["fusedq", "fused2"])
 @pytest.mark.parametrize("m", [2, 64, 300])
-def test_forward_fusedq_launch(cuda, oracle, monkeypatch, m):
-    """The single persistent launch with on-load requantisation
+def test_forward_fusedq_launch(cuda, oracle, monkeypatch, m, path):
+    """The single persistent launches -- on-load requantisation
     (FOCR_MOE_PATH=fusedq: the down GEMM's producer warps quantise the act rows
-    with the gate+up epilogue's per-row maximum) gives the same bits as the
-    oracle, for decode (forward) and prefill (ties-even) semantics, twice in a
-    row on one handle."""
+    with the gate+up epilogue's per-row maximum) and split B loads
+    (fused2: weights never wait, one warp loads each down job's act rows once
+    its expert is requantised) -- give the same bits as the oracle, for decode
+    (forward) and prefill (ties-even) semantics, twice in a row on one
+    handle."""
     from franken_ocr_b200 import synth
     from franken_ocr_b200.moe import MoeLayer
     from oracle.oracle import MoeOracle
 
-    monkeypatch.setenv("FOCR_MOE_PATH", "fusedq")
+    monkeypatch.setenv("FOCR_MOE_PATH", path)
     W = synth.moe_layer(813, shared_inter=1792)
     L = MoeLayer(W, max_tokens=m)
     O = MoeOracle(W)
