@@ -281,11 +281,16 @@ __global__ void __launch_bounds__(FT, 1) moe_m1_fused_kernel(const FusedArgs A) 
     };
 
     // ---- phase 0 ----
-    float xv[XPT];   // x in flight first
-#pragma unroll
-    for (int u = 0; u < XPT; u++) {
-        const int i = tid + FT * u;
-        xv[u] = i < H ? A.x[i] : 0.0f;
+    // Launched with programmatic stream serialisation: everything before
+    // pdl_wait() reads only weights (and this CTA's shared memory), so it
+    // overlaps the tail of the preceding kernel; x, the epoch word and every
+    // exchange buffer are touched after it.
+    pdl_trigger();
+    if (c < E && warp == FW - 1) {
+        // the router row this warp will dot with x, into L2 meanwhile
+        const float4 *g4 = reinterpret_cast<const float4 *>(A.router + (size_t)c * H);
+        for (int q = lane; q < (H >> 2); q += 32)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(g4 + q));
     }
     if (tid == 0) {
         FMARK(FM_START);
@@ -293,7 +298,6 @@ __global__ void __launch_bounds__(FT, 1) moe_m1_fused_kernel(const FusedArgs A) 
         M.nseg = act_segments(a0, a1, I, K, seg);
         for (int b = 0; b < 1 + NCH; b++) tc::mbar_init(&M.bars[b], 1);
         tc::fence_barrier_init();
-        M.ep = ld_relaxed_u32(A.epoch) + 1u;
         // Every barrier's byte count is fixed by the row ranges alone (the
         // route only picks source addresses), so all are armed now.
         tc::mbar_arrive_expect_tx(bar_dn, (uint32_t)dnc * dl);
@@ -313,6 +317,14 @@ __global__ void __launch_bounds__(FT, 1) moe_m1_fused_kernel(const FusedArgs A) 
     }
     if (dsh)
         for (int q = tid; q < dnc; q += FT) ds[q] = A.sh_down_s[d.c0 + q];
+    pdl_wait();
+    if (tid == 0) M.ep = ld_relaxed_u32(A.epoch) + 1u;
+    float xv[XPT];
+#pragma unroll
+    for (int u = 0; u < XPT; u++) {
+        const int i = tid + FT * u;
+        xv[u] = i < H ? A.x[i] : 0.0f;
+    }
 
     // router logit of expert e = c (last warp of the first E CTAs), pushed
     // into every CTA's mailbox; the warp reads the epoch itself so it does
@@ -726,12 +738,22 @@ int moe_decode_fused_m1(focr_moe_layer *L, const float *x, float *y, int32_t *id
     cfg.blockDim = dim3(FT);
     cfg.dynamicSmemBytes = A.lay.total;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    FOCR_CUDA_TRY(cudaLaunchKernelEx(&cfg, moe_m1_fused_kernel, A));
+    // FOCR_FUSED_M1_PDL=0: launch without the programmatic dependency
+    const char *pdl = getenv("FOCR_FUSED_M1_PDL");
+    cfg.numAttrs = (pdl && pdl[0] == '0') ? 1 : 2;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, moe_m1_fused_kernel, A);
+    if (e != cudaSuccess && cfg.numAttrs == 2) {
+        cudaGetLastError();   // this driver refuses the pair: plain cooperative launch
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, moe_m1_fused_kernel, A);
+    }
+    FOCR_CUDA_TRY(e);
     return FOCR_OK;
 }
 
