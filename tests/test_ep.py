@@ -161,7 +161,7 @@ def test_ep_multi_gpu_over_nccl(cuda):
         p.start()
     res = {}
     for _ in range(world):
-        r, ok = q.get(timeout=600)
+        r, ok = q.get(timeout=300)
         res[r] = ok
     for p in procs:
         p.join(60)
