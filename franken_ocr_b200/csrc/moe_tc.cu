@@ -121,7 +121,7 @@ __device__ bool sched_next(const P &p, DynIter &it, TcJob &jb) {
 // 128-gate + 128-up tile, which keeps the persistent CTAs balanced).
 // epilogue scratch of one warp quad: both halves of one 16-column chunk plus
 // the chunk's column maxima
-constexpr int GU_EPI_ONE = 2 * 64 * 17 * 4 + 16 * 4;
+constexpr int GU_EPI_ONE = 2 * 64 * 17 * 4 + 32 * 4;
 
 struct MoeGateUp {
     static constexpr int NA = 1, BN = 128, STAGES = 6;
@@ -219,7 +219,7 @@ struct MoeGateUp {
     __device__ void epilogue_impl(const TcJob &jb, uint32_t tmem, int q, int lane, void *smem,
                                   float *amax, float *sh_amax_, int sub = 0, int nsub = 1) const {
         int *acc = static_cast<int *>(smem);   // [2 halves][64 rows][17] (padded)
-        unsigned *cm = reinterpret_cast<unsigned *>(acc + 2 * 64 * 17);   // [16] column max
+        unsigned *cm = reinterpret_cast<unsigned *>(acc + 2 * 64 * 17);   // [4 warps][8] column max
         const bool routed = jb.t0 >= 0;
         const int rows = routed ? I : S;
         const int tid = 32 * q + lane;          // 0..127
@@ -231,7 +231,6 @@ struct MoeGateUp {
         float *out = routed ? act : sh_act;
         const float *scl = routed ? xs_sorted : xs;
         const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
-        if (AMAX && tid < 16) cm[tid] = 0u;
         for (int c0 = 16 * sub; c0 < jb.t3; c0 += 16 * nsub) {
             int v[16];
             tc::tmem_ld16(lane_base + c0, v);
@@ -261,16 +260,27 @@ struct MoeGateUp {
             for (int k = 0; k < 8; k++) {
                 const int c = col0 + 2 * k;
                 if (c < lim) out[(size_t)(jb.t2 + c0 + c) * rows + i] = res[k];
-                if (AMAX && c < lim) {
-                    const float mag = fabsf(res[k]);
-                    if (mag == mag) atomicMax(&cm[c], __float_as_uint(mag));
+            }
+            if (AMAX) {
+                // column c = col0 + 2k lives in the two warps with that col0:
+                // warp max by shuffles (fmaxf drops NaN), then the pair combined
+                const int w4 = q;   // this quad's warp 0..3 (col0 = w4 >> 1)
+#pragma unroll
+                for (int k = 0; k < 8; k++) {
+                    float mag = (col0 + 2 * k) < lim ? fabsf(res[k]) : 0.0f;
+                    if (mag != mag) mag = 0.0f;
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1)
+                        mag = fmaxf(mag, __shfl_xor_sync(0xffffffffu, mag, o));
+                    if (lane == 0) cm[w4 * 8 + k] = __float_as_uint(mag);
                 }
             }
             asm volatile("bar.sync %0, 128;" ::"r"(1 + sub) : "memory");
             if (AMAX && tid < lim) {
+                const int cc = tid & 1, k = tid >> 1;   // column tid = cc + 2k
+                const unsigned mx = max(cm[(2 * cc) * 8 + k], cm[(2 * cc + 1) * 8 + k]);
                 float *am = routed ? amax : sh_amax_;
-                atomicMax(reinterpret_cast<unsigned *>(am + jb.t2 + c0 + tid), cm[tid]);
-                cm[tid] = 0u;
+                atomicMax(reinterpret_cast<unsigned *>(am + jb.t2 + c0 + tid), mx);
             }
         }
     }
