@@ -185,3 +185,17 @@ int main() {
                    check=True)
     out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout
     assert out.strip() == "0"
+
+
+def test_nccl_unique_id_is_128_bytes_or_unsupported():
+    """The communicator bootstrap loads NCCL at run time: either a 128-byte
+    id comes back, or FOCR_E_UNSUPPORTED says why (no library)."""
+    import ctypes as C
+
+    from franken_ocr_b200._lib import FOCR_E_UNSUPPORTED, FOCR_OK, lib
+
+    buf = C.create_string_buffer(128)
+    rc = lib.focr_nccl_unique_id(buf)
+    assert rc in (FOCR_OK, FOCR_E_UNSUPPORTED)
+    if rc == FOCR_E_UNSUPPORTED:
+        assert b"nccl" in lib.focr_last_error().lower()
