@@ -86,6 +86,8 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __grid_constant_
     __shared__ float red[8];
     __shared__ float s_scale, s_inv;
     __shared__ int s_dest[8], s_pos[8];
+    __shared__ int s_before[FOCR_MAX_WORLD], s_total[FOCR_MAX_WORLD];
+    extern __shared__ int s_route[];   // [T * K] owner of each pair (-1: empty slot)
     const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int H = a.H, K = a.K;
     // quantise row t: scale = amax/127 (1 if 0), q = clamp(round_half_away(v * (1/scale)))
@@ -102,24 +104,58 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __grid_constant_
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if (lane == 0) red[warp] = m;
-    // destinations and positions of this token's pairs
-    if (tid < K) {
-        const int b = t * K + tid;
+    // destinations and positions of this token's pairs: the routing table is
+    // staged in shared memory and every thread counts a stride of it (a
+    // per-slot serial scan of global memory costs one load latency per pair)
+    const int P = a.T * K;
+    for (int b = tid; b < P; b += 256) {
         const int e = a.idx[b];
-        int dest = -1;
-        if (e >= 0) {
-            dest = e / a.e_local;
-            if (dest >= a.world) {
-                atomicOr(a.err, 2);
-                dest = -1;
+        int dest = e >= 0 ? e / a.e_local : -1;
+        if (dest >= a.world) {
+            atomicOr(a.err, 2);
+            dest = -1;
+        }
+        s_route[b] = dest;
+    }
+    if (tid < FOCR_MAX_WORLD) {
+        s_before[tid] = 0;
+        s_total[tid] = 0;
+    }
+    __syncthreads();
+    {
+        // pairs before this token's (b < t*K) per owner; block 0 also counts all
+        int cb[FOCR_MAX_WORLD] = {}, ca[FOCR_MAX_WORLD] = {};
+        const int lim = t == 0 ? P : t * K;
+        for (int b = tid; b < lim; b += 256) {
+            const int d = s_route[b];
+#pragma unroll
+            for (int k = 0; k < FOCR_MAX_WORLD; k++) {
+                cb[k] += (d == k) & (b < t * K);
+                ca[k] += d == k;
             }
         }
-        int pos = 0;
-        if (dest >= 0)
-            for (int q2 = 0; q2 < b; q2++) {
-                const int f = a.idx[q2];
-                pos += f >= 0 && f / a.e_local == dest;
+#pragma unroll
+        for (int k = 0; k < FOCR_MAX_WORLD; k++) {
+            if (k >= a.world) break;
+            int x = cb[k], y = ca[k];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                x += __shfl_xor_sync(0xffffffffu, x, o);
+                y += __shfl_xor_sync(0xffffffffu, y, o);
             }
+            if (lane == 0 && x) atomicAdd(&s_before[k], x);
+            if (lane == 0 && y) atomicAdd(&s_total[k], y);
+        }
+    }
+    __syncthreads();
+    if (tid < K) {
+        const int b = t * K + tid;
+        const int dest = s_route[b];
+        int pos = 0;
+        if (dest >= 0) {
+            pos = s_before[dest];
+            for (int j = 0; j < tid; j++) pos += s_route[t * K + j] == dest;
+        }
         s_dest[tid] = dest;
         s_pos[tid] = pos;
         a.rows[b] = dest < 0 ? -1 : dest * a.cap + pos;
@@ -163,14 +199,8 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __grid_constant_
         d[c] = src[c];
     }
     // block 0: how many pairs this rank sends each owner
-    if (t == 0 && tid < a.world) {
-        int c = 0;
-        for (int b = 0; b < a.T * K; b++) {
-            const int f = a.idx[b];
-            c += f >= 0 && f / a.e_local == tid;
-        }
-        reinterpret_cast<int *>(a.peer[tid] + a.off_counts)[a.rank] = c;
-    }
+    if (t == 0 && tid < a.world)
+        reinterpret_cast<int *>(a.peer[tid] + a.off_counts)[a.rank] = s_total[tid];
 }
 
 struct EpSignalArgs {
@@ -601,7 +631,8 @@ int focr_ep_dispatch(focr_ep *ep, const float *x, size_t T, const int32_t *idx, 
         a.own_xs = L->xs + sh0;
         a.rows = ep->rows;
         a.err = L->err;
-        ep_dispatch_kernel<<<(unsigned)T, 256, 0, st>>>(a);
+        const size_t route_smem = T * ep->topk * sizeof(int);   // <= 32 KB (world * cap <= 8192)
+        ep_dispatch_kernel<<<(unsigned)T, 256, route_smem, st>>>(a);
         FOCR_CUDA_TRY(cudaGetLastError());
     } else {
         // nothing to send: every owner still needs this rank's count (0)
