@@ -237,7 +237,8 @@ def run_ours(args, ws, rank, local):
         return run_ep(args, ws, rank, local)
     hbm_peak, peak_kind = peaks()
     if args.workload == "config1":
-        int8_peak, rows = igemm_sweep(dev, hbm_peak, peak_kind, reps=max(1, args.steps))
+        shape = tuple(int(v) for v in args.shape.split("x")) if args.shape else None
+        int8_peak, rows = igemm_sweep(dev, hbm_peak, peak_kind, reps=max(1, args.steps), shape=shape)
         tot_us = sum(r["us"] for r in rows)
         print(json.dumps({
             "metric": "int8 GEMM sweep (config 1): sum of per-shape times", "value": tot_us,
@@ -431,7 +432,7 @@ def m1_decode(dev, hbm_peak, peak_kind, steps=200):
             "cuda_graph": graph is not None, "l2": f"ring of {R} layers x 220 MB (> L2)"}
 
 
-def igemm_sweep(dev, hbm_peak, peak_kind, reps=5):
+def igemm_sweep(dev, hbm_peak, peak_kind, reps=5, shape=None):
     """Config 1: the raw int8 x int8 -> int32 GEMM sweep through
     focr_igemm_s8s8 on device tensors (out += A.B^T), each shape timed as one
     CUDA graph of `reps` calls.  Each shape's floor is
@@ -463,16 +464,21 @@ def igemm_sweep(dev, hbm_peak, peak_kind, reps=5):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) * 1e3 / reps
 
-    us_peak = timed(8192, 8192, 16384)
-    int8_peak = 2 * 8192 * 8192 * 16384 / us_peak / 1e6   # TOPS
+    if shape is None:
+        us_peak = timed(8192, 8192, 16384)
+        int8_peak = 2 * 8192 * 8192 * 16384 / us_peak / 1e6   # TOPS
+        shapes = [(m, n, k) for (n, k) in [(1792, 1280), (1280, 896), (129280, 1280)]
+                  for m in (1, 8, 64, 512, 4096)]
+    else:   # one shape (a small case for a profiler capture); no peak shape
+        int8_peak = None
+        shapes = [shape]
     rows = []
-    for (n, k) in [(1792, 1280), (1280, 896), (129280, 1280)]:
-        for m in (1, 8, 64, 512, 4096):
-            us = timed(m, n, k)
-            ops, byt = 2 * m * n * k, m * k + n * k + 8 * m * n
-            floor_us = max(byt / hbm_peak / 1e3, ops / int8_peak / 1e6)
-            rows.append({"m": m, "n": n, "k": k, "us": round(us, 2), "tops": ops / us / 1e6,
-                         "gbs": byt / us / 1e3, "floor_us": floor_us, "frac": floor_us / us})
+    for (m, n, k) in shapes:
+        us = timed(m, n, k)
+        ops, byt = 2 * m * n * k, m * k + n * k + 8 * m * n
+        floor_us = max(byt / hbm_peak / 1e3, ops / int8_peak / 1e6 if int8_peak else 0.0)
+        rows.append({"m": m, "n": n, "k": k, "us": round(us, 2), "tops": ops / us / 1e6,
+                     "gbs": byt / us / 1e3, "floor_us": floor_us, "frac": floor_us / us})
     return int8_peak, rows
 
 
@@ -936,6 +942,8 @@ def main():
     ap.add_argument("--workload", default="config2", choices=["config2", "config0", "config1", "config3", "config3_batch", "config4"],
                     help="config0: only the single-token layer; config1: the raw igemm sweep; "
                          "config3: the 12-layer decoder")
+    ap.add_argument("--shape", default=None,
+                    help="config1 only: time one MxNxK shape (e.g. 4096x4096x4096) instead of the sweep")
     args = ap.parse_args()
     ws, rank, local = dist_init()
     if args.impl == "reference":
