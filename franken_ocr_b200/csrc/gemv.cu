@@ -285,6 +285,165 @@ int launch_gemv_q1(const float *x, size_t K, bool te, const int8_t *B, const flo
     return FOCR_OK;
 }
 
+constexpr int GEMV_S4Q1_MAX_K = 2048;
+constexpr int S4Q1_ROWS = 4;   // weight rows per warp pass
+constexpr int S4Q1_U = 8;      // 16-byte chunks per lane per pass (ROWS * K / 32 <= 32 * U)
+
+// Int4 decode GEMV with in-kernel activation quantisation (int4.rs:304-343
+// for one row).  A warp takes S4Q1_ROWS weight rows per pass and spreads
+// their 16-byte chunks (32 nibbles: one group of 32 or two of 16) over its
+// lanes, so every chunk of the pass is in flight at once; the first pass's
+// chunks are requested before the block quantises x (the amax, scale and
+// rounding of quantize_rows_kernel), hiding that prologue behind the weight
+// stream.  Each chunk yields the exact integer dot of its group(s) and
+// scale * (f32)dot; the per-group terms go to shared memory and lane r folds
+// row r in increasing group order (acc = acc + t_g from 0.0, each step
+// rounded), as the reference's sequential group loop does, then scales by
+// the activation scale.  Optionally the block reduces its logits to one
+// first-maximum partial (argmax_row order, NaN skipped).
+template <int GROUP>
+__global__ void __launch_bounds__(GEMV_THREADS, 4)   // 4 blocks per SM: one wave at vocab-shard sizes
+gemv_s4_q1_kernel(const float *__restrict__ x, int K, int te, const uint8_t *__restrict__ Bp,
+                  const float *__restrict__ scales, int N, float *__restrict__ y,
+                  float *__restrict__ part_v, int *__restrict__ part_i) {
+    constexpr int WARPS = GEMV_THREADS / 32, GMAX = GEMV_S4Q1_MAX_K / GROUP, R = S4Q1_ROWS,
+                  U = S4Q1_U;
+    constexpr int SPC = 32 / GROUP;   // groups per 16-byte chunk (1 or 2)
+    __shared__ int4 sA[GEMV_S4Q1_MAX_K / 16];
+    __shared__ __align__(16) float tw[WARPS][R][GMAX];
+    __shared__ float red[WARPS];
+    __shared__ float s_sc, s_inv;
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int C = K >> 5, G = K / GROUP, Kb = K >> 1;
+    const int warp = blockIdx.x * WARPS + wib;
+    const int nwarps = gridDim.x * WARPS;
+    int4 wv[U];
+    float sv[U][SPC];
+    auto issue = [&](int n0) {
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int i = lane + 32 * u;
+            if (i < R * C) {
+                const int r = i / C, c = i - r * C;
+                const int n = min(n0 + r, N - 1);
+                wv[u] = ld_stream16(Bp + (size_t)n * Kb + (size_t)c * 16);
+#pragma unroll
+                for (int h = 0; h < SPC; h++) sv[u][h] = __ldg(scales + (size_t)n * G + SPC * c + h);
+            }
+        }
+    };
+    int n0 = warp * R;
+    if (n0 < N) issue(n0);
+    // quantise x (every block)
+    const float4 *x4 = reinterpret_cast<const float4 *>(x);
+    float m = 0.0f;
+    for (int i = threadIdx.x; i < K / 4; i += blockDim.x) {
+        const float4 v = x4[i];
+        m = fmaxf(m, fabsf(v.x));
+        m = fmaxf(m, fabsf(v.y));
+        m = fmaxf(m, fabsf(v.z));
+        m = fmaxf(m, fabsf(v.w));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[wib] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float a = 0.0f;
+        for (int w = 0; w < WARPS; w++) a = fmaxf(a, red[w]);
+        const float sc = a > 0.0f ? __fdiv_rn(a, 127.0f) : 1.0f;
+        s_sc = sc;
+        s_inv = __fdiv_rn(1.0f, sc);
+    }
+    __syncthreads();
+    const float inv = s_inv, as = s_sc;
+    int8_t *sq = reinterpret_cast<int8_t *>(sA);
+    for (int i = threadIdx.x; i < K / 4; i += blockDim.x) {
+        const float4 v = x4[i];
+        sq[4 * i] = (int8_t)quant_i8(v.x, inv, te != 0);
+        sq[4 * i + 1] = (int8_t)quant_i8(v.y, inv, te != 0);
+        sq[4 * i + 2] = (int8_t)quant_i8(v.z, inv, te != 0);
+        sq[4 * i + 3] = (int8_t)quant_i8(v.w, inv, te != 0);
+    }
+    __syncthreads();
+    int bi = -1;   // this thread's first-maximum candidate
+    float bv = 0.0f;
+    for (; n0 < N; n0 += nwarps * R) {
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int i = lane + 32 * u;
+            if (i < R * C) {
+                const int r = i / C, c = i - r * C;
+                const int4 a0 = sA[2 * c], a1 = sA[2 * c + 1];   // k = 32c .. 32c + 31
+                const uint32_t ww[4] = {(uint32_t)wv[u].x, (uint32_t)wv[u].y, (uint32_t)wv[u].z,
+                                        (uint32_t)wv[u].w};
+                const int aa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                int d[2] = {0, 0};   // k 0..15 / 16..31 of the chunk
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    int lo, hi;
+                    unpack8_s4(ww[q], lo, hi);
+                    d[q >> 1] = dp4a_ss(aa[2 * q + 1], hi, dp4a_ss(aa[2 * q], lo, d[q >> 1]));
+                }
+                if (SPC == 1) {
+                    tw[wib][r][c] = __fmul_rn(sv[u][0], (float)(d[0] + d[1]));
+                } else {
+                    tw[wib][r][2 * c] = __fmul_rn(sv[u][0], (float)d[0]);
+                    tw[wib][r][2 * c + 1] = __fmul_rn(sv[u][SPC - 1], (float)d[1]);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane < R && n0 + lane < N) {
+            const float *t = tw[wib][lane];
+            float acc = 0.0f;
+            int g = 0;
+            if ((G & 3) == 0) {
+                const float4 *t4 = reinterpret_cast<const float4 *>(t);
+#pragma unroll 4
+                for (; g < G; g += 4) {
+                    const float4 q4 = t4[g >> 2];
+                    acc = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(acc, q4.x), q4.y), q4.z), q4.w);
+                }
+            }
+            for (; g < G; g++) acc = __fadd_rn(acc, t[g]);
+            const float v = __fmul_rn(acc, as);
+            y[n0 + lane] = v;
+            if (v == v) better(bi, bv, n0 + lane, v);
+        }
+        __syncwarp();
+        if (n0 + nwarps * R < N) issue(n0 + nwarps * R);
+    }
+    if (part_v) {
+        block_best(bi, bv);
+        if (threadIdx.x == 0) {
+            part_v[blockIdx.x] = bv;
+            part_i[blockIdx.x] = bi;
+        }
+    }
+}
+
+int launch_gemv_s4_q1(const float *x, size_t K, bool te, const uint8_t *Bp, const float *scales,
+                      size_t group, size_t N, float *y, cudaStream_t st, float *part_v,
+                      int *part_i, int *parts) {
+    if (N == 0) return FOCR_OK;
+    if ((group != 16 && group != 32) || K % 32 || K == 0 || K > GEMV_S4Q1_MAX_K ||
+        S4Q1_ROWS * (K / 32) > 32 * S4Q1_U ||
+        ((uintptr_t)x % 16) || ((uintptr_t)Bp % 16) || ((uintptr_t)scales % 16) ||
+        N > (size_t)INT32_MAX)
+        return FOCR_E_UNSUPPORTED;
+    const int grid = gemv_grid(N, (GEMV_THREADS / 32) * S4Q1_ROWS);
+    if (parts) *parts = grid;
+    if (group == 32)
+        gemv_s4_q1_kernel<32><<<grid, GEMV_THREADS, 0, st>>>(x, (int)K, te ? 1 : 0, Bp, scales,
+                                                              (int)N, y, part_v, part_i);
+    else
+        gemv_s4_q1_kernel<16><<<grid, GEMV_THREADS, 0, st>>>(x, (int)K, te ? 1 : 0, Bp, scales,
+                                                              (int)N, y, part_v, part_i);
+    FOCR_CUDA_TRY(cudaGetLastError());
+    return FOCR_OK;
+}
+
 int launch_gemv_s4(const int8_t *A, const uint8_t *Bp, const float *scales, size_t group,
                    size_t M, size_t K, size_t N, float *out, const float *dequant_a,
                    cudaStream_t st) {

@@ -198,6 +198,45 @@ int launch_quantize_rows(const float *x, size_t M, size_t K, bool te, int8_t *xq
 // 16-byte aligned x and B; returns FOCR_E_UNSUPPORTED otherwise.
 int launch_gemv_q1(const float *x, size_t K, bool te, const int8_t *B, const float *w_scale,
                    size_t N, float *y, cudaStream_t st);
+// First maximum (NaN skipped) -- sampler::argmax_row (sampler.rs:168-186).
+// The rule "greater value, or equal value at a lower index" is associative
+// and commutative, so the row is split: block (c, r) reduces columns
+// [c * span, (c + 1) * span) of row r to one (value, index) partial, and
+// argmax_combine_kernel reduces a row's partials.  Index -1 = all NaN.
+__device__ __forceinline__ void better(int &bi, float &bv, int oi, float ov) {
+    if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) {
+        bi = oi;
+        bv = ov;
+    }
+}
+
+__device__ __forceinline__ void block_best(int &bi, float &bv) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        better(bi, bv, __shfl_xor_sync(0xffffffffu, bi, o), __shfl_xor_sync(0xffffffffu, bv, o));
+    if ((threadIdx.x & 31) == 0) {
+        sv[threadIdx.x >> 5] = bv;
+        si[threadIdx.x >> 5] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0)
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++) better(bi, bv, si[w], sv[w]);
+}
+
+// One activation row against packed int4 weights, quantised inside the GEMV:
+// y[n] = (sum over groups g, in increasing g, of scale[n,g] * f32(dot_g)) *
+// a_scale -- the values of launch_quantize_rows + launch_gemv_s4 with the
+// activation scale as dequant_a, in one launch.  Needs group 16 or 32,
+// K % 32 == 0, K <= 2048 and 16-byte aligned x, Bp and scales; returns
+// FOCR_E_UNSUPPORTED otherwise.
+// With part_v/part_i non-null the launch also reduces its logits to one
+// first-maximum (value, index) partial per block (*parts of them, indices
+// relative to row 0), for argmax_combine_kernel.
+int launch_gemv_s4_q1(const float *x, size_t K, bool te, const uint8_t *Bp, const float *scales,
+                      size_t group, size_t N, float *y, cudaStream_t st, float *part_v = nullptr,
+                      int *part_i = nullptr, int *parts = nullptr);
 // tcgen05 path of the packed int4 GEMM (tc_s4.cu): M >= 64 (32 for groups of
 // 16), N >= 128, K % 128 == 0, 16-byte aligned operands.
 bool tc_s4_eligible(const int8_t *A, const uint8_t *Bp, const float *scales, size_t group,

@@ -19,36 +19,13 @@ struct focr_lmhead {
     float *logits = nullptr;   // [T][rows]
     float *bv = nullptr;       // [T]
     int32_t *bi = nullptr;     // [T]
+    float *pv = nullptr;       // int4 head, one row: per-block top-1 partials of the GEMV
+    int *pi = nullptr;
 };
 
+constexpr int LMHEAD_MAX_PARTS = 4096;   // >= the GEMV grid (8 blocks per SM)
+
 namespace focr {
-
-// First maximum (NaN skipped) -- sampler::argmax_row (sampler.rs:168-186).
-// The rule "greater value, or equal value at a lower index" is associative
-// and commutative, so the row is split: block (c, r) reduces columns
-// [c * span, (c + 1) * span) of row r to one (value, index) partial, and
-// argmax_combine_kernel reduces a row's partials.  Index -1 = all NaN.
-__device__ __forceinline__ void better(int &bi, float &bv, int oi, float ov) {
-    if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) {
-        bi = oi;
-        bv = ov;
-    }
-}
-
-__device__ __forceinline__ void block_best(int &bi, float &bv) {
-    __shared__ float sv[32];
-    __shared__ int si[32];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-        better(bi, bv, __shfl_xor_sync(0xffffffffu, bi, o), __shfl_xor_sync(0xffffffffu, bv, o));
-    if ((threadIdx.x & 31) == 0) {
-        sv[threadIdx.x >> 5] = bv;
-        si[threadIdx.x >> 5] = bi;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0)
-        for (int w = 1; w < (int)(blockDim.x >> 5); w++) better(bi, bv, si[w], sv[w]);
-}
 
 __global__ void argmax_part_kernel(const float *__restrict__ logits, int n, int span,
                                    float *__restrict__ part_v, int *__restrict__ part_i) {
@@ -108,7 +85,7 @@ extern "C" {
 
 int focr_lmhead_destroy(focr_lmhead *h) {
     if (!h) return FOCR_OK;
-    void *ptrs[] = {h->w, h->wp, h->scales, h->x, h->xq, h->xs, h->logits, h->bv, h->bi};
+    void *ptrs[] = {h->w, h->wp, h->scales, h->x, h->xq, h->xs, h->logits, h->bv, h->bi, h->pv, h->pi};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     delete h;
@@ -161,13 +138,21 @@ int focr_lmhead_top1(focr_lmhead *h, const float *x, size_t m, float *best_val,
     }
     float *dlog = (mem == FOCR_MEM_DEVICE && logits) ? logits : h->logits;
     int rc = FOCR_E_UNSUPPORTED;
-    if (h->group) {
+    int parts = 0;   // > 0: the GEMV left per-block top-1 partials in h->pv / h->pi
+    if (h->group && m == 1 && num_sms() * 8 <= LMHEAD_MAX_PARTS) {
+        // quantisation inside the GEMV, first-maximum partials in its epilogue
+        rc = launch_gemv_s4_q1(dx, h->hidden, false, h->wp, h->scales, h->group, h->rows, dlog, st,
+                               h->pv, h->pi, &parts);
+        if (rc && rc != FOCR_E_UNSUPPORTED) return rc;
+        if (rc) parts = 0;
+    }
+    if (!h->group) {
+        if (m == 1) rc = launch_gemv_q1(dx, h->hidden, false, h->w, h->scales, h->rows, dlog, st);
+    } else if (rc) {
         // int4 head: logits = igemm_s4s8_packed(Q(x), W) * a_scale
         rc = launch_quantize_rows(dx, m, h->hidden, false, h->xq, h->xs, st);
         if (!rc) rc = launch_gemv_s4(h->xq, h->wp, h->scales, h->group, m, h->hidden, h->rows, dlog,
                                      h->xs, st);
-    } else if (m == 1) {
-        rc = launch_gemv_q1(dx, h->hidden, false, h->w, h->scales, h->rows, dlog, st);
     }
     if (rc && !h->group) {
         rc = launch_quantize_rows(dx, m, h->hidden, false, h->xq, h->xs, st);
@@ -176,8 +161,13 @@ int focr_lmhead_top1(focr_lmhead *h, const float *x, size_t m, float *best_val,
     if (rc) return rc;
     float *dbv = mem == FOCR_MEM_DEVICE ? best_val : h->bv;
     int32_t *dbi = mem == FOCR_MEM_DEVICE ? best_idx : h->bi;
-    rc = launch_argmax_rows(dlog, (int)m, (int)h->rows, (int)h->row_begin, dbv, dbi, st);
-    if (rc) return rc;
+    if (parts) {
+        argmax_combine_kernel<<<1, 256, 0, st>>>(h->pv, h->pi, parts, (int)h->row_begin, dbv, dbi);
+        FOCR_CUDA_TRY(cudaGetLastError());
+    } else {
+        rc = launch_argmax_rows(dlog, (int)m, (int)h->rows, (int)h->row_begin, dbv, dbi, st);
+        if (rc) return rc;
+    }
     if (mem == FOCR_MEM_HOST) {
         FOCR_CUDA_TRY(cudaMemcpyAsync(best_val, h->bv, m * 4, cudaMemcpyDeviceToHost, st));
         FOCR_CUDA_TRY(cudaMemcpyAsync(best_idx, h->bi, m * 4, cudaMemcpyDeviceToHost, st));
@@ -215,6 +205,8 @@ int focr_lmhead_create_s4(const uint8_t *packed, const float *scales, size_t gro
     A(h->logits, max_tokens * rows * 4);
     A(h->bv, max_tokens * 4);
     A(h->bi, max_tokens * 4);
+    A(h->pv, LMHEAD_MAX_PARTS * 4);
+    A(h->pi, LMHEAD_MAX_PARTS * 4);
 #undef A
     if (e == cudaSuccess) e = cudaMemcpy(h->wp, packed, rows * hidden / 2, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemcpy(h->scales, scales, ns * 4, cudaMemcpyHostToDevice);

@@ -26,15 +26,15 @@ def test_config4_int4_moe_layer(cuda, oracle, m):
     L.close()
 
 
-@pytest.mark.parametrize("m", [1, 256])
-def test_config4_int4_lmhead_shard(cuda, oracle, m):
+@pytest.mark.parametrize("m,g,rows", [(1, 32, 16160), (256, 32, 16160), (1, 16, 4099)])
+def test_config4_int4_lmhead_shard(cuda, oracle, m, g, rows):
     import torch
 
     from franken_ocr_b200.lmhead import LmHeadShard
     from franken_ocr_b200.quant import pack_int4_f32
     from franken_ocr_b200 import synth
 
-    rows, H, g = 16160, 1280, 32
+    H = 1280
     wf = synth.normal(4402, "lm_head", 3, (rows, H), 0.02)
     packed, sc = pack_int4_f32(wf, g)
     x = synth.hidden_states(4403, m)
