@@ -105,6 +105,12 @@ __device__ __forceinline__ void atomic_max_nonneg(float *addr, float v) {
 }
 
 __device__ __forceinline__ int dp4a_ss(int a, int b, int c) { return __dp4a(a, b, c); }
+// signed bytes of a times unsigned bytes of b
+__device__ __forceinline__ int dp4a_su(int a, int b, int c) {
+    int d;
+    asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
 __device__ __forceinline__ int dp4a_us(int a, int b, int c) {
     int d;
     asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));

@@ -310,6 +310,10 @@ gemv_s4_q1_kernel(const float *__restrict__ x, int K, int te, const uint8_t *__r
                   U = S4Q1_U;
     constexpr int SPC = 32 / GROUP;   // groups per 16-byte chunk (1 or 2)
     __shared__ int4 sA[GEMV_S4Q1_MAX_K / 16];
+    // Q(x) regrouped for nibble-parallel dots: per 8 values k0..k7, the word
+    // (k0,k2,k4,k6) in sE and (k1,k3,k5,k7) in sO (int4 c = chunk c)
+    __shared__ int4 sE[GEMV_S4Q1_MAX_K / 32], sO[GEMV_S4Q1_MAX_K / 32];
+    __shared__ int gsum[GEMV_S4Q1_MAX_K / 16];   // sum of Q(x) over each 16 values
     __shared__ __align__(16) float tw[WARPS][R][GMAX];
     __shared__ float red[WARPS];
     __shared__ float s_sc, s_inv;
@@ -366,6 +370,17 @@ gemv_s4_q1_kernel(const float *__restrict__ x, int K, int te, const uint8_t *__r
         sq[4 * i + 3] = (int8_t)quant_i8(v.w, inv, te != 0);
     }
     __syncthreads();
+    for (int i = threadIdx.x; i < K / 8; i += blockDim.x) {
+        const int2 a = reinterpret_cast<const int2 *>(sA)[i];   // k = 8i .. 8i + 7
+        reinterpret_cast<int *>(sE)[i] = (int)__byte_perm(a.x, a.y, 0x6420);
+        reinterpret_cast<int *>(sO)[i] = (int)__byte_perm(a.x, a.y, 0x7531);
+    }
+    for (int i = threadIdx.x; i < K / 16; i += blockDim.x) {
+        const int4 a = sA[i];
+        gsum[i] = dp4a_ss(a.x, 0x01010101, dp4a_ss(a.y, 0x01010101,
+                          dp4a_ss(a.z, 0x01010101, dp4a_ss(a.w, 0x01010101, 0))));
+    }
+    __syncthreads();
     int bi = -1;   // this thread's first-maximum candidate
     float bv = 0.0f;
     for (; n0 < N; n0 += nwarps * R) {
@@ -374,16 +389,17 @@ gemv_s4_q1_kernel(const float *__restrict__ x, int K, int te, const uint8_t *__r
             const int i = lane + 32 * u;
             if (i < R * C) {
                 const int r = i / C, c = i - r * C;
-                const int4 a0 = sA[2 * c], a1 = sA[2 * c + 1];   // k = 32c .. 32c + 31
-                const uint32_t ww[4] = {(uint32_t)wv[u].x, (uint32_t)wv[u].y, (uint32_t)wv[u].z,
-                                        (uint32_t)wv[u].w};
-                const int aa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-                int d[2] = {0, 0};   // k 0..15 / 16..31 of the chunk
+                // signed nibble s = (n ^ 8) - 8: dot(a, s) = dot(a, n ^ 8) - 8 * sum(a),
+                // with n ^ 8 in [0, 15] taken as unsigned bytes
+                const int4 ae = sE[c], ao = sO[c];   // k = 32c .. 32c + 31
+                const uint32_t ww[4] = {(uint32_t)wv[u].x ^ 0x88888888u, (uint32_t)wv[u].y ^ 0x88888888u,
+                                        (uint32_t)wv[u].z ^ 0x88888888u, (uint32_t)wv[u].w ^ 0x88888888u};
+                const int ea[4] = {ae.x, ae.y, ae.z, ae.w}, oa[4] = {ao.x, ao.y, ao.z, ao.w};
+                int d[2] = {-8 * gsum[2 * c], -8 * gsum[2 * c + 1]};   // k 0..15 / 16..31
 #pragma unroll
                 for (int q = 0; q < 4; q++) {
-                    int lo, hi;
-                    unpack8_s4(ww[q], lo, hi);
-                    d[q >> 1] = dp4a_ss(aa[2 * q + 1], hi, dp4a_ss(aa[2 * q], lo, d[q >> 1]));
+                    const int lo = (int)(ww[q] & 0x0F0F0F0Fu), hi = (int)((ww[q] >> 4) & 0x0F0F0F0Fu);
+                    d[q >> 1] = dp4a_su(ea[q], lo, dp4a_su(oa[q], hi, d[q >> 1]));
                 }
                 if (SPC == 1) {
                     tw[wib][r][c] = __fmul_rn(sv[u][0], (float)(d[0] + d[1]));
