@@ -204,8 +204,9 @@ __global__ void __launch_bounds__(128) attention_scores_kernel(
 //      which skips NaN as the reference's `score > run_max` does);
 //   2. per key, in parallel, the fold's two exponentials: the correction
 //      c_r = exp(m_{r-1} - s_r) (0 while m_{r-1} is -inf; exactly 1 when the
-//      max did not move, and then the multiply is skipped -- x * 1 == x, so
-//      that is the reference's untaken branch) and the weight
+//      max did not move -- multiplying by it is then the identity, so the
+//      rescale can always run and still equal the reference's untaken
+//      branch) and the weight
 //      w_r = exp(s_r - m_r);
 //   3. the serial recurrence den = den * c_r + w_r, acc[d] = acc[d] * c_r +
 //      w_r * v_r[d] in key order, one lane per dimension, fed from a ring of
@@ -293,17 +294,31 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_fold_kernel(
         if (warp == 0) {
             const float *buf = sv + (c % ATT_STAGES) * ATT_CH * ATT_DG + lane;
             const int r0 = c * ATT_CH, r1 = min(r0 + ATT_CH, total);
-#pragma unroll 8
-            for (int r = r0; r < r1; r++) {
+            // Branch-free: when the max did not move c_r is exactly 1 and
+            // acc * 1 == acc bit for bit (signed zeros, infinities and NaN
+            // included), which is the reference's untaken rescale.  The
+            // operands of 8 keys are loaded before their 8 chain steps.
+            int r = r0;
+            for (; r + 8 <= r1; r += 8) {
+                float cr[8], w[8], vv[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    cr[j] = sc[r + j];
+                    w[j] = sw[r + j];
+                    vv[j] = buf[(r + j - r0) * ATT_DG];
+                }
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const float wv = __fmul_rn(w[j], vv[j]);
+                    acc = __fadd_rn(__fmul_rn(acc, cr[j]), wv);
+                    den = __fadd_rn(__fmul_rn(den, cr[j]), w[j]);
+                }
+            }
+            for (; r < r1; r++) {
                 const float cr = sc[r], w = sw[r];
                 const float wv = __fmul_rn(w, buf[(r - r0) * ATT_DG]);
-                if (cr == 1.0f) {
-                    acc = __fadd_rn(acc, wv);
-                    den = __fadd_rn(den, w);
-                } else {
-                    acc = __fadd_rn(__fmul_rn(acc, cr), wv);
-                    den = __fadd_rn(__fmul_rn(den, cr), w);
-                }
+                acc = __fadd_rn(__fmul_rn(acc, cr), wv);
+                den = __fadd_rn(__fmul_rn(den, cr), w);
             }
         }
         __syncthreads();
