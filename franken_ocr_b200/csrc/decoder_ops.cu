@@ -139,7 +139,7 @@ __global__ void rope_kernel(float *__restrict__ x, int seq, int cols, int head_d
 constexpr int ATT_THREADS = 256;
 constexpr int ATT_MAX_KEYS = 16384;
 constexpr int ATT_DG = 32;      // dimensions per CTA (one fold warp, a lane per dimension)
-constexpr int ATT_CH = 64;      // keys per staged V chunk
+constexpr int ATT_CH = 128;     // keys per staged V chunk
 constexpr int ATT_STAGES = 4;   // V chunks in flight
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
