@@ -166,6 +166,7 @@ __global__ void __launch_bounds__(128) attention_scores_kernel(
     float *__restrict__ scores, int score_stride, const int *__restrict__ ring_len_dev) {
     extern __shared__ __align__(16) float sc_sm[];
     const int h = blockIdx.x, r0 = blockIdx.y * ATT_SB, tid = threadIdx.x;
+    pdl_trigger();   // the fold kernel may start staging V meanwhile
     if (ring_len_dev) ring_len = *ring_len_dev;
     const int total = prefill_len + ring_len;
     if (r0 >= total) return;
@@ -241,6 +242,10 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_fold_kernel(
         if (c < nch) stage(c);
         cp_async_commit();
     }
+    // launched as the programmatic dependent of the scores kernel: V, the
+    // ring length and everything before the scores kernel are complete;
+    // the scores are visible after this wait
+    pdl_wait();
     const float *hs = scores + (size_t)h * score_stride;
     for (int r = tid; r < total; r += ATT_THREADS) sw[r] = hs[r];
     __syncthreads();
@@ -357,11 +362,11 @@ static int launch_attention(const float *q, const float *ref_k, const float *ref
                                               ring_stride, head_dim, (float *)scr.p, keys_cap,
                                               ring_len_dev);
     FOCR_CUDA_TRY(cudaGetLastError());
-    attention_fold_kernel<<<dim3((unsigned)heads, (unsigned)(head_dim / ATT_DG)), ATT_THREADS,
-                            att_smem(keys_cap), st>>>(
-        (const float *)scr.p, keys_cap, ref_v, prefill_len, ref_stride, ring_v, ring_len,
-        ring_stride, head_dim, out, ring_len_dev);
-    FOCR_CUDA_TRY(cudaGetLastError());
+    FOCR_CUDA_TRY(launch_pdl(attention_fold_kernel,
+                             dim3((unsigned)heads, (unsigned)(head_dim / ATT_DG)), dim3(ATT_THREADS),
+                             att_smem(keys_cap), st, (const float *)scr.p, keys_cap, ref_v,
+                             prefill_len, ref_stride, ring_v, ring_len, ring_stride, head_dim, out,
+                             ring_len_dev));
     return FOCR_OK;
 }
 
