@@ -131,6 +131,8 @@ __global__ void decode_prologue_kernel(int *__restrict__ st, const int *__restri
                                        int ring_window, int *__restrict__ tokens_out,
                                        int max_tokens, float *__restrict__ x) {
     __shared__ int tok;
+    pdl_wait();
+    pdl_trigger();
     if (threadIdx.x == 0) {
         int t = *token;
         if (t < 0 || t >= vocab) {
@@ -164,6 +166,8 @@ __global__ void ring_write_kernel(const float *__restrict__ k, const float *__re
                                   int heads, int head_dim, float *__restrict__ ring_k,
                                   float *__restrict__ ring_v, int ring_stride,
                                   const int *__restrict__ st) {
+    pdl_wait();
+    pdl_trigger();
     const int slot = st[FOCR_STATE_SLOT];
     const int n = heads * head_dim;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
@@ -381,10 +385,9 @@ int focr_decode_prologue(int32_t *state, const int32_t *token, const float *embe
     if (!state || !token || !embed || !x) return fail(FOCR_E_ARG, "decode_prologue: null pointer");
     if (ring_window == 0 || vocab > (size_t)INT32_MAX || hidden > (size_t)INT32_MAX)
         return fail(FOCR_E_SHAPE, "decode_prologue: bad sizes");
-    decode_prologue_kernel<<<1, 256, 0, (cudaStream_t)stream>>>(
-        state, token, embed, (int)vocab, (int)hidden, (int)ring_window, tokens_out,
-        (int)max_tokens, x);
-    FOCR_CUDA_TRY(cudaGetLastError());
+    FOCR_CUDA_TRY(launch_pdl(decode_prologue_kernel, dim3(1), dim3(256), 0, (cudaStream_t)stream,
+                             state, token, embed, (int)vocab, (int)hidden, (int)ring_window,
+                             tokens_out, (int)max_tokens, x));
     return FOCR_OK;
 }
 
@@ -393,9 +396,9 @@ int focr_ring_write(const float *k, const float *v, size_t heads, size_t head_di
     if (!k || !v || !ring_k || !ring_v || !state) return fail(FOCR_E_ARG, "ring_write: null pointer");
     const long n = (long)(heads * head_dim);
     if (n == 0) return FOCR_OK;
-    ring_write_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
-        k, v, (int)heads, (int)head_dim, ring_k, ring_v, (int)ring_stride, state);
-    FOCR_CUDA_TRY(cudaGetLastError());
+    FOCR_CUDA_TRY(launch_pdl(ring_write_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0,
+                             (cudaStream_t)stream, k, v, (int)heads, (int)head_dim, ring_k, ring_v,
+                             (int)ring_stride, state));
     return FOCR_OK;
 }
 

@@ -39,6 +39,8 @@ __global__ void rms_norm_kernel(const float *__restrict__ x, int rows, int cols,
                                 const float *__restrict__ w, float eps, float *__restrict__ y,
                                 const float *__restrict__ add = nullptr,
                                 float *__restrict__ h = nullptr) {
+    pdl_wait();   // launched as a programmatic dependent (launch_pdl)
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= rows) return;
@@ -118,6 +120,8 @@ __global__ void rms_norm_kernel(const float *__restrict__ x, int rows, int cols,
 __global__ void rope_kernel(float *__restrict__ x, int seq, int cols, int head_dim,
                             const float *__restrict__ cos_t, const float *__restrict__ sin_t,
                             const int *__restrict__ pos_dev = nullptr) {
+    pdl_wait();
+    pdl_trigger();
     const int half = head_dim / 2, heads = cols / head_dim;
     if (pos_dev) {
         cos_t += (size_t)(*pos_dev) * head_dim;
@@ -166,6 +170,7 @@ __global__ void __launch_bounds__(128) attention_scores_kernel(
     float *__restrict__ scores, int score_stride, const int *__restrict__ ring_len_dev) {
     extern __shared__ __align__(16) float sc_sm[];
     const int h = blockIdx.x, r0 = blockIdx.y * ATT_SB, tid = threadIdx.x;
+    pdl_wait();
     pdl_trigger();   // the fold kernel may start staging V meanwhile
     if (ring_len_dev) ring_len = *ring_len_dev;
     const int total = prefill_len + ring_len;
@@ -357,11 +362,10 @@ static int launch_attention(const float *q, const float *ref_k, const float *ref
     DevBuf scr;
     FOCR_CUDA_TRY(scr.alloc((size_t)heads * keys_cap * sizeof(float), st));
     const size_t ssm = ((size_t)head_dim + (size_t)ATT_SB * (head_dim + 1)) * sizeof(float);
-    attention_scores_kernel<<<dim3((unsigned)heads, (unsigned)((keys_cap + ATT_SB - 1) / ATT_SB)),
-                              128, ssm, st>>>(q, ref_k, prefill_len, ref_stride, ring_k, ring_len,
-                                              ring_stride, head_dim, (float *)scr.p, keys_cap,
-                                              ring_len_dev);
-    FOCR_CUDA_TRY(cudaGetLastError());
+    FOCR_CUDA_TRY(launch_pdl(attention_scores_kernel,
+                             dim3((unsigned)heads, (unsigned)((keys_cap + ATT_SB - 1) / ATT_SB)),
+                             dim3(128), ssm, st, q, ref_k, prefill_len, ref_stride, ring_k, ring_len,
+                             ring_stride, head_dim, (float *)scr.p, keys_cap, ring_len_dev));
     FOCR_CUDA_TRY(launch_pdl(attention_fold_kernel,
                              dim3((unsigned)heads, (unsigned)(head_dim / ATT_DG)), dim3(ATT_THREADS),
                              att_smem(keys_cap), st, (const float *)scr.p, keys_cap, ref_v,
@@ -406,9 +410,13 @@ int focr_rms_norm(const float *x, size_t rows, size_t cols, const float *weight,
     const int blocks = (int)((rows + 7) / 8);
     if (mem == FOCR_MEM_DEVICE) {
         if (rms_vec_ok(x, y, weight, nullptr, nullptr, cols))
-            rms_norm_kernel<true><<<blocks, 256, 0, st>>>(x, (int)rows, (int)cols, weight, eps, y);
+            FOCR_CUDA_TRY(launch_pdl(rms_norm_kernel<true>, dim3(blocks), dim3(256), 0, st, x,
+                                     (int)rows, (int)cols, weight, eps, y, (const float *)nullptr,
+                                     (float *)nullptr));
         else
-            rms_norm_kernel<false><<<blocks, 256, 0, st>>>(x, (int)rows, (int)cols, weight, eps, y);
+            FOCR_CUDA_TRY(launch_pdl(rms_norm_kernel<false>, dim3(blocks), dim3(256), 0, st, x,
+                                     (int)rows, (int)cols, weight, eps, y, (const float *)nullptr,
+                                     (float *)nullptr));
         FOCR_CUDA_TRY(cudaGetLastError());
         return FOCR_OK;
     }
@@ -439,7 +447,8 @@ int focr_rope_apply(float *x, size_t seq, size_t cols, size_t head_dim, const fl
     const long n = (long)seq * (cols / 2);
     const int blocks = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
     if (mem == FOCR_MEM_DEVICE) {
-        rope_kernel<<<blocks, 256, 0, st>>>(x, (int)seq, (int)cols, (int)head_dim, cos_t, sin_t);
+        FOCR_CUDA_TRY(launch_pdl(rope_kernel, dim3(blocks), dim3(256), 0, st, x, (int)seq, (int)cols,
+                                 (int)head_dim, cos_t, sin_t, (const int *)nullptr));
         FOCR_CUDA_TRY(cudaGetLastError());
         return FOCR_OK;
     }
@@ -516,9 +525,9 @@ int focr_rope_apply_at(float *x, size_t cols, size_t head_dim, const float *cos_
     if (head_dim == 0 || head_dim % 2 || cols % head_dim || cols > (size_t)INT32_MAX)
         return fail(FOCR_E_SHAPE, "rope_apply_at: cols not a multiple of head_dim");
     const long n = (long)(cols / 2);
-    rope_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
-        x, 1, (int)cols, (int)head_dim, cos_table, sin_table, state + FOCR_STATE_POS);
-    FOCR_CUDA_TRY(cudaGetLastError());
+    FOCR_CUDA_TRY(launch_pdl(rope_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0,
+                             (cudaStream_t)stream, x, 1, (int)cols, (int)head_dim, cos_table,
+                             sin_table, (const int *)(state + FOCR_STATE_POS)));
     return FOCR_OK;
 }
 
@@ -547,12 +556,11 @@ int focr_add_rms_norm(const float *a, const float *b, size_t rows, size_t cols,
         return fail(FOCR_E_UNSUPPORTED, "add_rms_norm: dimension exceeds int32 range");
     const unsigned blocks = (unsigned)((rows + 7) / 8);
     if (rms_vec_ok(a, y, weight, b, h, cols))
-        rms_norm_kernel<true><<<blocks, 256, 0, (cudaStream_t)stream>>>(a, (int)rows, (int)cols,
-                                                                        weight, eps, y, b, h);
+        FOCR_CUDA_TRY(launch_pdl(rms_norm_kernel<true>, dim3(blocks), dim3(256), 0,
+                                 (cudaStream_t)stream, a, (int)rows, (int)cols, weight, eps, y, b, h));
     else
-        rms_norm_kernel<false><<<blocks, 256, 0, (cudaStream_t)stream>>>(a, (int)rows, (int)cols,
-                                                                         weight, eps, y, b, h);
-    FOCR_CUDA_TRY(cudaGetLastError());
+        FOCR_CUDA_TRY(launch_pdl(rms_norm_kernel<false>, dim3(blocks), dim3(256), 0,
+                                 (cudaStream_t)stream, a, (int)rows, (int)cols, weight, eps, y, b, h));
     return FOCR_OK;
 }
 

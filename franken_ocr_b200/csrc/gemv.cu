@@ -104,6 +104,20 @@ gemv_q1_kernel(const float *__restrict__ x, int K, int te, const int8_t *__restr
     __shared__ float red[GEMV_THREADS / 32];
     __shared__ float s_sc, s_inv;
     const int lane = threadIdx.x & 31;
+    // Launched as a programmatic dependent: the weights do not depend on
+    // the preceding kernel, so this warp's first two rows are requested
+    // into L2 before the dependency wait (x is read after it).
+    pdl_trigger();
+    {
+        const int w0 = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+        const int lines = (K + 127) >> 7;
+        for (int l = lane; l < 2 * lines; l += 32) {
+            const int n = w0 * 2 + l / lines;
+            if (n < N)
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(B + (size_t)n * K + (size_t)(l % lines) * 128));
+        }
+    }
+    pdl_wait();
     const float4 *x4 = reinterpret_cast<const float4 *>(x);
     float m = 0.0f;
     for (int i = threadIdx.x; i < K / 4; i += blockDim.x) {
@@ -279,9 +293,8 @@ int launch_gemv_q1(const float *x, size_t K, bool te, const int8_t *B, const flo
     if (K == 0 || K % 16 || K > (size_t)GEMV_Q1_MAX_K || ((uintptr_t)x % 16) ||
         ((uintptr_t)B % 16) || N > (size_t)INT32_MAX)
         return FOCR_E_UNSUPPORTED;
-    gemv_q1_kernel<<<gemv_grid(N, (GEMV_THREADS / 32) * 2), GEMV_THREADS, 0, st>>>(
-        x, (int)K, te ? 1 : 0, B, w_scale, (int)N, y);
-    FOCR_CUDA_TRY(cudaGetLastError());
+    FOCR_CUDA_TRY(launch_pdl(gemv_q1_kernel, dim3(gemv_grid(N, (GEMV_THREADS / 32) * 2)),
+                             dim3(GEMV_THREADS), 0, st, x, (int)K, te ? 1 : 0, B, w_scale, (int)N, y));
     return FOCR_OK;
 }
 

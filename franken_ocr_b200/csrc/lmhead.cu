@@ -29,6 +29,8 @@ namespace focr {
 
 __global__ void argmax_part_kernel(const float *__restrict__ logits, int n, int span,
                                    float *__restrict__ part_v, int *__restrict__ part_i) {
+    pdl_wait();
+    pdl_trigger();
     const float *row = logits + (size_t)blockIdx.y * n;
     const int c0 = blockIdx.x * span, c1 = min(c0 + span, n);
     int bi = -1;
@@ -50,6 +52,8 @@ __global__ void argmax_part_kernel(const float *__restrict__ logits, int n, int 
 __global__ void argmax_combine_kernel(const float *__restrict__ part_v,
                                       const int *__restrict__ part_i, int parts, int offset,
                                       float *__restrict__ best_v, int32_t *__restrict__ best_i) {
+    pdl_wait();
+    pdl_trigger();
     int bi = -1;
     float bv = 0.0f;
     for (int p = threadIdx.x; p < parts; p += blockDim.x)
@@ -68,12 +72,10 @@ static int launch_argmax_rows(const float *logits, int m, int n, int offset, flo
     DevBuf pv, pi;
     FOCR_CUDA_TRY(pv.alloc((size_t)m * parts * 4, st));
     FOCR_CUDA_TRY(pi.alloc((size_t)m * parts * 4, st));
-    argmax_part_kernel<<<dim3((unsigned)parts, (unsigned)m), 256, 0, st>>>(
-        logits, n, span, (float *)pv.p, (int *)pi.p);
-    FOCR_CUDA_TRY(cudaGetLastError());
-    argmax_combine_kernel<<<(unsigned)m, 256, 0, st>>>((const float *)pv.p, (const int *)pi.p, parts,
-                                                     offset, best_v, best_i);
-    FOCR_CUDA_TRY(cudaGetLastError());
+    FOCR_CUDA_TRY(launch_pdl(argmax_part_kernel, dim3((unsigned)parts, (unsigned)m), dim3(256), 0,
+                             st, logits, n, span, (float *)pv.p, (int *)pi.p));
+    FOCR_CUDA_TRY(launch_pdl(argmax_combine_kernel, dim3((unsigned)m), dim3(256), 0, st,
+                             (const float *)pv.p, (const int *)pi.p, parts, offset, best_v, best_i));
     return FOCR_OK;
 }
 
