@@ -38,6 +38,7 @@ EXPORTS = [
     "focr_ep_create", "focr_ep_destroy", "focr_ep_ipc_handle", "focr_ep_connect",
     "focr_ep_connect_comm", "focr_ep_connect_local", "focr_ep_forward", "focr_ep_dispatch",
     "focr_ep_experts", "focr_ep_combine", "focr_ep_decode", "focr_ep_status",
+    "focr_decoder_create", "focr_decoder_destroy", "focr_decoder_prefill", "focr_decoder_generate",
 ]
 
 
@@ -76,6 +77,27 @@ class MoeWeights(C.Structure):
         "router", "gate_w", "gate_s", "up_w", "up_s", "down_w", "down_s",
         "gate_p", "gate_gs", "up_p", "up_gs", "down_p", "down_gs",
         "sh_gate_w", "sh_gate_s", "sh_up_w", "sh_up_s", "sh_down_w", "sh_down_s")]
+
+
+class DecoderConfig(C.Structure):
+    _fields_ = [
+        ("hidden", C.c_uint32), ("heads", C.c_uint32), ("head_dim", C.c_uint32),
+        ("n_layers", C.c_uint32), ("vocab", C.c_uint32), ("max_prefill", C.c_uint32),
+        ("ring_window", C.c_uint32), ("rope_theta", C.c_float), ("rms_eps", C.c_float),
+        ("moe", MoeConfig),
+    ]
+
+
+class DecoderLayerWeights(C.Structure):
+    _fields_ = [(n, vp) for n in (
+        "input_ln", "post_ln", "q_w", "k_w", "v_w", "o_w", "q_s", "k_s", "v_s", "o_s", "moe")] + [
+        ("dense_inter", C.c_uint32)] + [(n, vp) for n in (
+            "gate_w", "up_w", "down_w", "gate_s", "up_s", "down_s")]
+
+
+class DecoderWeights(C.Structure):
+    _fields_ = [("layers", C.POINTER(DecoderLayerWeights))] + [
+        (n, vp) for n in ("final_norm", "lm_w", "lm_s", "embed")]
 
 
 lib.focr_last_error.restype = C.c_char_p
@@ -129,6 +151,11 @@ lib.focr_add.argtypes = [vp, vp, sz, vp, i32, vp]
 lib.focr_attention_prefill.argtypes = [vp, vp, vp, sz, sz, sz, vp, i32, vp]
 lib.focr_rope_table.argtypes = [vp, sz, sz, C.c_float, vp, vp]
 lib.focr_decode_prologue.argtypes = [vp, vp, vp, sz, sz, sz, vp, sz, vp, vp]
+lib.focr_decoder_create.argtypes = [C.POINTER(DecoderConfig), C.POINTER(DecoderWeights),
+                                    C.POINTER(vp)]
+lib.focr_decoder_destroy.argtypes = [vp]
+lib.focr_decoder_prefill.argtypes = [vp, vp, sz, vp, i32, vp]
+lib.focr_decoder_generate.argtypes = [vp, vp, sz, sz, vp, i32, vp]
 lib.focr_rope_apply_at.argtypes = [vp, sz, sz, vp, vp, vp, vp]
 lib.focr_ring_write.argtypes = [vp, vp, sz, sz, vp, vp, sz, vp, vp]
 lib.focr_add_rms_norm.argtypes = [vp, vp, sz, sz, vp, C.c_float, vp, vp, vp]

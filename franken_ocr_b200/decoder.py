@@ -33,7 +33,10 @@ from dataclasses import dataclass, field
 
 import numpy as np
 
-from ._lib import MEM_DEVICE, check, lib
+import ctypes as C
+
+from ._lib import (MEM_DEVICE, MEM_HOST, DecoderConfig, DecoderLayerWeights, DecoderWeights,
+                   MoeConfig, MoeWeights, check, lib)
 from .synth import MoeWeightsHost
 
 HEAD_DIM = 128
@@ -383,3 +386,84 @@ class DecoderI8:
             raise RuntimeError("decode: token id outside the embedding table")
         self.ring_len, self.ring_pos = int(st[1]), int(st[2])
         return out
+
+
+def _np_ptr(a):
+    return None if a is None else a.ctypes.data
+
+
+class DecoderLib:
+    """The whole decoder as one library object (``focr_decoder_*``): weights
+    uploaded, caches and activations allocated and the decode step captured
+    in a CUDA graph by ``libfocr_cuda.so`` itself -- the path a host without
+    PyTorch (the reference's Rust engine over its FFI crate) drives.  Host
+    numpy inputs and outputs."""
+
+    def __init__(self, W: DecoderWeightsHost, max_prefill: int):
+        self.W = W
+        self.hidden, self.vocab = W.hidden, W.vocab
+        keep = []
+
+        def arr(a, dt):
+            a = np.ascontiguousarray(a, dtype=dt)
+            keep.append(a)
+            return a.ctypes.data
+
+        moe_shape = next((L.moe for L in W.layers if L.moe is not None), None)
+        mc = MoeConfig()
+        if moe_shape is not None:
+            mc = MoeConfig(moe_shape.hidden, moe_shape.inter, moe_shape.n_experts, moe_shape.topk,
+                           moe_shape.shared_inter, int(W.norm_topk_prob),
+                           float(W.routed_scaling_factor), moe_shape.group,
+                           moe_shape.expert_begin, moe_shape.expert_count, max_prefill)
+        cfg = DecoderConfig(W.hidden, W.heads, HEAD_DIM, len(W.layers), W.vocab, max_prefill,
+                            RING_WINDOW, ROPE_THETA, RMS_NORM_EPS, mc)
+        layers = (DecoderLayerWeights * len(W.layers))()
+        moe_w = []
+        for i, L in enumerate(W.layers):
+            lw = layers[i]
+            lw.input_ln, lw.post_ln = arr(L.input_ln, np.float32), arr(L.post_ln, np.float32)
+            for r in ("q", "k", "v", "o"):
+                setattr(lw, r + "_w", arr(L.proj[r + "_w"], np.int8))
+                setattr(lw, r + "_s", arr(L.proj[r + "_s"], np.float32))
+            if L.moe is not None:
+                mw = MoeWeights()
+                mw.router = arr(L.moe.router, np.float32)
+                for name, a in L.moe.arrays.items():
+                    setattr(mw, name, _np_ptr(a))
+                    keep.append(a)
+                moe_w.append(mw)
+                lw.moe = C.cast(C.pointer(mw), C.c_void_p)
+            else:
+                lw.dense_inter = L.dense["gate_w"].shape[0]
+                for n in ("gate", "up", "down"):
+                    setattr(lw, n + "_w", arr(L.dense[n + "_w"], np.int8))
+                    setattr(lw, n + "_s", arr(L.dense[n + "_s"], np.float32))
+        wt = DecoderWeights(layers, arr(W.final_norm, np.float32), arr(W.lm_w, np.int8),
+                            arr(W.lm_s, np.float32), arr(W.embed, np.float32))
+        h = C.c_void_p()
+        check(lib.focr_decoder_create(C.byref(cfg), C.byref(wt), C.byref(h)))
+        self._h = h
+        del keep, moe_w
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib.focr_decoder_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def prefill(self, embeds: np.ndarray) -> np.ndarray:
+        e = np.ascontiguousarray(embeds, dtype=np.float32)
+        out = np.empty_like(e)
+        check(lib.focr_decoder_prefill(self._h, e.ctypes.data, e.shape[0], out.ctypes.data,
+                                       MEM_HOST, None))
+        return out
+
+    def generate(self, embeds: np.ndarray, n_tokens: int) -> np.ndarray:
+        e = np.ascontiguousarray(embeds, dtype=np.float32)
+        toks = np.empty(n_tokens, np.int32)
+        check(lib.focr_decoder_generate(self._h, e.ctypes.data, e.shape[0], n_tokens,
+                                        toks.ctypes.data, MEM_HOST, None))
+        return toks.astype(np.int64)

@@ -408,6 +408,73 @@ int focr_attention_decode_at(const float *q, const float *ref_k, const float *re
                              const float *ring_v, size_t ring_stride, size_t heads,
                              size_t head_dim, const int32_t *state, float *out, void *stream);
 
+/* ---- the whole int8 decoder as one object (config-3 decoder) ----------
+ * Replaces the reference engine's int8 decode path end to end:
+ * DecoderWeightCacheI8::build (native_engine/decoder.rs:2001-2117) at create,
+ * prefill_with_cache_i8 (decoder.rs:2412-2540), decode_step_with_cache_i8
+ * (decoder.rs:2542-2640) and the greedy loop of generate_cached_i8
+ * (native_engine/mod.rs:1860-1898; no EOS stop, a fixed token count).  The
+ * library allocates and zero-fills the R-SWA caches and every activation
+ * buffer and captures the decode step in its own CUDA graph, so a host with
+ * no GPU framework drives the decoder through these calls alone. */
+typedef struct focr_decoder_config {
+    uint32_t hidden;       /* 1280 */
+    uint32_t heads;        /* 10 */
+    uint32_t head_dim;     /* 128 (the only value supported) */
+    uint32_t n_layers;     /* 12 */
+    uint32_t vocab;        /* 129280 */
+    uint32_t max_prefill;  /* longest prefill (reference block rows per layer) */
+    uint32_t ring_window;  /* R-SWA ring rows (128, rswa.rs) */
+    float rope_theta;      /* 10000 */
+    float rms_eps;         /* 1e-6 */
+    focr_moe_config moe;   /* shape of every MoE layer; max_tokens is set to max_prefill */
+} focr_decoder_config;
+
+/* One layer, host memory: norms [hidden]; q/k/v [heads*head_dim][hidden] and
+ * o [hidden][heads*head_dim] int8 with per-row f32 scales; either a MoE layer
+ * (moe != NULL) or the dense SwiGLU MLP: gate/up [dense_inter][hidden],
+ * down [hidden][dense_inter] int8 + per-row scales. */
+typedef struct focr_decoder_layer_weights {
+    const float *input_ln, *post_ln;
+    const int8_t *q_w, *k_w, *v_w, *o_w;
+    const float *q_s, *k_s, *v_s, *o_s;
+    const focr_moe_weights *moe;
+    uint32_t dense_inter;
+    const int8_t *gate_w, *up_w, *down_w;
+    const float *gate_s, *up_s, *down_s;
+} focr_decoder_layer_weights;
+
+/* layers[n_layers]; final_norm [hidden]; lm_w [vocab][hidden] int8 + lm_s
+ * [vocab]; embed [vocab][hidden] f32.  Host memory. */
+typedef struct focr_decoder_weights {
+    const focr_decoder_layer_weights *layers;
+    const float *final_norm;
+    const int8_t *lm_w;
+    const float *lm_s;
+    const float *embed;
+} focr_decoder_weights;
+
+typedef struct focr_decoder focr_decoder;
+
+int focr_decoder_create(const focr_decoder_config *cfg, const focr_decoder_weights *w,
+                        focr_decoder **out);
+int focr_decoder_destroy(focr_decoder *d);
+
+/* prefill_with_cache_i8: embeds [seq][hidden] (host or device per mem) ->
+ * final hidden states [seq][hidden] into `hidden` (may be NULL); records
+ * every layer's prefill K/V as its reference block and empties the rings. */
+int focr_decoder_prefill(focr_decoder *d, const float *embeds, size_t seq, float *hidden,
+                         int mem, void *stream);
+
+/* Greedy decode of n_tokens after prefilling `embeds` (host or device per
+ * mem): token i is decoded at position seq + i - 1; tokens [n_tokens] int32
+ * is host memory, written when the call returns (it synchronises `stream`).
+ * The decode step is captured once per (seq, n_tokens) and replayed; a NULL
+ * stream runs the call on a stream the decoder owns (the legacy default
+ * stream cannot be captured). */
+int focr_decoder_generate(focr_decoder *d, const float *embeds, size_t seq, size_t n_tokens,
+                          int32_t *tokens, int mem, void *stream);
+
 /* ---- device event trace (GPU counterpart of FOCR_PROFILE_DECODE,
  * native_engine/decoder.rs:986-1024) ------------------------------------
  * Register a device buffer of `capacity` 16-byte events {u32 tag, u32 phase,
