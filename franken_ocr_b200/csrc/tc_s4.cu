@@ -317,23 +317,42 @@ __global__ void __launch_bounds__(S4_THREADS, 1)
 #pragma unroll
             for (int c = 0; c < HC; c++) acc[c] = 0.0f;
             bool ok = true;
+            // group scales two K blocks ahead of their use, so their load
+            // latency overlaps the tensor-memory folds of the blocks between
+            float scn[2][SLOTS];
+#pragma unroll
+            for (int a = 0; a < 2; a++)
+#pragma unroll
+                for (int g = 0; g < SLOTS; g++)
+                    scn[a][g] = a < kblocks ? __ldg(srow + a * SLOTS + g) : 0.0f;
             for (int kb = 0; kb < kblocks; kb++, kbi++) {
                 const uint32_t buf = kbi & 1;
                 float sc[SLOTS];
 #pragma unroll
-                for (int g = 0; g < SLOTS; g++) sc[g] = __ldg(srow + kb * SLOTS + g);
+                for (int g = 0; g < SLOTS; g++) {
+                    sc[g] = scn[0][g];
+                    scn[0][g] = scn[1][g];
+                    scn[1][g] = kb + 2 < kblocks ? __ldg(srow + (kb + 2) * SLOTS + g) : 0.0f;
+                }
                 if (!(ok = tc::mbar_wait(&tfull[buf], (kbi >> 1) & 1, err))) break;
                 tc::fence_after();
+                // four groups' 16 columns per tensor-memory round trip (one wait
+                // for four loads), folded in increasing group order per column
 #pragma unroll
-                for (int g = 0; g < SLOTS; g++) {
-                    int v[16];
+                for (int c0 = 0; c0 < HC; c0 += 16) {
 #pragma unroll
-                    for (int c0 = 0; c0 < HC; c0 += 16) {
-                        tc::tmem_ld16(lane_base + buf * 256 + g * NC + c0, v);
+                    for (int g0 = 0; g0 < SLOTS; g0 += 4) {
+                        int v[4][16];
+#pragma unroll
+                        for (int g = 0; g < 4; g++)
+                            tc::tmem_ld16(lane_base + buf * 256 + (g0 + g) * NC + c0, v[g]);
                         tc::tmem_ld_wait();
 #pragma unroll
-                        for (int c = 0; c < 16; c++)
-                            acc[c0 + c] = __fadd_rn(acc[c0 + c], __fmul_rn(sc[g], (float)v[c]));
+                        for (int g = 0; g < 4; g++)
+#pragma unroll
+                            for (int c = 0; c < 16; c++)
+                                acc[c0 + c] =
+                                    __fadd_rn(acc[c0 + c], __fmul_rn(sc[g0 + g], (float)v[g][c]));
                     }
                 }
                 tc::fence_before();
