@@ -337,9 +337,12 @@ __global__ void __launch_bounds__(S4_THREADS, 1)
                 if (!(ok = tc::mbar_wait(&tfull[buf], (kbi >> 1) & 1, err))) break;
                 tc::fence_after();
                 // four groups' 16 columns per tensor-memory round trip (one wait
-                // for four loads), folded in increasing group order per column
+                // for four loads), folded in increasing group order per column;
+                // 16-column blocks past the job's valid columns are skipped
+                // (warp-uniform: the loads are warp-collective)
 #pragma unroll
                 for (int c0 = 0; c0 < HC; c0 += 16) {
+                    if (half * HC + c0 >= jb.nv) break;
 #pragma unroll
                     for (int g0 = 0; g0 < SLOTS; g0 += 4) {
                         int v[4][16];
