@@ -391,6 +391,17 @@ int focr_decode_prologue(int32_t *state, const int32_t *token, const float *embe
     return FOCR_OK;
 }
 
+int focr_rms_norm_linear_i8(const float *a, const float *b, size_t k, const float *norm_w,
+                            float eps, float *h, const int8_t *w, const float *w_scale, size_t n,
+                            float *y, void *stream) {
+    if (!a || !norm_w || !w || !w_scale || !y)
+        return fail(FOCR_E_ARG, "rms_norm_linear_i8: null pointer");
+    int rc = launch_gemv_q1_norm(a, b, k, norm_w, eps, h, w, w_scale, n, y, (cudaStream_t)stream);
+    if (rc == FOCR_E_UNSUPPORTED)
+        return fail(rc, "rms_norm_linear_i8: k % 16 == 0, k <= 4096 and 16-byte aligned pointers required");
+    return rc;
+}
+
 int focr_ring_write(const float *k, const float *v, size_t heads, size_t head_dim, float *ring_k,
                     float *ring_v, size_t ring_stride, const int32_t *state, void *stream) {
     if (!k || !v || !ring_k || !ring_v || !state) return fail(FOCR_E_ARG, "ring_write: null pointer");

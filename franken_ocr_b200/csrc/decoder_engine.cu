@@ -179,11 +179,13 @@ static int decoder_step(focr_decoder *d, size_t n_tokens, cudaStream_t st) {
     for (size_t li = 0; li < d->layers.size(); li++) {
         const focr_decoder_layer_dev &L = d->layers[li];
         const float *xin = li == 0 ? d->e : d->x;
+        // residual add + input RMSNorm + q|k|v projection in one launch
         if (li == 0)
-            TRY(focr_rms_norm(d->e, 1, H, L.input_ln, eps, d->nrm, FOCR_MEM_DEVICE, st));
+            TRY(focr_rms_norm_linear_i8(d->e, nullptr, H, L.input_ln, eps, nullptr, L.qkv_w,
+                                        L.qkv_s, 3 * D, d->qkv, st));
         else
-            TRY(focr_add_rms_norm(d->hh, d->mlp, 1, H, L.input_ln, eps, d->x, d->nrm, st));
-        TRY(focr_linear_i8(d->nrm, 1, H, L.qkv_w, L.qkv_s, 3 * D, 0, d->qkv, FOCR_MEM_DEVICE, st));
+            TRY(focr_rms_norm_linear_i8(d->hh, d->mlp, H, L.input_ln, eps, d->x, L.qkv_w,
+                                        L.qkv_s, 3 * D, d->qkv, st));
         // q and k: one row of 2 * heads heads
         TRY(focr_rope_apply_at(d->qkv, 2 * D, hd, d->rope_cos, d->rope_sin, d->state, st));
         TRY(focr_ring_write(d->qkv + D, d->qkv + 2 * D, c.heads, hd, L.ring_k, L.ring_v,

@@ -97,12 +97,25 @@ constexpr int GEMV_Q1_MAX_K = 16384;
 // launch_gemv_q1: every block quantises the row itself (amax, scale and
 // rounding exactly as quantize_rows_kernel) into shared memory, then streams
 // two weight rows per warp as gemv16_kernel<1>.
+//
+// NORM: the row is first formed as x (+ add) and RMS-normalised in every
+// CTA, with the arithmetic of rms_norm_kernel (sum of squares over 4-element
+// chunks lane-striped across one warp, then an xor butterfly; y = (h * r) *
+// norm_w) -- the residual add + RMSNorm before a projection fused into it;
+// CTA 0 stores h when h_out is set.
+constexpr int GEMV_Q1N_MAX_K = 4096;
+
+template <bool NORM>
 __global__ void __launch_bounds__(GEMV_THREADS)
 gemv_q1_kernel(const float *__restrict__ x, int K, int te, const int8_t *__restrict__ B,
-               const float *__restrict__ w_scale, int N, float *__restrict__ y) {
+               const float *__restrict__ w_scale, int N, float *__restrict__ y,
+               const float *__restrict__ add = nullptr, const float *__restrict__ norm_w = nullptr,
+               float eps = 0.0f, float *__restrict__ h_out = nullptr) {
     __shared__ int4 sA[GEMV_Q1_MAX_K / 16];
     __shared__ float red[GEMV_THREADS / 32];
     __shared__ float s_sc, s_inv;
+    __shared__ __align__(16) float sx[NORM ? GEMV_Q1N_MAX_K : 4];
+    __shared__ float s_r;
     const int lane = threadIdx.x & 31;
     // Launched as a programmatic dependent: the weights do not depend on
     // the preceding kernel, so this warp's first two rows are requested
@@ -119,6 +132,47 @@ gemv_q1_kernel(const float *__restrict__ x, int K, int te, const int8_t *__restr
     }
     pdl_wait();
     const float4 *x4 = reinterpret_cast<const float4 *>(x);
+    if (NORM) {
+        float4 *s4 = reinterpret_cast<float4 *>(sx);
+        const float4 *a4 = reinterpret_cast<const float4 *>(add);
+        for (int i = threadIdx.x; i < K / 4; i += blockDim.x) {
+            float4 v = x4[i];
+            if (add) {
+                const float4 b = a4[i];
+                v = make_float4(__fadd_rn(v.x, b.x), __fadd_rn(v.y, b.y), __fadd_rn(v.z, b.z),
+                                __fadd_rn(v.w, b.w));
+                if (h_out && blockIdx.x == 0) reinterpret_cast<float4 *>(h_out)[i] = v;
+            }
+            s4[i] = v;
+        }
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            float s = 0.0f;
+            for (int c = lane; c < K / 4; c += 32) {
+                const float4 v = s4[c];
+                s = __fadd_rn(s, __fmul_rn(v.x, v.x));
+                s = __fadd_rn(s, __fmul_rn(v.y, v.y));
+                s = __fadd_rn(s, __fmul_rn(v.z, v.z));
+                s = __fadd_rn(s, __fmul_rn(v.w, v.w));
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+            if (lane == 0) {
+                const float ms = __fdiv_rn(s, (float)K);
+                s_r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+            }
+        }
+        __syncthreads();
+        const float r = s_r;
+        const float4 *w4 = reinterpret_cast<const float4 *>(norm_w);
+        for (int i = threadIdx.x; i < K / 4; i += blockDim.x) {
+            const float4 v = s4[i], ww = w4[i];
+            s4[i] = make_float4(__fmul_rn(__fmul_rn(v.x, r), ww.x), __fmul_rn(__fmul_rn(v.y, r), ww.y),
+                                __fmul_rn(__fmul_rn(v.z, r), ww.z), __fmul_rn(__fmul_rn(v.w, r), ww.w));
+        }
+        __syncthreads();
+        x4 = s4;
+    }
     float m = 0.0f;
     for (int i = threadIdx.x; i < K / 4; i += blockDim.x) {
         const float4 v = x4[i];
@@ -293,8 +347,23 @@ int launch_gemv_q1(const float *x, size_t K, bool te, const int8_t *B, const flo
     if (K == 0 || K % 16 || K > (size_t)GEMV_Q1_MAX_K || ((uintptr_t)x % 16) ||
         ((uintptr_t)B % 16) || N > (size_t)INT32_MAX)
         return FOCR_E_UNSUPPORTED;
-    FOCR_CUDA_TRY(launch_pdl(gemv_q1_kernel, dim3(gemv_grid(N, (GEMV_THREADS / 32) * 2)),
-                             dim3(GEMV_THREADS), 0, st, x, (int)K, te ? 1 : 0, B, w_scale, (int)N, y));
+    FOCR_CUDA_TRY(launch_pdl(gemv_q1_kernel<false>, dim3(gemv_grid(N, (GEMV_THREADS / 32) * 2)),
+                             dim3(GEMV_THREADS), 0, st, x, (int)K, te ? 1 : 0, B, w_scale, (int)N, y,
+                             (const float *)nullptr, (const float *)nullptr, 0.0f, (float *)nullptr));
+    return FOCR_OK;
+}
+
+int launch_gemv_q1_norm(const float *a, const float *b, size_t K, const float *norm_w, float eps,
+                        float *h, const int8_t *B, const float *w_scale, size_t N, float *y,
+                        cudaStream_t st) {
+    if (N == 0) return FOCR_OK;
+    if (K == 0 || K % 16 || K > GEMV_Q1N_MAX_K || !norm_w ||
+        (((uintptr_t)a | (uintptr_t)b | (uintptr_t)h | (uintptr_t)norm_w | (uintptr_t)B) % 16) ||
+        N > (size_t)INT32_MAX)
+        return FOCR_E_UNSUPPORTED;
+    FOCR_CUDA_TRY(launch_pdl(gemv_q1_kernel<true>, dim3(gemv_grid(N, (GEMV_THREADS / 32) * 2)),
+                             dim3(GEMV_THREADS), 0, st, a, (int)K, 0, B, w_scale, (int)N, y, b,
+                             norm_w, eps, h));
     return FOCR_OK;
 }
 

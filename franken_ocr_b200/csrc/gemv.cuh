@@ -237,6 +237,15 @@ __device__ __forceinline__ void block_best(int &bi, float &bv) {
 int launch_gemv_s4_q1(const float *x, size_t K, bool te, const uint8_t *Bp, const float *scales,
                       size_t group, size_t N, float *y, cudaStream_t st, float *part_v = nullptr,
                       int *part_i = nullptr, int *parts = nullptr);
+// Residual add + RMSNorm + single-row GEMV in one launch: h = a (+ b),
+// y[n] = ((f32)(Q(rms_norm(h) * norm_w) . B[n]) * a_scale) * w_scale[n],
+// half-away quantisation; bit-identical to focr_add_rms_norm (or
+// focr_rms_norm when b is null) followed by launch_gemv_q1.  h (may be
+// null) receives a + b.  K % 16 == 0, K <= 4096, 16-byte aligned pointers;
+// FOCR_E_UNSUPPORTED otherwise.
+int launch_gemv_q1_norm(const float *a, const float *b, size_t K, const float *norm_w, float eps,
+                        float *h, const int8_t *B, const float *w_scale, size_t N, float *y,
+                        cudaStream_t st);
 // tcgen05 path of the packed int4 GEMM (tc_s4.cu): M >= 64 (32 for groups of
 // 16), N >= 128, K % 128 == 0, 16-byte aligned operands.
 bool tc_s4_eligible(const int8_t *A, const uint8_t *Bp, const float *scales, size_t group,

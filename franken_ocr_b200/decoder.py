@@ -308,11 +308,17 @@ class DecoderI8:
         x = self._x
         mlp = None
         for d in self.layers:
+            # residual add + input RMSNorm + q|k|v projection, one launch
+            qkv = self._empty(1, 3 * D)
             if mlp is None:
-                normed = self._norm(x, d["input_ln"])
+                check(lib.focr_rms_norm_linear_i8(_p(x), None, self.hidden, _p(d["input_ln"]),
+                                                  RMS_NORM_EPS, None, _p(d["qkv_w"]),
+                                                  _p(d["qkv_s"]), 3 * D, _p(qkv), st))
             else:
-                x, normed = self._add_norm(h, mlp, d["input_ln"])
-            qkv = self._linear(normed, d["qkv_w"], d["qkv_s"], False)
+                x = self._empty(1, self.hidden)
+                check(lib.focr_rms_norm_linear_i8(_p(h), _p(mlp), self.hidden, _p(d["input_ln"]),
+                                                  RMS_NORM_EPS, _p(x), _p(d["qkv_w"]),
+                                                  _p(d["qkv_s"]), 3 * D, _p(qkv), st))
             check(lib.focr_rope_apply_at(_p(qkv), 2 * D, HEAD_DIM, _p(self._cos), _p(self._sin),
                                          _p(self._state), st))
             k = qkv[0, D:2 * D]

@@ -397,6 +397,17 @@ int focr_decode_prologue(int32_t *state, const int32_t *token, const float *embe
 int focr_rope_apply_at(float *x, size_t cols, size_t head_dim, const float *cos_table,
                        const float *sin_table, const int32_t *state, void *stream);
 
+/* One decode row: h = a + b (b may be NULL: h = a), y = the half-away int8
+ * projection (gemv_i8, decoder.rs:1607) of rms_norm(h) * norm_w -- the
+ * residual add, the layer's input RMSNorm (nn.rs:240-252, the order
+ * focr_rms_norm uses) and the q|k|v projection of decode_step_with_cache_i8
+ * (decoder.rs:2560-2590) in one launch, bit-identical to focr_add_rms_norm +
+ * focr_linear_i8.  h (may be NULL) receives a + b.  Device pointers, k % 16
+ * == 0, k <= 4096, 16-byte aligned. */
+int focr_rms_norm_linear_i8(const float *a, const float *b, size_t k, const float *norm_w,
+                            float eps, float *h, const int8_t *w, const float *w_scale, size_t n,
+                            float *y, void *stream);
+
 /* RingCache::write_decode_step's copy: k, v [heads][head_dim] into ring
  * slot state[FOCR_STATE_SLOT] of ring_k/ring_v [heads][ring_stride][head_dim]. */
 int focr_ring_write(const float *k, const float *v, size_t heads, size_t head_dim, float *ring_k,
