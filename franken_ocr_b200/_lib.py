@@ -39,7 +39,7 @@ EXPORTS = [
     "focr_ep_connect_comm", "focr_ep_connect_local", "focr_ep_forward", "focr_ep_dispatch",
     "focr_ep_experts", "focr_ep_combine", "focr_ep_decode", "focr_ep_status",
     "focr_decoder_create", "focr_decoder_destroy", "focr_decoder_prefill", "focr_decoder_generate",
-    "focr_rms_norm_linear_i8",
+    "focr_rms_norm_linear_i8", "focr_rope_ring_at",
 ]
 
 
@@ -152,6 +152,7 @@ lib.focr_add.argtypes = [vp, vp, sz, vp, i32, vp]
 lib.focr_attention_prefill.argtypes = [vp, vp, vp, sz, sz, sz, vp, i32, vp]
 lib.focr_rope_table.argtypes = [vp, sz, sz, C.c_float, vp, vp]
 lib.focr_decode_prologue.argtypes = [vp, vp, vp, sz, sz, sz, vp, sz, vp, vp]
+lib.focr_rope_ring_at.argtypes = [vp, sz, sz, vp, vp, vp, vp, sz, vp, vp]
 lib.focr_rms_norm_linear_i8.argtypes = [vp, vp, sz, vp, C.c_float, vp, vp, vp, sz, vp, vp]
 lib.focr_decoder_create.argtypes = [C.POINTER(DecoderConfig), C.POINTER(DecoderWeights),
                                     C.POINTER(vp)]

@@ -178,6 +178,44 @@ __global__ void ring_write_kernel(const float *__restrict__ k, const float *__re
     }
 }
 
+// RoPE of one decode row's q and k at the position state[FOCR_STATE_POS]
+// (rope_kernel's arithmetic) and the ring write of the rotated k and of v
+// into slot state[FOCR_STATE_SLOT], in one launch.  qkv = [q | k | v], each
+// heads * head_dim wide.
+__global__ void rope_ring_kernel(float *__restrict__ qkv, int heads, int head_dim,
+                                 const float *__restrict__ cos_t, const float *__restrict__ sin_t,
+                                 float *__restrict__ ring_k, float *__restrict__ ring_v,
+                                 int ring_stride, const int *__restrict__ st) {
+    pdl_wait();
+    pdl_trigger();
+    const int pos = st[FOCR_STATE_POS], slot = st[FOCR_STATE_SLOT];
+    const int half = head_dim / 2, D = heads * head_dim;
+    const float *ct = cos_t + (size_t)pos * head_dim, *stb = sin_t + (size_t)pos * head_dim;
+    const int n = 2 * heads * half;   // rotation pairs of q and k
+    for (int g = blockIdx.x * blockDim.x + threadIdx.x; g < n + heads * head_dim;
+         g += gridDim.x * blockDim.x) {
+        if (g < n) {
+            const int i = g % half, hh = g / half;   // hh < heads: q head, else k head
+            float *row = qkv + (size_t)hh * head_dim;
+            const float a = row[i], b = row[half + i];
+            const float c = ct[i], s = stb[i];
+            const float x0 = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+            const float x1 = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
+            row[i] = x0;
+            row[half + i] = x1;
+            if (hh >= heads) {
+                const int h = hh - heads;
+                float *dst = ring_k + ((size_t)h * ring_stride + slot) * head_dim;
+                dst[i] = x0;
+                dst[half + i] = x1;
+            }
+        } else {
+            const int j = g - n, h = j / head_dim, d = j % head_dim;
+            ring_v[((size_t)h * ring_stride + slot) * head_dim + d] = qkv[2 * D + j];
+        }
+    }
+}
+
 static unsigned grid_for(long n) {
     const long b = (n + 255) / 256;
     return (unsigned)(b < 148 * 16 ? (b > 0 ? b : 1) : 148 * 16);
@@ -400,6 +438,20 @@ int focr_rms_norm_linear_i8(const float *a, const float *b, size_t k, const floa
     if (rc == FOCR_E_UNSUPPORTED)
         return fail(rc, "rms_norm_linear_i8: k % 16 == 0, k <= 4096 and 16-byte aligned pointers required");
     return rc;
+}
+
+int focr_rope_ring_at(float *qkv, size_t heads, size_t head_dim, const float *cos_table,
+                      const float *sin_table, float *ring_k, float *ring_v, size_t ring_stride,
+                      const int32_t *state, void *stream) {
+    if (!qkv || !cos_table || !sin_table || !ring_k || !ring_v || !state)
+        return fail(FOCR_E_ARG, "rope_ring_at: null pointer");
+    if (head_dim == 0 || head_dim % 2 || heads * head_dim > (size_t)INT32_MAX / 4)
+        return fail(FOCR_E_SHAPE, "rope_ring_at: bad head shape");
+    const long n = (long)(heads * head_dim * 2);   // q/k pairs + v values
+    FOCR_CUDA_TRY(launch_pdl(rope_ring_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0,
+                             (cudaStream_t)stream, qkv, (int)heads, (int)head_dim, cos_table,
+                             sin_table, ring_k, ring_v, (int)ring_stride, state));
+    return FOCR_OK;
 }
 
 int focr_ring_write(const float *k, const float *v, size_t heads, size_t head_dim, float *ring_k,

@@ -186,10 +186,9 @@ static int decoder_step(focr_decoder *d, size_t n_tokens, cudaStream_t st) {
         else
             TRY(focr_rms_norm_linear_i8(d->hh, d->mlp, H, L.input_ln, eps, d->x, L.qkv_w,
                                         L.qkv_s, 3 * D, d->qkv, st));
-        // q and k: one row of 2 * heads heads
-        TRY(focr_rope_apply_at(d->qkv, 2 * D, hd, d->rope_cos, d->rope_sin, d->state, st));
-        TRY(focr_ring_write(d->qkv + D, d->qkv + 2 * D, c.heads, hd, L.ring_k, L.ring_v,
-                            c.ring_window, d->state, st));
+        // RoPE of q and k, then k and v into the ring slot: one launch
+        TRY(focr_rope_ring_at(d->qkv, c.heads, hd, d->rope_cos, d->rope_sin, L.ring_k, L.ring_v,
+                              c.ring_window, d->state, st));
         TRY(focr_attention_decode_at(d->qkv, L.ref_k, L.ref_v, d->prefill_len, c.max_prefill,
                                      L.ring_k, L.ring_v, c.ring_window, c.heads, hd, d->state,
                                      d->ctx, st));

@@ -319,12 +319,10 @@ class DecoderI8:
                 check(lib.focr_rms_norm_linear_i8(_p(h), _p(mlp), self.hidden, _p(d["input_ln"]),
                                                   RMS_NORM_EPS, _p(x), _p(d["qkv_w"]),
                                                   _p(d["qkv_s"]), 3 * D, _p(qkv), st))
-            check(lib.focr_rope_apply_at(_p(qkv), 2 * D, HEAD_DIM, _p(self._cos), _p(self._sin),
-                                         _p(self._state), st))
-            k = qkv[0, D:2 * D]
-            v = qkv[0, 2 * D:]
-            check(lib.focr_ring_write(_p(k), _p(v), self.heads, HEAD_DIM, _p(d["ring_k"]),
-                                      _p(d["ring_v"]), RING_WINDOW, _p(self._state), st))
+            # RoPE of q and k, then k and v into the ring slot: one launch
+            check(lib.focr_rope_ring_at(_p(qkv), self.heads, HEAD_DIM, _p(self._cos),
+                                        _p(self._sin), _p(d["ring_k"]), _p(d["ring_v"]),
+                                        RING_WINDOW, _p(self._state), st))
             ctx = self._empty(1, D)
             check(lib.focr_attention_decode_at(
                 _p(qkv), _p(d["ref_k"]), _p(d["ref_v"]), self.prefill_len, self.max_prefill,
@@ -345,10 +343,13 @@ class DecoderI8:
         check(lib.focr_lmhead_top1(self.head._h, _p(normed), 1, _p(self._bv), _p(self._tok), None,
                                    MEM_DEVICE, self._stream()))
 
-    def generate_graph(self, embeds, n_tokens: int, use_graph: bool = True) -> np.ndarray:
+    def generate_graph(self, embeds, n_tokens: int, use_graph: bool = True,
+                       timer: list | None = None) -> np.ndarray:
         """:meth:`generate` with the decode loop on the device: the step is
         captured once in a CUDA graph and replayed per token; tokens are
-        recorded on the device and read back once at the end."""
+        recorded on the device and read back once at the end.  With `timer`
+        (a list) the call appends (start event, end event, replayed steps)
+        bracketing the graph replays on the current stream."""
         torch = self._torch
         from ._lib import STATE_NEXT_POS, STATE_WORDS
 
@@ -380,8 +381,15 @@ class DecoderI8:
                     with torch.cuda.graph(g):
                         self._step_dev()
                     self._graph = g
+                if timer is not None:
+                    t0 = torch.cuda.Event(enable_timing=True)
+                    t1 = torch.cuda.Event(enable_timing=True)
+                    t0.record()
                 for _ in range(steps - 1):
                     g.replay()
+                if timer is not None:
+                    t1.record()
+                    timer.append((t0, t1, steps - 1))
             else:
                 for _ in range(steps - 1):
                     self._step_dev()

@@ -408,6 +408,13 @@ int focr_rms_norm_linear_i8(const float *a, const float *b, size_t k, const floa
                             float eps, float *h, const int8_t *w, const float *w_scale, size_t n,
                             float *y, void *stream);
 
+/* focr_rope_apply_at on the q and k parts of qkv [3][heads * head_dim]
+ * followed by focr_ring_write of the rotated k and of v, in one launch
+ * (bit-identical to the two calls). */
+int focr_rope_ring_at(float *qkv, size_t heads, size_t head_dim, const float *cos_table,
+                      const float *sin_table, float *ring_k, float *ring_v, size_t ring_stride,
+                      const int32_t *state, void *stream);
+
 /* RingCache::write_decode_step's copy: k, v [heads][head_dim] into ring
  * slot state[FOCR_STATE_SLOT] of ring_k/ring_v [heads][ring_stride][head_dim]. */
 int focr_ring_write(const float *k, const float *v, size_t heads, size_t head_dim, float *ring_k,
