@@ -302,14 +302,14 @@ int launch_igemm(const void *A, bool au8, const int8_t *B, size_t M, size_t K, s
                  int32_t *out, cudaStream_t st) {
     if (M == 0 || N == 0) return FOCR_OK;
     if (K == 0) return FOCR_OK;  // every dot is empty: out += 0
-    if (!au8 && tc_igemm_eligible(A, B, M, K, N, out))
+    if (tc_igemm_eligible(A, B, M, K, N, out))
         return launch_tc_igemm(A, M, au8, B, M, K, N, out, st);
     // 4 < M < 128 with more than 16 rows or a large weight matrix (>= 32 MB,
     // beyond one L2-resident pass per 8-row chunk): stage A in a zero-padded
     // 128-row scratch and run the tensor-core path (the output rows past M
     // are never written).  Otherwise the GEMV tier streams the weights, in
     // 8-row chunks of one launch.
-    if (!au8 && M > 4 && M < 128 && (M > 16 || N * K >= ((size_t)32 << 20)) &&
+    if (M > 4 && M < 128 && (M > 16 || N * K >= ((size_t)32 << 20)) &&
         tc_igemm_eligible(A, B, 128, K, N, out)) {
         DevBuf pad;
         FOCR_CUDA_TRY(pad.alloc(128 * K, st));

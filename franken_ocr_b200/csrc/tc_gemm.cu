@@ -71,8 +71,9 @@ static int make_tmap_out_s32(CUtensorMap *map, int32_t *base, uint64_t rows, uin
 // swizzled shared-memory box (two per warp, alternating) and adds it onto
 // `out` with one TMA reduce-add (out must be 16-byte aligned, N % 4 == 0);
 // otherwise each lane adds its row in place.
-template <int BN_, int STAGES_, bool TMA_EPI = false>
+template <int BN_, int STAGES_, bool TMA_EPI = false, bool AU8_ = false>
 struct RawIgemm {
+    static constexpr bool A_U8 = AU8_;   // u8 activations (igemm_u8s8)
     static constexpr int NA = 1, BN = BN_, STAGES = STAGES_, JOB_SMEM = 0;
     static constexpr int EPI_SMEM = TMA_EPI ? 4 * 2 * 4096 + 1024 : 0;
     static constexpr uint32_t KERNEL_ID = 1;
@@ -178,10 +179,10 @@ bool tc_igemm_eligible(const void *A, const int8_t *B, size_t M, size_t K, size_
            K <= (size_t)INT32_MAX / 2;
 }
 
-template <int BN, int S, bool TMA_EPI>
+template <int BN, int S, bool TMA_EPI, bool AU8>
 static int run_raw(const void *A, size_t a_rows, const int8_t *B, size_t M, size_t K, size_t N,
                    int32_t *out, int *err, cudaStream_t st) {
-    RawIgemm<BN, S, TMA_EPI> p;
+    RawIgemm<BN, S, TMA_EPI, AU8> p;
     int rc = make_tmap_i8(&p.ta, A, a_rows, K, 128);
     if (!rc) rc = make_tmap_i8(&p.tb, B, N, K, BN);
     if (!rc && TMA_EPI) rc = make_tmap_out_s32(&p.to, out, M, N);
@@ -241,11 +242,9 @@ int tc_status_read(int *word, bool clear) {
     return FOCR_OK;
 }
 
-// A has a_rows >= M rows (rows past M, if any, are padding; at least 128
-// when M < 128 so every A box lies inside its tensor).
-int launch_tc_igemm(const void *A, size_t a_rows, bool au8, const int8_t *B, size_t M, size_t K,
-                    size_t N, int32_t *out, cudaStream_t st) {
-    if (au8) return fail(FOCR_E_UNSUPPORTED, "tc igemm: u8 activations use the GEMV tier");
+template <bool AU8>
+static int launch_tc_igemm_t(const void *A, size_t a_rows, const int8_t *B, size_t M, size_t K,
+                             size_t N, int32_t *out, cudaStream_t st) {
     int *err = nullptr;
     if (int rc = tc_status_word(&err)) return rc;
     const size_t mt = (M + 127) / 128;
@@ -254,13 +253,22 @@ int launch_tc_igemm(const void *A, size_t a_rows, bool au8, const int8_t *B, siz
     // epilogue when the output rows are 16-byte aligned
     const bool tma_epi = N % 4 == 0 && (uintptr_t)out % 16 == 0 && !getenv("FOCR_SCALAR_EPILOGUE");
     if (N >= 256 && mt * ((N + 255) / 256) >= (size_t)sms)
-        return tma_epi ? run_raw<256, 4, true>(A, a_rows, B, M, K, N, out, err, st)
-                       : run_raw<256, 4, false>(A, a_rows, B, M, K, N, out, err, st);
+        return tma_epi ? run_raw<256, 4, true, AU8>(A, a_rows, B, M, K, N, out, err, st)
+                       : run_raw<256, 4, false, AU8>(A, a_rows, B, M, K, N, out, err, st);
     if (N >= 128 && mt * ((N + 127) / 128) >= (size_t)sms)
-        return tma_epi ? run_raw<128, 6, true>(A, a_rows, B, M, K, N, out, err, st)
-                       : run_raw<128, 6, false>(A, a_rows, B, M, K, N, out, err, st);
-    return tma_epi ? run_raw<64, 8, true>(A, a_rows, B, M, K, N, out, err, st)
-                   : run_raw<64, 8, false>(A, a_rows, B, M, K, N, out, err, st);
+        return tma_epi ? run_raw<128, 6, true, AU8>(A, a_rows, B, M, K, N, out, err, st)
+                       : run_raw<128, 6, false, AU8>(A, a_rows, B, M, K, N, out, err, st);
+    return tma_epi ? run_raw<64, 8, true, AU8>(A, a_rows, B, M, K, N, out, err, st)
+                   : run_raw<64, 8, false, AU8>(A, a_rows, B, M, K, N, out, err, st);
+}
+
+// A has a_rows >= M rows (rows past M, if any, are padding; at least 128
+// when M < 128 so every A box lies inside its tensor).  au8: A holds unsigned
+// bytes (the MMA's A-signedness bit is cleared; B stays signed).
+int launch_tc_igemm(const void *A, size_t a_rows, bool au8, const int8_t *B, size_t M, size_t K,
+                    size_t N, int32_t *out, cudaStream_t st) {
+    return au8 ? launch_tc_igemm_t<true>(A, a_rows, B, M, K, N, out, st)
+               : launch_tc_igemm_t<false>(A, a_rows, B, M, K, N, out, st);
 }
 
 }  // namespace focr

@@ -113,6 +113,15 @@ constexpr size_t tc_smem_bytes() {
            P::JOB_SMEM;
 }
 
+// A operand type of a job set: unsigned bytes when the parameter struct
+// declares `static constexpr bool A_U8 = true`, signed bytes otherwise.
+template <class P, class = void>
+struct a_u8_trait { static constexpr bool value = false; };
+template <class P>
+struct a_u8_trait<P, decltype(void(P::A_U8))> { static constexpr bool value = P::A_U8; };
+template <class P>
+__host__ __device__ constexpr bool a_is_u8() { return a_u8_trait<P>::value; }
+
 template <class P>
 __global__ void __launch_bounds__(tc_threads<P>(), 1) tc_gemm_kernel(const __grid_constant__ P p) {
     constexpr int NA = P::NA, BN = P::BN, S = P::STAGES, XW = TcXw<P>::value, EW = TcEw<P>::value;
@@ -244,7 +253,7 @@ __global__ void __launch_bounds__(tc_threads<P>(), 1) tc_gemm_kernel(const __gri
                     break;
                 tc::fence_after();
                 const uint32_t acc = tmem + (uint32_t)(buf * NA * BN);
-                const uint32_t idesc = tc::idesc_i8(128, jb.n_mma);
+                const uint32_t idesc = tc::idesc_i8(128, jb.n_mma, !a_is_u8<P>());
                 for (int kb = 0; kb < jb.kblocks; kb++, it++) {
                     const uint32_t s = it % S;
                     if (!(ok = tc::mbar_wait(&full[s], (it / S) & 1, err))) break;

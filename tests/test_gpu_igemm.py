@@ -100,6 +100,26 @@ def test_config1_sweep_device(cuda, m, n, k):
     assert torch.equal(out[rows][:, cols].cpu().to(torch.int64), ref)
 
 
+@pytest.mark.parametrize("m,n,k", [(512, 1280, 896), (4096, 1792, 1280), (48, 1792, 1280)])
+def test_u8s8_tensor_cores(cuda, m, n, k):
+    """igemm_u8s8 (dispatch.rs:276) at tensor-core shapes: unsigned activations
+    in [0, 255] (the MMA's A operand unsigned, B signed), += onto a seeded out,
+    every element exact against an int64 product."""
+    import torch
+
+    from franken_ocr_b200 import simd
+
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    a = torch.randint(0, 256, (m, k), dtype=torch.uint8, device="cuda", generator=g)
+    b = torch.randint(-128, 128, (n, k), dtype=torch.int8, device="cuda", generator=g)
+    seed = torch.arange(m * n, dtype=torch.int32, device="cuda").reshape(m, n) - 1000
+    out = seed.clone()
+    simd.igemm_u8s8(a, b, m, k, n, out)
+    torch.cuda.synchronize()
+    ref = a.cpu().to(torch.int64) @ b.cpu().to(torch.int64).T + seed.cpu().to(torch.int64)
+    assert torch.equal(out.cpu().to(torch.int64), ref)
+
+
 def test_int4_cases(cuda, oracle):
     """tests/int4_packed_parity.rs cases, K=6848 worst case and the config-4
     shapes: bit-identical f32 to the oracle; out is overwritten."""
