@@ -305,18 +305,14 @@ int launch_igemm(const void *A, bool au8, const int8_t *B, size_t M, size_t K, s
     if (tc_igemm_eligible(A, B, M, K, N, out))
         return launch_tc_igemm(A, M, au8, B, M, K, N, out, st);
     // 4 < M < 128 with more than 16 rows or a large weight matrix (>= 32 MB,
-    // beyond one L2-resident pass per 8-row chunk): stage A in a zero-padded
-    // 128-row scratch and run the tensor-core path (the output rows past M
-    // are never written).  Otherwise the GEMV tier streams the weights, in
-    // 8-row chunks of one launch.
+    // beyond one L2-resident pass per 8-row chunk): the tensor-core path reads
+    // A in place; its 128-row TMA boxes run past row M and the copy engine
+    // fills those rows with zeros (the output rows past M are never written).
+    // Otherwise the GEMV tier streams the weights, in 8-row chunks of one
+    // launch.
     if (M > 4 && M < 128 && (M > 16 || N * K >= ((size_t)32 << 20)) &&
-        tc_igemm_eligible(A, B, 128, K, N, out)) {
-        DevBuf pad;
-        FOCR_CUDA_TRY(pad.alloc(128 * K, st));
-        FOCR_CUDA_TRY(cudaMemsetAsync((uint8_t *)pad.p + M * K, 0, (128 - M) * K, st));
-        FOCR_CUDA_TRY(cudaMemcpyAsync(pad.p, A, M * K, cudaMemcpyDeviceToDevice, st));
-        return launch_tc_igemm(pad.p, 128, au8, B, M, K, N, out, st);
-    }
+        tc_igemm_eligible(A, B, 128, K, N, out))
+        return launch_tc_igemm(A, M, au8, B, M, K, N, out, st);
     if (K > (size_t)INT32_MAX || N > (size_t)INT32_MAX)
         return fail(FOCR_E_UNSUPPORTED, "igemm: dimension exceeds int32 range");
     return au8 ? launch_chunk<true, EPI_ADD_I32>(reinterpret_cast<const int8_t *>(A), B, (int)M,

@@ -262,8 +262,9 @@ static int launch_tc_igemm_t(const void *A, size_t a_rows, const int8_t *B, size
                    : run_raw<64, 8, false, AU8>(A, a_rows, B, M, K, N, out, err, st);
 }
 
-// A has a_rows >= M rows (rows past M, if any, are padding; at least 128
-// when M < 128 so every A box lies inside its tensor).  au8: A holds unsigned
+// A has a_rows >= M rows (rows past M, if any, are padding; with fewer
+// than 128 the A box runs past the tensor and TMA fills those rows with
+// zeros, as it does for a partial last K block).  au8: A holds unsigned
 // bytes (the MMA's A-signedness bit is cleared; B stays signed).
 int launch_tc_igemm(const void *A, size_t a_rows, bool au8, const int8_t *B, size_t M, size_t K,
                     size_t N, int32_t *out, cudaStream_t st) {

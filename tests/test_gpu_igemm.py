@@ -171,8 +171,9 @@ def test_tc_accumulate_ragged(cuda, m, n, k):
     """+= onto a seeded int32 out with ragged edges on every multi-row route:
     the tensor-core path with the TMA reduce-add epilogue (N % 4 == 0) and
     the per-row one (N % 4 != 0); 8 < M < 128 through the chunked GEMV grid
-    (small weights) and through the zero-padded tensor-core path (weights of
-    32 MB and more)."""
+    (small weights) and through the tensor-core path, whose 128-row A boxes
+    run past row M and read zeros there (weights of 32 MB and more, and any
+    M > 16)."""
     import torch
 
     from franken_ocr_b200 import simd
